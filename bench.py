@@ -1,0 +1,329 @@
+"""Benchmark of the fused RMSNorm -> int4 decode GEMV on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (config 1): out = rmsnorm(x) @ W^T with M=1, K=2048, N=6144 (fused
+QKV), W int4 group-128 in the fused path's plain layout (FusedWeight bits=4),
+x = residual bf16 N(0,1), gamma = bf16(1 + N(0, 0.1)), eps 1e-6. Synthetic
+seeded inputs with BASELINE.json's distributions (no dataset exists for this).
+
+One step = one CUDA-graph replay of R back-to-back rms_gemv calls, each on a
+different copy of the weights; the R copies total >= 4x the L2 size, so
+every call streams its weights from HBM (inputs larger than L2, no flush
+needed). value = algorithmic bytes moved per second (GB/s), summed over
+GPUs; per GPU the replicas are independent (weak scaling, no collectives).
+
+--impl reference times the reference's own CPU path (torch dequant +
+F.linear on the host cores, all threads) on the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (str(ROOT), str(ROOT / "breeze-tts-2_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+M, K, N = 1, 2048, 6144
+GROUP = 128
+EPS = 1e-6
+# codes + scale + min + x + gamma + out
+ALGO_BYTES = N * K // 2 + 2 * (N * K // GROUP) * 2 + M * K * 2 + K * 2 + M * N * 2
+METRIC = "fused quant GEMV HBM GB/s (% of 8 TB/s) at M=1; decode-step µs/token"
+CONFIG = {"workload": "config1: fused RMSNorm -> int4 g128 GEMV, M=1, K=2048, N=6144 (plain int4 layout)",
+          "global_batch": M, "seq_len": 1, "parallelism": "replicas"}
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+def measured_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def known_traffic():
+    p = ROOT / "profiles" / "roofline_traffic.json"
+    if p.exists():
+        return json.loads(p.read_text()).get("config1")
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu, self.proc, self.t0 = gpu, None, 0.0
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [c.strip() for c in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_inputs(device, seed: int):
+    """Config-1 tensors on the device (seeded; plain int4 layout)."""
+    from breeze_b200.fused.kernels import FusedWeight
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    codes = torch.randint(0, 16, (N, K), generator=g, device=device, dtype=torch.int32).to(torch.uint8)
+    scale = ((torch.randn(N, K // GROUP, generator=g, device=device) * 0.02).abs() / 7).to(torch.bfloat16)
+    x = torch.randn(M, K, generator=g, device=device).to(torch.bfloat16)
+    gamma = (1 + 0.1 * torch.randn(K, generator=g, device=device)).to(torch.bfloat16)
+    packed = (codes[:, 0::2] | (codes[:, 1::2] << 4)).contiguous()
+    mn = (-8.0 * scale.float()).to(torch.bfloat16)
+    fw = FusedWeight.from_parts(4, packed, scale, mn)
+    return fw, x, gamma
+
+
+def run_ours(args, rank, local_rank, world):
+    from breeze_b200 import _lib
+    from breeze_b200.fused.kernels import rms_gemv
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import torch.distributed as dist
+
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    fw, x, gamma = make_inputs(device, seed=1234 + rank)
+    l2 = torch.cuda.get_device_properties(device).L2_cache_size
+    R = max(8, -(-4 * l2 // fw.w.numel()))  # copies totalling >= 4x L2
+    copies = [fw.clone() for _ in range(R)]
+    out = torch.empty(M, N, device=device, dtype=torch.bfloat16)
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(stream):
+        for c in copies[:2]:
+            rms_gemv(x, c, gamma, EPS, out=out)
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for c in copies:
+                rms_gemv(x, c, gamma, EPS, out=out)
+    torch.cuda.current_stream(device).wait_stream(stream)
+    torch.cuda.synchronize(device)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier(device_ids=[local_rank])
+
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize(device)
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize(device)
+    cur = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(cur)
+    for _ in range(args.steps):
+        graph.replay()
+    e1.record(cur)
+    torch.cuda.synchronize(device)
+    barrier()
+    clock = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], device=device, dtype=torch.float64)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+
+    # ---- end to end through the public API: H2D x, rms_gemv, D2H out per call
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty_like(x)
+    e2e_steps = max(1, min(args.steps, 200))
+
+    def e2e_step():
+        for c in copies:
+            xd.copy_(x_host, non_blocking=True)
+            rms_gemv(xd, c, gamma, EPS, out=out)
+            out_host.copy_(out, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize(device)
+    barrier()
+    h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h0.record(cur)
+    for _ in range(e2e_steps):
+        e2e_step()
+    h1.record(cur)
+    torch.cuda.synchronize(device)
+    e2e_ms = h0.elapsed_time(h1)
+    te = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        dist.barrier(device_ids=[local_rank])
+    e2e_ms = float(te.item())
+    status = _lib.device_status(local_rank)
+
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        per_launch_s = ms_max / 1e3 / (args.steps * R)
+        achieved = ALGO_BYTES / per_launch_s / 1e9
+        value = world * ALGO_BYTES * R * args.steps / (ms_max / 1e3) / 1e9
+        e2e_val = world * ALGO_BYTES * R * e2e_steps / (e2e_ms / 1e3) / 1e9
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int4 weights, bf16 activations, fp32 accumulate",
+            "data": "synthetic (seeded, BASELINE config-1 distributions)",
+            "config": {**CONFIG, "calls_per_step": R, "l2_policy": f"inputs > L2: {R} weight copies = "
+                       f"{R * ALGO_BYTES / 2**20:.0f} MiB rotated per step"},
+            "us_per_call": round(per_launch_s * 1e6, 3),
+            "pct_of_8TBs": round(100 * achieved / 8000, 1),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "traffic": known_traffic(), "algorithmic_bytes_per_launch": ALGO_BYTES},
+            "e2e": {"value": round(e2e_val, 1), "unit": "GB/s", "h2d_bytes_per_step": R * M * K * 2,
+                    "d2h_bytes_per_step": R * M * N * 2, "steps": e2e_steps,
+                    "how": "eager Python rms_gemv calls, pinned H2D of x and D2H of out per call"},
+            "gpu_launches": R * args.steps,
+            "clocks": clock,
+            "device_error_bits": status,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        del graph
+        dist.destroy_process_group()
+
+
+def _cpu_inputs():
+    g = torch.Generator().manual_seed(1234)
+    codes = torch.randint(0, 16, (N, K), generator=g, dtype=torch.int32).to(torch.uint8)
+    scale = ((torch.randn(N, K // GROUP, generator=g) * 0.02).abs() / 7).to(torch.bfloat16)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    gamma = (1 + 0.1 * torch.randn(K, generator=g)).to(torch.bfloat16)
+    packed = (codes[:, 0::2] | (codes[:, 1::2] << 4)).contiguous()
+    mn = (-8.0 * scale.float()).to(torch.bfloat16)
+    return x, packed, scale, mn, gamma
+
+
+def cpu_baseline(seconds: float = 10.0):
+    """The reference's CPU path (torch dequant + F.linear) on a bounded sample."""
+    from oracle import cpu_path
+
+    x, packed, scale, mn, gamma = _cpu_inputs()
+    cpu_path.rms_gemv_int4_plain(x, packed, scale, mn, gamma, EPS)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        cpu_path.rms_gemv_int4_plain(x, packed, scale, mn, gamma, EPS)
+        n += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = (time.perf_counter() - t0) / n
+    return {"value": round(ALGO_BYTES / dt / 1e9, 4), "unit": "GB/s", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"{n} calls of the full config-1 GEMV (M=1, K=2048, N=6144), "
+            f"{dt * 1e3:.1f} ms per call"}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    from oracle import cpu_path
+
+    x, packed, scale, mn, gamma = _cpu_inputs()
+    for _ in range(args.warmup):
+        cpu_path.rms_gemv_int4_plain(x, packed, scale, mn, gamma, EPS)
+    steps = args.steps
+    t0 = time.perf_counter()
+    deadline = t0 + args.cpu_seconds * 6
+    done = 0
+    for _ in range(steps):
+        cpu_path.rms_gemv_int4_plain(x, packed, scale, mn, gamma, EPS)
+        done += 1
+        if time.perf_counter() > deadline:
+            break
+    dt = time.perf_counter() - t0
+    value = ALGO_BYTES * done / dt / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": 0,
+        "steps": done, "warmup": args.warmup, "ms_per_step": round(dt / done * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int4 weights, fp32 dequant + F.linear (CPU)",
+        "data": "synthetic (seeded, BASELINE config-1 distributions)", "config": CONFIG,
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": f"{done} calls of the full config-1 GEMV on the host"},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank, local_rank, world = dist_env()
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    run_ours(args, rank, local_rank, world)
+
+
+if __name__ == "__main__":
+    main()

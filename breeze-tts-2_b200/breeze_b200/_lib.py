@@ -1,0 +1,301 @@
+"""ctypes binding of libbreeze_b200.so (the C ABI in include/breeze_b200.h).
+
+The library is the only compute path: if it is missing, or the tensors are
+not on a CUDA device, calls raise -- there is no CPU or PyTorch fallback.
+Status codes map to the exception types the reference raises for the same
+conditions (ValueError for shape/format problems, RuntimeError otherwise).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "libbreeze_b200.so"
+
+# ---- constants mirrored from include/breeze_b200.h ----------------------
+BQ_OK = 0
+BQ_ERR_INVALID_ARG, BQ_ERR_SHAPE, BQ_ERR_ALIGN, BQ_ERR_FORMAT = -1, -2, -3, -4
+BQ_ERR_WORKSPACE, BQ_ERR_CUDA, BQ_ERR_DEVICE = -5, -6, -7
+BQ_DEVERR_WAIT_TIMEOUT = 1
+
+W_BF16, W_INT4_TINYGEMM, W_INT4_PLAIN, W_FP8_E4M3, W_INT8 = 0, 1, 2, 3, 4
+EPI_NONE, EPI_SILU_MUL, EPI_ADD_RESIDUAL = 0, 1, 2
+DT_BF16, DT_F16, DT_F32 = 0, 1, 2
+FLAG_PDL, FLAG_SCALE_ROUND_BF16 = 1, 2
+
+_DT = {torch.bfloat16: DT_BF16, torch.float16: DT_F16, torch.float32: DT_F32}
+
+
+class GemvDesc(ctypes.Structure):
+    """Mirror of ``bq_gemv_desc``."""
+
+    _fields_ = [
+        ("M", ctypes.c_int32), ("N", ctypes.c_int32), ("K", ctypes.c_int32),
+        ("wfmt", ctypes.c_int32), ("group", ctypes.c_int32), ("epilogue", ctypes.c_int32),
+        ("x_dtype", ctypes.c_int32), ("out_dtype", ctypes.c_int32), ("res_dtype", ctypes.c_int32),
+        ("flags", ctypes.c_uint32), ("eps", ctypes.c_float), ("reserved", ctypes.c_int32),
+        ("x", ctypes.c_void_p), ("ldx", ctypes.c_int64),
+        ("gamma", ctypes.c_void_p), ("w", ctypes.c_void_p), ("scale", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p), ("residual", ctypes.c_void_p), ("ldr", ctypes.c_int64),
+        ("out", ctypes.c_void_p), ("ldo", ctypes.c_int64),
+    ]
+
+
+_lib = None
+_lock = threading.Lock()
+
+_SIGS = {
+    "bq_version": (ctypes.c_int32, []),
+    "bq_last_error_string": (ctypes.c_char_p, []),
+    "bq_device_status": (ctypes.c_int32, [ctypes.c_int32, ctypes.POINTER(ctypes.c_uint32)]),
+    "bq_device_status_clear": (ctypes.c_int32, [ctypes.c_int32]),
+    "bq_gemv_workspace_bytes": (ctypes.c_int32, [ctypes.POINTER(GemvDesc), ctypes.POINTER(ctypes.c_size_t)]),
+    "bq_gemv": (ctypes.c_int32, [ctypes.POINTER(GemvDesc), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "bq_int4_tinygemm_pack": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
+                                               ctypes.c_int32, ctypes.c_void_p]),
+    "bq_int4_tinygemm_unpack": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
+                                                 ctypes.c_int32, ctypes.c_void_p]),
+    "bq_dequant": (ctypes.c_int32, [ctypes.POINTER(GemvDesc), ctypes.c_void_p, ctypes.c_void_p]),
+    "bq_rmsnorm": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
+                                    ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_float,
+                                    ctypes.c_void_p]),
+    "bq_silu_mul": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
+                                     ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                                     ctypes.c_void_p]),
+}
+
+
+def default_flags() -> int:
+    """Programmatic dependent launch is on unless BREEZE_B200_PDL=0: each
+    GEMV starts streaming its (static) weights while the previous kernel in
+    the stream finishes, and waits for it before reading activations."""
+    return 0 if os.environ.get("BREEZE_B200_PDL", "1") == "0" else FLAG_PDL
+
+
+def exported_symbols() -> list[str]:
+    return list(_SIGS)
+
+
+def load() -> ctypes.CDLL:
+    """Load the library once (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            path = os.environ.get("BREEZE_B200_LIB", str(LIB_PATH))
+            if not Path(path).exists():
+                raise RuntimeError(
+                    f"{path} is missing: build it with `python breeze-tts-2_b200/build.py` "
+                    "(breeze_b200 has no fallback path)")
+            lib = ctypes.CDLL(path)
+            for name, (res, args) in _SIGS.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def last_error() -> str:
+    return load().bq_last_error_string().decode()
+
+
+def check(rc: int, what: str) -> None:
+    if rc == BQ_OK:
+        return
+    msg = f"{what}: {last_error()} (status {rc})"
+    if rc in (BQ_ERR_SHAPE, BQ_ERR_FORMAT, BQ_ERR_ALIGN, BQ_ERR_INVALID_ARG, BQ_ERR_WORKSPACE):
+        raise ValueError(msg)
+    raise RuntimeError(msg)
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(*tensors: torch.Tensor | None) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("breeze_b200 kernels need CUDA tensors (there is no CPU path)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"tensors on different devices: {dev} and {t.device}")
+    if dev is None:
+        raise RuntimeError("no tensor given")
+    if dev.index != torch.cuda.current_device():
+        torch.cuda.set_device(dev)
+    return dev
+
+
+# ---- workspace ---------------------------------------------------------------
+class Workspace:
+    """Per-device scratch for split-K partial sums and arrival counters.
+
+    Zero-filled when (re)allocated; the kernels leave the counters at zero
+    after every call, so the buffer is reused as is. It only grows outside
+    stream capture: capture a CUDA graph after one warm-up call per shape,
+    as the reference does before capturing its decode graphs.
+    """
+
+    def __init__(self):
+        self._bufs: dict[int, torch.Tensor] = {}
+
+    def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
+        idx = device.index
+        buf = self._bufs.get(idx)
+        if buf is None or buf.numel() < nbytes:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError(
+                    f"breeze_b200 workspace must grow to {nbytes} bytes during CUDA graph capture; "
+                    "run the shape once before capturing")
+            size = max(nbytes, 1 << 20, 0 if buf is None else 2 * buf.numel())
+            buf = torch.zeros(size, dtype=torch.uint8, device=device)
+            self._bufs[idx] = buf
+        return buf
+
+    def reset(self) -> None:
+        for b in self._bufs.values():
+            b.zero_()
+
+
+WORKSPACE = Workspace()
+
+
+def make_desc(x: torch.Tensor, w: torch.Tensor, wfmt: int, n: int, *, scale=None, group: int = 128, gamma=None,
+              eps: float = 1e-6, epilogue: int = EPI_NONE, residual=None, bias=None, out: torch.Tensor,
+              flags: int = 0) -> GemvDesc:
+    m, k = x.shape
+    d = GemvDesc()
+    d.M, d.N, d.K = m, n, k
+    d.wfmt, d.group, d.epilogue = wfmt, group, epilogue
+    d.x_dtype = _DT[x.dtype]
+    d.out_dtype = _DT[out.dtype]
+    d.res_dtype = _DT[residual.dtype] if residual is not None else DT_BF16
+    d.flags = flags
+    d.eps = eps
+    d.x, d.ldx = x.data_ptr(), x.stride(0)
+    d.gamma = _ptr(gamma)
+    d.w = w.data_ptr()
+    d.scale = _ptr(scale)
+    d.bias = _ptr(bias)
+    d.residual = _ptr(residual)
+    d.ldr = residual.stride(0) if residual is not None else 0
+    d.out, d.ldo = out.data_ptr(), out.stride(0)
+    return d
+
+
+def _rowmajor(t: torch.Tensor, name: str) -> torch.Tensor:
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError(f"{name} must be a 2-D tensor with unit stride in the last dimension")
+    return t
+
+
+def gemv(x: torch.Tensor, w: torch.Tensor, wfmt: int, n: int, *, scale=None, group: int = 128, gamma=None,
+         eps: float = 1e-6, epilogue: int = EPI_NONE, residual=None, bias=None, out: torch.Tensor | None = None,
+         out_dtype: torch.dtype | None = None, flags: int = 0) -> torch.Tensor:
+    """out = epilogue(rmsnorm(x) @ dequant(w)^T) on the current stream."""
+    dev = _require_cuda(x, w, scale, gamma, residual, bias, out)
+    x = _rowmajor(x, "x")
+    if x.dtype not in _DT:
+        raise ValueError(f"unsupported activation dtype {x.dtype}")
+    m = x.shape[0]
+    n_out = n // 2 if epilogue == EPI_SILU_MUL else n
+    if residual is not None:
+        residual = _rowmajor(residual, "residual")
+    if out is None:
+        dt = out_dtype or (residual.dtype if residual is not None else torch.bfloat16)
+        out = torch.empty(m, n_out, device=dev, dtype=dt)
+    else:
+        out = _rowmajor(out, "out")
+    if gamma is not None and gamma.dtype != torch.bfloat16:
+        gamma = gamma.to(torch.bfloat16)
+    if bias is not None and bias.dtype != out.dtype:
+        bias = bias.to(out.dtype)
+    lib = load()
+    d = make_desc(x, w, wfmt, n, scale=scale, group=group, gamma=gamma, eps=eps, epilogue=epilogue,
+                  residual=residual, bias=bias, out=out, flags=flags)
+    need = ctypes.c_size_t(0)
+    check(lib.bq_gemv_workspace_bytes(ctypes.byref(d), ctypes.byref(need)), "bq_gemv_workspace_bytes")
+    ws = WORKSPACE.get(dev, need.value)
+    check(lib.bq_gemv(ctypes.byref(d), ws.data_ptr(), ws.numel(), _stream(dev)), "bq_gemv")
+    return out
+
+
+def dequant(w: torch.Tensor, wfmt: int, n: int, k: int, *, scale=None, group: int = 128) -> torch.Tensor:
+    """fp32 [N, K] dequantized weights, bit-exact with the reference."""
+    dev = _require_cuda(w, scale)
+    d = GemvDesc()
+    d.N, d.K, d.wfmt, d.group = n, k, wfmt, group
+    d.w, d.scale = w.data_ptr(), _ptr(scale)
+    out = torch.empty(n, k, device=dev, dtype=torch.float32)
+    check(load().bq_dequant(ctypes.byref(d), out.data_ptr(), _stream(dev)), "bq_dequant")
+    return out
+
+
+def tinygemm_pack(packed_u8: torch.Tensor, inner_k_tiles: int = 8) -> torch.Tensor:
+    """(N, K/2) uint8 (odd k low) -> tinygemm int32 tiles, on the GPU."""
+    dev = _require_cuda(packed_u8)
+    packed_u8 = packed_u8.contiguous()
+    n, kh = packed_u8.shape
+    k = 2 * kh
+    out = torch.empty(n // 8, k // (16 * inner_k_tiles), 32, inner_k_tiles // 2, device=dev, dtype=torch.int32)
+    check(load().bq_int4_tinygemm_pack(packed_u8.data_ptr(), out.data_ptr(), n, k, inner_k_tiles, _stream(dev)),
+          "bq_int4_tinygemm_pack")
+    return out
+
+
+def tinygemm_unpack(w: torch.Tensor) -> torch.Tensor:
+    """tinygemm int32 tiles -> (N, K/2) uint8 (odd k low), on the GPU."""
+    dev = _require_cuda(w)
+    nt, kt, _, half = w.shape
+    n, ikt = nt * 8, half * 2
+    k = kt * 16 * ikt
+    out = torch.empty(n, k // 2, device=dev, dtype=torch.uint8)
+    check(load().bq_int4_tinygemm_unpack(w.contiguous().data_ptr(), out.data_ptr(), n, k, ikt, _stream(dev)),
+          "bq_int4_tinygemm_unpack")
+    return out
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6, out=None) -> torch.Tensor:
+    dev = _require_cuda(x, w)
+    m, k = x.shape
+    if out is None:
+        out = torch.empty_like(x)
+    check(load().bq_rmsnorm(x.data_ptr(), x.stride(0), w.data_ptr(), out.data_ptr(), out.stride(0), m, k, eps,
+                            _stream(dev)), "bq_rmsnorm")
+    return out
+
+
+def silu_mul(g: torch.Tensor, u: torch.Tensor, out=None) -> torch.Tensor:
+    dev = _require_cuda(g, u)
+    m, n = g.shape
+    if out is None:
+        out = torch.empty_like(g)
+    check(load().bq_silu_mul(g.data_ptr(), g.stride(0), u.data_ptr(), u.stride(0), out.data_ptr(), out.stride(0),
+                             m, n, _stream(dev)), "bq_silu_mul")
+    return out
+
+
+def device_status(device: int | None = None, clear: bool = False) -> int:
+    """Device-side error bits (BQ_DEVERR_*) accumulated by the kernels."""
+    lib = load()
+    dev = torch.cuda.current_device() if device is None else device
+    bits = ctypes.c_uint32(0)
+    check(lib.bq_device_status(dev, ctypes.byref(bits)), "bq_device_status")
+    if clear:
+        check(lib.bq_device_status_clear(dev), "bq_device_status_clear")
+    return bits.value

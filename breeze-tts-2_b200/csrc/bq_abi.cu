@@ -1,0 +1,254 @@
+// C ABI entry points (include/breeze_b200.h), argument validation, error
+// reporting, device property cache and TMA descriptor encoding.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "bq_device.cuh"
+#include "bq_host.h"
+
+namespace bq {
+
+namespace {
+thread_local char g_err[512] = "no error";
+std::mutex g_mu;
+std::vector<DeviceInfo> g_dev;                         // indexed by device ordinal
+std::vector<std::pair<const void*, int>> g_smem_attr;  // (kernel, device) raised
+}  // namespace
+
+int set_error(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+const DeviceInfo* device_info() {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        set_error(BQ_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (int(g_dev.size()) <= dev) g_dev.resize(dev + 1, DeviceInfo{-1, 0, 0, 0, 0});
+    DeviceInfo& d = g_dev[dev];
+    if (d.device < 0) {
+        DeviceInfo n{dev, 0, 0, 0, 0};
+        if (cudaDeviceGetAttribute(&n.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&n.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&n.major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&n.minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) {
+            set_error(BQ_ERR_CUDA, "cudaDeviceGetAttribute failed on device %d", dev);
+            return nullptr;
+        }
+        d = n;
+    }
+    return &d;
+}
+
+int dtype_size(int dt) { return dt == BQ_DT_F32 ? 4 : 2; }
+
+int ensure_smem_attr(const void* fn, uint32_t bytes) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        for (auto& kv : g_smem_attr)
+            if (kv.first == fn && kv.second == dev) return BQ_OK;
+    }
+    const DeviceInfo* di = device_info();
+    if (!di) return BQ_ERR_CUDA;
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, di->smem_optin);
+    if (e != cudaSuccess) return set_error(BQ_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    (void)bytes;
+    std::lock_guard<std::mutex> lk(g_mu);
+    g_smem_attr.emplace_back(fn, dev);
+    return BQ_OK;
+}
+
+// ---- TMA descriptors ------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+static int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+                     uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return set_error(BQ_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {row_stride_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(BQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+    return BQ_OK;
+}
+
+int encode_weight_maps(const bq_gemv_desc* d, CUtensorMap* tm_w, CUtensorMap* tm_sz) {
+    const uint64_t N = d->N, K = d->K;
+    int rc = BQ_OK;
+    switch (d->wfmt) {
+        case BQ_W_INT4_TINYGEMM:
+            rc = encode_2d(tm_w, CU_TENSOR_MAP_DATA_TYPE_INT32, d->w, K, N / 8, K * 4, 128, 2);
+            break;
+        case BQ_W_INT4_PLAIN:
+            rc = encode_2d(tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, d->w, K / 2, N, K / 2, 64, 16);
+            break;
+        case BQ_W_FP8_E4M3:
+        case BQ_W_INT8:
+            rc = encode_2d(tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, d->w, K, N, K, 64, 16);
+            break;
+        case BQ_W_BF16:
+            rc = encode_2d(tm_w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d->w, K, N, K * 2, 32, 16);
+            break;
+        default:
+            return set_error(BQ_ERR_FORMAT, "unknown weight format %d", d->wfmt);
+    }
+    if (rc) return rc;
+    if (d->wfmt == BQ_W_INT4_TINYGEMM || d->wfmt == BQ_W_INT4_PLAIN) {
+        const int g = d->group;
+        const uint32_t rows = g >= 128 ? 1 : 128 / g;
+        return encode_2d(tm_sz, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d->scale, 2 * N, K / g, 4 * N, 32, rows);
+    }
+    *tm_sz = *tm_w;
+    return BQ_OK;
+}
+
+// ---- validation -------------------------------------------------------------
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int validate_gemv(const bq_gemv_desc* d) {
+    if (!d) return set_error(BQ_ERR_INVALID_ARG, "desc is NULL");
+    if (d->M < 1 || d->N < 1 || d->K < 1)
+        return set_error(BQ_ERR_SHAPE, "M, N, K must be positive (got %d, %d, %d)", d->M, d->N, d->K);
+    if (d->K % 128) return set_error(BQ_ERR_SHAPE, "K=%d must be a multiple of 128", d->K);
+    if (d->wfmt < BQ_W_BF16 || d->wfmt > BQ_W_INT8) return set_error(BQ_ERR_FORMAT, "unknown weight format %d", d->wfmt);
+    if (d->epilogue < BQ_EPI_NONE || d->epilogue > BQ_EPI_ADD_RESIDUAL)
+        return set_error(BQ_ERR_INVALID_ARG, "unknown epilogue %d", d->epilogue);
+    for (int dt : {d->x_dtype, d->out_dtype, d->res_dtype})
+        if (dt < BQ_DT_BF16 || dt > BQ_DT_F32) return set_error(BQ_ERR_INVALID_ARG, "unknown dtype %d", dt);
+    if (!d->x || !d->w || !d->out) return set_error(BQ_ERR_INVALID_ARG, "x, w and out must be non-NULL");
+    if (d->ldx < d->K) return set_error(BQ_ERR_SHAPE, "ldx=%lld < K=%d", (long long)d->ldx, d->K);
+    const int n_out = d->epilogue == BQ_EPI_SILU_MUL ? d->N / 2 : d->N;
+    if (d->ldo < n_out) return set_error(BQ_ERR_SHAPE, "ldo=%lld < output width %d", (long long)d->ldo, n_out);
+    if (d->epilogue == BQ_EPI_SILU_MUL && (d->N % 2))
+        return set_error(BQ_ERR_SHAPE, "SiLU*up epilogue needs an even N (got %d)", d->N);
+    if (d->epilogue == BQ_EPI_ADD_RESIDUAL) {
+        if (!d->residual) return set_error(BQ_ERR_INVALID_ARG, "residual epilogue without a residual");
+        if (d->ldr < n_out) return set_error(BQ_ERR_SHAPE, "ldr=%lld < output width %d", (long long)d->ldr, n_out);
+    }
+    if (!aligned16(d->w)) return set_error(BQ_ERR_ALIGN, "weight pointer must be 16-byte aligned");
+    const bool int4 = d->wfmt == BQ_W_INT4_TINYGEMM || d->wfmt == BQ_W_INT4_PLAIN;
+    if (int4 || d->wfmt == BQ_W_FP8_E4M3 || d->wfmt == BQ_W_INT8) {
+        if (!d->scale) return set_error(BQ_ERR_INVALID_ARG, "this weight format needs a scale tensor");
+    }
+    if (int4) {
+        if (!aligned16(d->scale)) return set_error(BQ_ERR_ALIGN, "scale/zero tensor must be 16-byte aligned");
+        if (d->N % 8) return set_error(BQ_ERR_SHAPE, "int4 weights need N %% 8 == 0 (got %d)", d->N);
+        if (d->epilogue == BQ_EPI_SILU_MUL && ((d->N / 2) % 8))
+            return set_error(BQ_ERR_SHAPE, "int4 SiLU*up needs (N/2) %% 8 == 0 (got N=%d)", d->N);
+        if (d->wfmt == BQ_W_INT4_TINYGEMM) {
+            if (d->group != 32 && d->group != 64 && d->group != 128 && d->group != 256)
+                return set_error(BQ_ERR_SHAPE, "tinygemm int4 group must be 32, 64, 128 or 256 (got %d)", d->group);
+            if (d->K % d->group) return set_error(BQ_ERR_SHAPE, "K=%d not divisible by group %d", d->K, d->group);
+        } else if (d->group != 128) {
+            return set_error(BQ_ERR_SHAPE, "plain int4 layout uses group 128 (got %d)", d->group);
+        }
+    }
+    return BQ_OK;
+}
+
+}  // namespace bq
+
+using namespace bq;
+
+// The GEMV handles up to 16 activation rows per launch; larger M is run as
+// consecutive launches over 16-row blocks.
+static constexpr int kRowsPerLaunch = 16;
+
+extern "C" {
+
+int32_t bq_version(void) { return BQ_VERSION; }
+
+const char* bq_last_error_string(void) { return g_err; }
+
+int32_t bq_device_status(int32_t device, uint32_t* bits) {
+    if (!bits) return set_error(BQ_ERR_INVALID_ARG, "bits is NULL");
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaError_t e = cudaSetDevice(device);
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(bits, g_device_error, sizeof(uint32_t));
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) return set_error(BQ_ERR_CUDA, "reading device status: %s", cudaGetErrorString(e));
+    return BQ_OK;
+}
+
+int32_t bq_device_status_clear(int32_t device) {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    const uint32_t zero = 0;
+    cudaError_t e = cudaSetDevice(device);
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(uint32_t));
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) return set_error(BQ_ERR_CUDA, "clearing device status: %s", cudaGetErrorString(e));
+    return BQ_OK;
+}
+
+int32_t bq_gemv_workspace_bytes(const bq_gemv_desc* desc, size_t* bytes) {
+    if (!bytes) return set_error(BQ_ERR_INVALID_ARG, "bytes is NULL");
+    int rc = validate_gemv(desc);
+    if (rc) return rc;
+    GemvPlan pl;
+    rc = plan_gemv(desc, desc->M > 8 ? kRowsPerLaunch : desc->M, &pl);
+    if (rc) return rc;
+    *bytes = size_t(pl.counters_bytes + pl.partials_bytes);
+    return BQ_OK;
+}
+
+int32_t bq_gemv(const bq_gemv_desc* desc, void* workspace, size_t workspace_bytes, void* stream) {
+    int rc = validate_gemv(desc);
+    if (rc) return rc;
+    const DeviceInfo* di = device_info();
+    if (!di) return BQ_ERR_CUDA;
+    if (di->major != 10) return set_error(BQ_ERR_DEVICE, "sm_%d%d device: this library is built for sm_100a", di->major, di->minor);
+    size_t need = 0;
+    rc = bq_gemv_workspace_bytes(desc, &need);
+    if (rc) return rc;
+    if (!workspace || workspace_bytes < need)
+        return set_error(BQ_ERR_WORKSPACE, "workspace of %zu bytes given, %zu needed", workspace_bytes, need);
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+        return set_error(BQ_ERR_ALIGN, "workspace must be 256-byte aligned");
+    for (int row0 = 0; row0 < desc->M; row0 += kRowsPerLaunch) {
+        const int rows = desc->M - row0 < kRowsPerLaunch ? desc->M - row0 : kRowsPerLaunch;
+        GemvPlan pl;
+        rc = plan_gemv(desc, rows, &pl);
+        if (rc) return rc;
+        rc = launch_gemv(desc, pl, row0, rows, workspace, static_cast<cudaStream_t>(stream));
+        if (rc) return rc;
+    }
+    return BQ_OK;
+}
+
+}  // extern "C"

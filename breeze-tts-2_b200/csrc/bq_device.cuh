@@ -1,0 +1,204 @@
+// Device helpers for sm_100a: mbarriers, TMA tile loads, programmatic
+// dependent launch, m16n8k16 tensor-core MMA and in-register dequantization
+// of int4 / fp8 / int8 weights into f16 pairs. Hand-written inline PTX.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "bq_internal.h"
+
+namespace bq {
+
+// Device error word, one per device (set by bounded waits that give up).
+extern __device__ unsigned int g_device_error;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: gives up after ~kWaitCycles SM cycles, records the failure in
+// the device error word and returns false. Never spins forever.
+constexpr long long kWaitCycles = 4ll << 30;  // ~2 s at 1.9 GHz
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - t0 > kWaitCycles) {
+            atomicOr(&g_device_error, BQ_DEVERR_WAIT_TIMEOUT_BIT);
+            return false;
+        }
+    }
+    return true;
+}
+
+// ---------------------------------------------------------------- TMA
+// 2-D tiled bulk tensor load global -> shared, completion on an mbarrier.
+// No cluster multicast: every CTA fetches its own tiles.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int32_t c0, int32_t c1,
+                                            uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ---------------------------------------------------------------- PDL
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// ---------------------------------------------------------------- loads
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ float2 lds_f2(uint32_t addr) {
+    float2 v;
+    asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
+    return v;
+}
+// L2-coherent loads of data written by other CTAs during this kernel.
+__device__ __forceinline__ float4 ldcg_f4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
+
+// ---------------------------------------------------------------- MMA
+// D = A(16x16, row) * B(16x8, col) + C, fp32 accumulate.
+__device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// ---------------------------------------------------------------- conversions
+template <uint32_t LUT>
+__device__ __forceinline__ uint32_t lop3(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, %4;" : "=r"(d) : "r"(a), "r"(b), "r"(c), "n"(LUT));
+    return d;
+}
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+__device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// Two int4 codes sitting in bits [0,4) and [16,20) of `w` (the 0x000F000F
+// lanes) -> f16x2 {code - OFS}, exact. 0x6400 is 1024.0 in f16; OR-ing a
+// 4-bit code into its mantissa gives 1024 + code.
+template <int OFS>
+__device__ __forceinline__ uint32_t i4lo_to_f16x2(uint32_t w) {
+    constexpr uint32_t kBias = (OFS == 8) ? 0x64086408u : 0x64006400u;  // 1032 / 1024
+    return hsub2(lop3<(0xF0 & 0xCC) | 0xAA>(w, 0x000F000Fu, 0x64006400u), kBias);
+}
+// Codes in bits [4,8) and [20,24) (the 0x00F000F0 lanes): 1024 + 16*code,
+// then (v * 1/16) - (64 + OFS) = code - OFS, exact.
+template <int OFS>
+__device__ __forceinline__ uint32_t i4hi_to_f16x2(uint32_t w) {
+    constexpr uint32_t kScale = 0x2C002C00u;                             // 1/16
+    constexpr uint32_t kBias = (OFS == 8) ? 0xD480D480u : 0xD400D400u;  // -72 / -64
+    return hfma2(lop3<(0xF0 & 0xCC) | 0xAA>(w, 0x00F000F0u, 0x64006400u), kScale, kBias);
+}
+
+// Two e4m3 bytes (low byte -> low half) -> f16x2, exact (hardware cvt).
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint16_t v) {
+    uint32_t d;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(d) : "h"(v));
+    return d;
+}
+
+// Two signed bytes of `w` selected by `sel` (0x4140: bytes 0,1; 0x4342:
+// bytes 2,3) -> f16x2, exact. `wx` is w ^ 0x80808080 (code + 128 unsigned);
+// 0x64 placed above each byte gives 1024 + code + 128.
+__device__ __forceinline__ uint32_t i8pair_to_f16x2(uint32_t wx, uint32_t sel) {
+    return hsub2(prmt(wx, 0x64646464u, sel), 0x64806480u);  // - 1152
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pack_bf162(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float load_act(const void* p, int64_t idx, int dtype) {
+    if (dtype == BQ_DT_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[idx]);
+    if (dtype == BQ_DT_F16) return __half2float(static_cast<const __half*>(p)[idx]);
+    return static_cast<const float*>(p)[idx];
+}
+__device__ __forceinline__ void store_act(void* p, int64_t idx, int dtype, float v) {
+    if (dtype == BQ_DT_BF16)
+        static_cast<__nv_bfloat16*>(p)[idx] = __float2bfloat16_rn(v);
+    else if (dtype == BQ_DT_F16)
+        static_cast<__half*>(p)[idx] = __float2half_rn(v);
+    else
+        static_cast<float*>(p)[idx] = v;
+}
+
+__device__ __forceinline__ float silu(float g) { return g / (1.0f + __expf(-g)); }
+
+}  // namespace bq

@@ -1,0 +1,154 @@
+/*
+ * breeze_b200.h -- C ABI of the B200-native weight-only quantized decode GEMV.
+ *
+ * One shared library (libbreeze_b200.so, built for sm_100a) replaces the
+ * per-token decode linear layers of the reference:
+ *
+ *   models/fused/kernels.py:334  rms_gemv(x, fw, norm_weight, eps, epilogue, residual, out)
+ *   models/fused/kernels.py:41   rms_gemv_kernel      (RMSNorm prologue + streamed GEMV)
+ *   models/fused/kernels.py:107  gemv_epilogue_kernel (split-K sum, fp8 scale, SiLU*up / +residual)
+ *   models/int4_linear.py:99     Int4Linear.forward   (torch._weight_int4pack_mm, tinygemm layout)
+ *   models/fp8_linear.py:68      Fp8Linear.forward    (torch._scaled_mm)
+ *   models/int8_linear.py:50     Int8Linear.forward   (dequant + F.linear)
+ *   models/int4_linear.py:59     torch._convert_weight_to_int4pack (int4 re-tiling)
+ *   models/fused/kernels.py:541  rmsnorm_kernel, :560 silu_mul_kernel (glue)
+ *
+ * Conventions
+ *   - Plain C types only: device pointers are void*, sizes are int32/int64,
+ *     streams are cudaStream_t passed as void*. No torch types.
+ *   - Every entry point returns 0 on success or a negative BQ_ERR_* code and
+ *     never aborts; bq_last_error_string() describes the last failure of the
+ *     calling host thread.
+ *   - Nothing here allocates or frees device memory. Scratch space (split-K
+ *     partial sums and arrival counters) is a caller-provided workspace of
+ *     bq_gemv_workspace_bytes() bytes that must be ZERO-FILLED ONCE before
+ *     its first use; every call leaves the counters at zero again. One
+ *     workspace must not be used by two calls that can run concurrently.
+ *   - Launches are asynchronous on the given stream, take no host
+ *     synchronization and keep a fixed grid for fixed shapes, so they can be
+ *     captured into CUDA graphs.
+ */
+#ifndef BREEZE_B200_H
+#define BREEZE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BQ_VERSION 1
+
+/* ---- status codes ------------------------------------------------------ */
+#define BQ_OK 0
+#define BQ_ERR_INVALID_ARG -1  /* null pointer where one is required, bad enum */
+#define BQ_ERR_SHAPE -2        /* M/N/K/group not supported or inconsistent    */
+#define BQ_ERR_ALIGN -3        /* pointer or stride alignment                  */
+#define BQ_ERR_FORMAT -4       /* weight format / dtype combination            */
+#define BQ_ERR_WORKSPACE -5    /* workspace missing or too small               */
+#define BQ_ERR_CUDA -6         /* a CUDA runtime/driver call failed            */
+#define BQ_ERR_DEVICE -7       /* device is not sm_100 (B200 class)            */
+
+/* Device-side error bits, read with bq_device_status(). */
+#define BQ_DEVERR_WAIT_TIMEOUT 1u /* a bounded mbarrier wait gave up */
+
+/* ---- enums --------------------------------------------------------------- */
+/* Weight formats. */
+#define BQ_W_BF16 0          /* w: bf16 [N, K] row-major (FusedWeight bits=16)             */
+#define BQ_W_INT4_TINYGEMM 1 /* w: int32 [N/8, K/128, 32, 4] (Int4Linear.weight_int4,
+                                innerKTiles=8), scale: bf16 [K/g, N, 2] (scale, zero),
+                                w = (q - 8) * scale + zero, g in {32, 64, 128, 256}          */
+#define BQ_W_INT4_PLAIN 2    /* w: uint8 [N, K/2] even-k low nibble (FusedWeight bits=4),
+                                scale: bf16 [K/128, N, 2] (scale, min), w = q * scale + min  */
+#define BQ_W_FP8_E4M3 3      /* w: e4m3 [N, K] row-major, scale: fp32 [N], w = q * scale    */
+#define BQ_W_INT8 4          /* w: int8 [N, K] row-major, scale: fp32 [N], w = q * scale    */
+
+/* Epilogues (models/fused/kernels.py:116-137). */
+#define BQ_EPI_NONE 0         /* out = acc                                             */
+#define BQ_EPI_SILU_MUL 1     /* out[:, n] = silu(acc[:, n]) * acc[:, n + N/2], N/2 outputs */
+#define BQ_EPI_ADD_RESIDUAL 2 /* out = acc + residual                                  */
+
+/* Activation / output dtypes. */
+#define BQ_DT_BF16 0
+#define BQ_DT_F16 1
+#define BQ_DT_F32 2
+
+/* Flags. */
+#define BQ_FLAG_PDL 1u              /* launch with programmatic dependent launch: weight
+                                       streaming starts before the previous kernel ends  */
+#define BQ_FLAG_SCALE_ROUND_BF16 2u /* int8: round the per-row scale to bf16 first, as
+                                       Int8Linear does for bf16 activations              */
+
+typedef struct bq_gemv_desc {
+    int32_t M;         /* activation rows (decode batch), >= 1 */
+    int32_t N;         /* weight rows = output features (for SILU_MUL: gate+up rows) */
+    int32_t K;         /* input features, multiple of 128 */
+    int32_t wfmt;      /* BQ_W_* */
+    int32_t group;     /* int4 group size (tinygemm: 32/64/128/256; plain: 128) */
+    int32_t epilogue;  /* BQ_EPI_* */
+    int32_t x_dtype;   /* BQ_DT_* */
+    int32_t out_dtype; /* BQ_DT_* */
+    int32_t res_dtype; /* BQ_DT_* (residual) */
+    uint32_t flags;    /* BQ_FLAG_* */
+    float eps;         /* RMSNorm epsilon (used when gamma != NULL) */
+    int32_t reserved;
+    const void* x;        /* [M, ldx] activations (the residual stream when gamma != NULL) */
+    int64_t ldx;          /* row stride of x, elements */
+    const void* gamma;    /* bf16 [K] RMSNorm weight, or NULL for no norm */
+    const void* w;        /* packed weights, 16-byte aligned */
+    const void* scale;    /* see BQ_W_* */
+    const void* bias;     /* bf16 [N] or NULL (int8 / bf16 formats) */
+    const void* residual; /* [M, ldr] for BQ_EPI_ADD_RESIDUAL, else NULL */
+    int64_t ldr;
+    void* out;            /* [M, ldo] */
+    int64_t ldo;
+} bq_gemv_desc;
+
+/* ---- library ----------------------------------------------------------- */
+int32_t bq_version(void);
+const char* bq_last_error_string(void);
+
+/* Device-side error bits accumulated by the kernels on `device` since the
+ * last clear (blocking read; not for use inside stream capture). */
+int32_t bq_device_status(int32_t device, uint32_t* bits);
+int32_t bq_device_status_clear(int32_t device);
+
+/* ---- GEMV (replaces rms_gemv / Int4Linear / Fp8Linear / Int8Linear) ------ */
+/* Workspace bytes needed by bq_gemv for `desc` on the current device. */
+int32_t bq_gemv_workspace_bytes(const bq_gemv_desc* desc, size_t* bytes);
+
+/* out = epilogue( rmsnorm(x) @ dequant(w)^T ), fp32 accumulation.
+ * Replaces models/fused/kernels.py:334-351 (rms_gemv + both kernels),
+ * models/int4_linear.py:99-109, models/fp8_linear.py:68-83 (weight-only),
+ * models/int8_linear.py:50-53. */
+int32_t bq_gemv(const bq_gemv_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- layouts and dequantization ---------------------------------------- */
+/* (N, K/2) uint8 odd-k-low -> tinygemm int32 [N/8, K/(16*ikt), 32, ikt/2].
+ * Replaces torch._convert_weight_to_int4pack (models/int4_linear.py:59). */
+int32_t bq_int4_tinygemm_pack(const void* packed_u8, void* out_i32, int32_t N, int32_t K,
+                              int32_t inner_k_tiles, void* stream);
+/* Inverse of bq_int4_tinygemm_pack (tinygemm int32 -> (N, K/2) uint8). */
+int32_t bq_int4_tinygemm_unpack(const void* in_i32, void* packed_u8, int32_t N, int32_t K,
+                                int32_t inner_k_tiles, void* stream);
+
+/* Dequantized weights W[N, K] as fp32, bit-exact with the reference's
+ * dequantization (int4: fmaf((q-8), s, z) / fmaf(q, s, min); fp8: q * s;
+ * int8: bf16(bf16(q) * bf16(s)); bf16: the value). Uses desc->{N, K, wfmt,
+ * group, w, scale}. For parity checks and debugging. */
+int32_t bq_dequant(const bq_gemv_desc* desc, float* out, void* stream);
+
+/* ---- glue kernels (models/fused/kernels.py:541-575) ---------------------- */
+/* out[M, K] = x * rsqrt(mean(x^2) + eps) * gamma (fp32 math), bf16 in/out. */
+int32_t bq_rmsnorm(const void* x, int64_t ldx, const void* gamma, void* out, int64_t ldo,
+                   int32_t M, int32_t K, float eps, void* stream);
+/* out[M, N] = silu(g) * u, bf16 in/out. */
+int32_t bq_silu_mul(const void* g, int64_t ldg, const void* u, int64_t ldu, void* out, int64_t ldo,
+                    int32_t M, int32_t N, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BREEZE_B200_H */
