@@ -56,6 +56,7 @@ _SIGS = {
     "bq_device_status_clear": (ctypes.c_int32, [ctypes.c_int32]),
     "bq_gemv_workspace_bytes": (ctypes.c_int32, [ctypes.POINTER(GemvDesc), ctypes.POINTER(ctypes.c_size_t)]),
     "bq_gemv": (ctypes.c_int32, [ctypes.POINTER(GemvDesc), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "bq_gemv_noalloc": (ctypes.c_int32, [ctypes.POINTER(GemvDesc), ctypes.c_void_p]),
     "bq_int4_tinygemm_pack": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
                                                ctypes.c_int32, ctypes.c_void_p]),
     "bq_int4_tinygemm_unpack": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,

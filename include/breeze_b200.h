@@ -124,6 +124,17 @@ int32_t bq_gemv_workspace_bytes(const bq_gemv_desc* desc, size_t* bytes);
  * models/int8_linear.py:50-53. */
 int32_t bq_gemv(const bq_gemv_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Same computation as bq_gemv, for callers that cannot allocate device
+ * memory (fixed VRAM budgets, hosts that own all allocations, real-time
+ * threads that must not call cudaMalloc/cudaFree). No counterpart in the
+ * reference. Instead of a caller workspace it uses one 4 MiB scratch array
+ * built into the library (held by every GPU that loads it until exit);
+ * shapes needing more scratch return BQ_ERR_WORKSPACE without launching.
+ * The first call on a device sets the array up (blocking; make it before
+ * any stream capture). All calls on a device share the array: calls whose
+ * kernels can overlap on the GPU race and must be serialized. */
+int32_t bq_gemv_noalloc(const bq_gemv_desc* desc, void* stream);
+
 /* ---- layouts and dequantization ---------------------------------------- */
 /* (N, K/2) uint8 odd-k-low -> tinygemm int32 [N/8, K/(16*ikt), 32, ikt/2].
  * Replaces torch._convert_weight_to_int4pack (models/int4_linear.py:59). */
