@@ -3,6 +3,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -184,9 +185,6 @@ int validate_gemv(const bq_gemv_desc* d) {
 
 using namespace bq;
 
-// The GEMV handles up to 16 activation rows per launch; larger M is run as
-// consecutive launches over 16-row blocks.
-static constexpr int kRowsPerLaunch = 16;
 
 extern "C" {
 
@@ -220,32 +218,39 @@ int32_t bq_gemv_workspace_bytes(const bq_gemv_desc* desc, size_t* bytes) {
     if (!bytes) return set_error(BQ_ERR_INVALID_ARG, "bytes is NULL");
     int rc = validate_gemv(desc);
     if (rc) return rc;
-    GemvPlan pl;
-    rc = plan_gemv(desc, desc->M > 8 ? kRowsPerLaunch : desc->M, &pl);
-    if (rc) return rc;
-    *bytes = size_t(pl.counters_bytes + pl.partials_bytes);
+    const int step = gemv2_rows_per_launch(desc);
+    int64_t need = 0;
+    for (int row0 = 0; row0 < desc->M; row0 += step) {
+        Gemv2Plan pl;
+        rc = plan_gemv2(desc, std::min(step, desc->M - row0), &pl);
+        if (rc) return rc;
+        need = std::max(need, pl.ws_bytes);
+    }
+    *bytes = size_t(need);
     return BQ_OK;
 }
 
 int32_t bq_gemv(const bq_gemv_desc* desc, void* workspace, size_t workspace_bytes, void* stream) {
     int rc = validate_gemv(desc);
     if (rc) return rc;
+    if (desc->gamma && (reinterpret_cast<uintptr_t>(desc->gamma) & 15))
+        return set_error(BQ_ERR_ALIGN, "gamma must be 16-byte aligned");
     const DeviceInfo* di = device_info();
     if (!di) return BQ_ERR_CUDA;
     if (di->major != 10) return set_error(BQ_ERR_DEVICE, "sm_%d%d device: this library is built for sm_100a", di->major, di->minor);
-    size_t need = 0;
-    rc = bq_gemv_workspace_bytes(desc, &need);
-    if (rc) return rc;
-    if (!workspace || workspace_bytes < need)
-        return set_error(BQ_ERR_WORKSPACE, "workspace of %zu bytes given, %zu needed", workspace_bytes, need);
-    if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
-        return set_error(BQ_ERR_ALIGN, "workspace must be 256-byte aligned");
-    for (int row0 = 0; row0 < desc->M; row0 += kRowsPerLaunch) {
-        const int rows = desc->M - row0 < kRowsPerLaunch ? desc->M - row0 : kRowsPerLaunch;
-        GemvPlan pl;
-        rc = plan_gemv(desc, rows, &pl);
+    const int step = gemv2_rows_per_launch(desc);
+    for (int row0 = 0; row0 < desc->M; row0 += step) {
+        Gemv2Plan pl;
+        rc = plan_gemv2(desc, std::min(step, desc->M - row0), &pl);
         if (rc) return rc;
-        rc = launch_gemv(desc, pl, row0, rows, workspace, static_cast<cudaStream_t>(stream));
+        if (pl.ws_bytes > 0) {
+            if (!workspace || int64_t(workspace_bytes) < pl.ws_bytes)
+                return set_error(BQ_ERR_WORKSPACE, "workspace of %zu bytes given, %lld needed", workspace_bytes,
+                                 (long long)pl.ws_bytes);
+            if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+                return set_error(BQ_ERR_ALIGN, "workspace must be 256-byte aligned");
+        }
+        rc = launch_gemv2(desc, pl, row0, workspace, static_cast<cudaStream_t>(stream));
         if (rc) return rc;
     }
     return BQ_OK;

@@ -76,6 +76,15 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// ---------------------------------------------------------------- cp.async
+// 8-byte asynchronous global -> shared copy (L2 only, no registers used).
+__device__ __forceinline__ void cp_async8(uint32_t dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- PDL
 __device__ __forceinline__ void pdl_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -107,7 +116,7 @@ __device__ __forceinline__ float4 ldcg_f4(const float* p) { return __ldcg(reinte
 // D = A(16x16, row) * B(16x8, col) + C, fp32 accumulate.
 __device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                         uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
         "{%0, %1, %2, %3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
@@ -115,7 +124,7 @@ __device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1,
 }
 __device__ __forceinline__ void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
         "{%0, %1, %2, %3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
@@ -160,6 +169,17 @@ __device__ __forceinline__ uint32_t i4hi_to_f16x2(uint32_t w) {
     constexpr uint32_t kScale = 0x2C002C00u;                             // 1/16
     constexpr uint32_t kBias = (OFS == 8) ? 0xD480D480u : 0xD400D400u;  // -72 / -64
     return hfma2(lop3<(0xF0 & 0xCC) | 0xAA>(w, 0x00F000F0u, 0x64006400u), kScale, kBias);
+}
+
+// int4 codes -> f16 pairs WITHOUT removing the magic offset (one LOP3 each).
+// Low lanes (bits 0-3 / 16-19): 1024 + q. High lanes (bits 4-7 / 20-23):
+// 1024 + 16 q. The GEMV pre-scales the activations that meet high lanes by
+// 1/16 and subtracts the offsets once per group from precomputed sums.
+__device__ __forceinline__ uint32_t i4lo_raw(uint32_t w) {
+    return lop3<(0xF0 & 0xCC) | 0xAA>(w, 0x000F000Fu, 0x64006400u);
+}
+__device__ __forceinline__ uint32_t i4hi_raw(uint32_t w) {
+    return lop3<(0xF0 & 0xCC) | 0xAA>(w, 0x00F000F0u, 0x64006400u);
 }
 
 // Two e4m3 bytes (low byte -> low half) -> f16x2, exact (hardware cvt).

@@ -4,7 +4,7 @@
 #include <cuda.h>
 #include <stdint.h>
 
-#include "../../include/breeze_b200.h"
+#include "breeze_b200.h"
 
 #define BQ_DEVERR_WAIT_TIMEOUT_BIT 1u
 
