@@ -38,7 +38,7 @@ import torch  # noqa: E402
 M, K, N = 1, 2048, 6144
 GROUP = 128
 EPS = 1e-6
-# codes + scale + min + x + gamma + out
+# algorithmic bytes of one call: codes + scale + min + x + gamma + out
 ALGO_BYTES = N * K // 2 + 2 * (N * K // GROUP) * 2 + M * K * 2 + K * 2 + M * N * 2
 METRIC = "fused quant GEMV HBM GB/s (% of 8 TB/s) at M=1; decode-step µs/token"
 CONFIG = {"workload": "config1: fused RMSNorm -> int4 g128 GEMV, M=1, K=2048, N=6144 (plain int4 layout)",
@@ -57,11 +57,9 @@ def measured_peak():
     return 6650.0, "fallback"
 
 
-def known_traffic():
-    p = ROOT / "profiles" / "roofline_traffic.json"
-    if p.exists():
-        return json.loads(p.read_text()).get("config1")
-    return None
+# DRAM bytes (read + write) of one gemv2_kernel launch on this workload, from
+# the ncu capture summarised in profiles/gemv2_int4_plain_config1.md.
+NCU_TRAFFIC_BYTES = 6_747_392
 
 
 class ClockSampler:
@@ -229,7 +227,7 @@ def run_ours(args, rank, local_rank, world):
             "pct_of_8TBs": round(100 * achieved / 8000, 1),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                         "traffic": known_traffic(), "algorithmic_bytes_per_launch": ALGO_BYTES},
+                         "traffic": NCU_TRAFFIC_BYTES, "algorithmic_bytes_per_launch": ALGO_BYTES},
             "e2e": {"value": round(e2e_val, 1), "unit": "GB/s", "h2d_bytes_per_step": R * M * K * 2,
                     "d2h_bytes_per_step": R * M * N * 2, "steps": e2e_steps,
                     "how": "eager Python rms_gemv calls, pinned H2D of x and D2H of out per call"},

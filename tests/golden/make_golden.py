@@ -20,7 +20,7 @@ in the order written below, then moved to the device, so the CPU tests can
 regenerate the same inputs. Outputs land in ``--out`` as .npz files (bf16 is
 stored as its uint16 bit pattern, fp8 as uint8) plus meta.json.
 
-    python tests/golden/make_golden.py --ref baseline/_ref --out gpurun_out/golden
+    python tests/golden/make_golden.py --ref baseline/_ref --out <dir>
 """
 
 from __future__ import annotations
@@ -52,7 +52,7 @@ def gen(seed: int) -> torch.Generator:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="baseline/_ref")
-    ap.add_argument("--out", default="gpurun_out/golden")
+    ap.add_argument("--out", default="tests/golden/regen")
     args = ap.parse_args()
     out = Path(args.out)
     out.mkdir(parents=True, exist_ok=True)
