@@ -237,12 +237,71 @@ def run_ours(args, rank, local_rank, world):
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
+    decode = None if args.no_decode_step else decode_step_bench(device, world, local_rank)
+    if rank == 0:
+        if decode is not None:
+            line["decode_step"] = decode
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
 
         del graph
         dist.destroy_process_group()
+
+
+DECODE_FORMATS = ("int4", "fp8", "int8")
+DECODE_ROWS = (1, 2, 4, 8, 16)
+DECODE_LAYERS = 28
+
+
+def decode_step_bench(device, world: int, local_rank: int, replays: int = 10, warmup: int = 3):
+    """Decode-step leg (the 28-layer projection stack + head as one CUDA graph,
+    breeze_b200.fused.stack.DecodeStack) for each weight format and row count.
+    The stack's weights (1.0 GB int4, 1.9 GB fp8/int8) exceed L2 by far, so
+    every replay streams them from HBM. Device time per replay, max over ranks."""
+    from breeze_b200.fused.stack import DecodeStack, synthetic_stack
+
+    results = []
+    cur = torch.cuda.current_stream(device)
+    for fmt in DECODE_FORMATS:
+        layers, head, ln_f = synthetic_stack(fmt, DECODE_LAYERS, device, seed=7)
+        for rows in DECODE_ROWS:
+            st = DecodeStack(layers, head, ln_f, rows=rows)
+            st.x.copy_(torch.randn(rows, st.hidden, device=device, generator=torch.Generator(device=device)
+                                   .manual_seed(rows)).to(torch.bfloat16))
+            st.capture()
+            for _ in range(warmup):
+                st.replay()
+            torch.cuda.synchronize(device)
+            if world > 1:
+                import torch.distributed as dist
+
+                dist.barrier(device_ids=[local_rank])
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(cur)
+            for _ in range(replays):
+                st.replay()
+            e1.record(cur)
+            torch.cuda.synchronize(device)
+            t = torch.tensor([e0.elapsed_time(e1) / replays], device=device, dtype=torch.float64)
+            if world > 1:
+                import torch.distributed as dist
+
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            step_us = float(t.item()) * 1e3
+            wb = st.weight_bytes
+            results.append({"format": fmt, "rows": rows, "step_us": round(step_us, 1),
+                            "us_per_row": round(step_us / rows, 2),
+                            "GBps": round(wb / step_us / 1e3, 1), "weight_bytes": wb,
+                            "finite": bool(torch.isfinite(st.logits).all().item())})
+            del st
+        del layers, head, ln_f
+        torch.cuda.empty_cache()
+    return {"what": f"{DECODE_LAYERS} layers x (QKV 2048->6144 +RMSNorm, O 2048->2048 +residual, "
+                    "gate+up 2048->16384 +RMSNorm +SiLU*up, down 8192->2048 +residual) + head 2048->8192 "
+                    "+RMSNorm (fp32 logits); one CUDA graph of 113 bq_gemv launches with PDL",
+            "launches_per_step": 4 * DECODE_LAYERS + 1, "replays_timed": replays,
+            "l2_policy": "weights 1-1.9 GB per step >> L2", "results": results}
 
 
 def _cpu_inputs():
@@ -313,6 +372,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode-step", action="store_true", help="skip the 28-layer decode-step leg")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

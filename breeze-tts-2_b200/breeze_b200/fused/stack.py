@@ -1,0 +1,218 @@
+"""The projection chain of a decode step, as one CUDA graph of bq_gemv launches.
+
+Per decoder layer, in the order of the reference's FusedDecoderLayer.forward
+(models/fused/layer.py:87-98):
+
+    qkv = rms_gemv(x, Wqkv, ln1)                      # fused RMSNorm prologue
+    h   = gemv(attn, Wo) + x                          # residual epilogue
+    act = silu(gate) * up, [gate|up] = rms_gemv(h, Wgu, ln2)
+    x'  = gemv(act, Wd) + h
+
+then the output head ``logits = rms_gemv(x, Whead, ln_f)`` in fp32 (the
+reference keeps its output heads in fp32, cudagraph/backbone_graph.py:70).
+``attn`` is the attention output; this chain has no attention kernel, so the
+first ``attn_cols`` columns of ``qkv`` (the query block) stand in for it,
+which keeps the data dependency QKV -> O of the real step.
+
+Every projection is one bq_gemv launch (int4 tinygemm / plain, fp8 or int8
+weight-only, bf16), launched with programmatic dependent launch so each
+kernel's weight prefetch overlaps the previous kernel. The whole chain is
+captured once and replayed; static buffers hold every intermediate.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from .. import _lib
+
+
+@dataclass
+class QWeight:
+    """A quantized (or bf16) weight in one of the bq_gemv formats.
+
+    w / scale follow the reference's buffers: Int4Linear ``weight_int4`` and
+    ``scales_zeros`` [K/g, N, 2]; Fp8Linear ``weight_fp8`` and ``weight_scale``;
+    Int8Linear ``weight_int8`` and ``weight_scale``; FusedWeight ``w`` and its
+    scale/min pair.
+    """
+
+    wfmt: int
+    w: torch.Tensor
+    scale: torch.Tensor | None
+    N: int
+    K: int
+    group: int = 128
+
+    @property
+    def nbytes(self) -> int:
+        b = self.w.numel() * self.w.element_size()
+        if self.scale is not None:
+            b += self.scale.numel() * self.scale.element_size()
+        return b
+
+    @classmethod
+    def from_module(cls, mod) -> "QWeight":
+        """Adopt the buffers of an Int4Linear / Fp8Linear / Int8Linear."""
+        name = type(mod).__name__
+        if name == "Int4Linear":
+            return cls(_lib.W_INT4_TINYGEMM, mod.weight_int4, mod.scales_zeros, mod.out_features, mod.in_features,
+                       mod.group_size)
+        if name == "Fp8Linear":
+            return cls(_lib.W_FP8_E4M3, mod.weight_fp8, mod.weight_scale.reshape(-1).float().contiguous(),
+                       mod.out_features, mod.in_features)
+        if name == "Int8Linear":
+            if mod.bias is not None:
+                raise ValueError("DecodeStack projections carry no bias")
+            return cls(_lib.W_INT8, mod.weight_int8, mod.weight_scale.reshape(-1).float().contiguous(),
+                       mod.out_features, mod.in_features)
+        raise TypeError(f"cannot adopt a {name}")
+
+    @classmethod
+    def from_fused(cls, fw) -> "QWeight":
+        """Adopt a FusedWeight (bits 16 / 8 / 4)."""
+        a = fw.gemv_args()
+        return cls(a["wfmt"], fw.w, a["scale"], fw.N, fw.K)
+
+
+def synthetic_weight(fmt: str, n: int, k: int, device, gen: torch.Generator, group: int = 128) -> QWeight:
+    """Seeded random weight for the decode-stack benchmark, generated on
+    ``device``: int4 codes uniform 0..15 (tinygemm tiles) with bf16 scales
+    |N(0, 0.02)| / 7 and zero point 8; fp8 codes from N(0, 64) clamped to
+    +-448 (the spread of a row scaled by absmax / 448) with per-row fp32
+    scales; int8 codes uniform in -127..127 with per-row fp32 scales."""
+    if fmt == "int4":
+        # tinygemm tiles: every nibble of the int32 words is one code
+        w = torch.randint(-(2 ** 31), 2 ** 31 - 1, (n // 8, k // 128, 32, 4), device=device, generator=gen,
+                          dtype=torch.int64).to(torch.int32)
+        s = (torch.randn(k // group, n, device=device, generator=gen).abs() * 0.02 / 7).to(torch.bfloat16)
+        sz = torch.stack([s, torch.zeros_like(s)], dim=-1).contiguous()
+        return QWeight(_lib.W_INT4_TINYGEMM, w, sz, n, k, group)
+    if fmt == "fp8":
+        q = (torch.randn(n, k, device=device, generator=gen, dtype=torch.bfloat16) * 64).clamp(-448, 448)
+        q = q.to(torch.float8_e4m3fn)
+        scale = torch.rand(n, device=device, generator=gen) * (0.08 / 448) + 1e-6
+        return QWeight(_lib.W_FP8_E4M3, q, scale, n, k)
+    if fmt == "int8":
+        q = torch.randint(-127, 128, (n, k), device=device, generator=gen, dtype=torch.int8)
+        scale = torch.rand(n, device=device, generator=gen) * (0.08 / 127) + 1e-6
+        return QWeight(_lib.W_INT8, q, scale, n, k)
+    if fmt == "bf16":
+        w = (torch.randn(n, k, device=device, generator=gen) * 0.02).to(torch.bfloat16)
+        return QWeight(_lib.W_BF16, w, None, n, k)
+    raise ValueError(f"unknown format {fmt!r}")
+
+
+@dataclass
+class DecodeLayer:
+    wqkv: QWeight
+    wo: QWeight
+    wgu: QWeight
+    wd: QWeight
+    ln1: torch.Tensor
+    ln2: torch.Tensor
+
+
+def synthetic_stack(fmt: str, n_layers: int, device, seed: int = 0, hidden: int = 2048, qkv: int = 6144,
+                    inter: int = 8192, head: int = 8192):
+    """Layers of the decode-stack benchmark: QKV hidden->qkv, O hidden->hidden,
+    gate+up hidden->2*inter, down inter->hidden, plus the output head."""
+    gen = torch.Generator(device=device).manual_seed(seed)
+
+    def norm_w():
+        return (1 + 0.1 * torch.randn(hidden, device=device, generator=gen)).to(torch.bfloat16)
+
+    layers = []
+    for _ in range(n_layers):
+        layers.append(DecodeLayer(synthetic_weight(fmt, qkv, hidden, device, gen),
+                                  synthetic_weight(fmt, hidden, hidden, device, gen),
+                                  synthetic_weight(fmt, 2 * inter, hidden, device, gen),
+                                  synthetic_weight(fmt, hidden, inter, device, gen), norm_w(), norm_w()))
+    return layers, synthetic_weight(fmt, head, hidden, device, gen), norm_w()
+
+
+class DecodeStack:
+    """Static-buffer decode step over ``layers`` plus an output head.
+
+    ``x`` (rows, hidden) bf16 is the input of the step, ``logits`` (rows,
+    head N) fp32 its output. ``run()`` enqueues the launches on the current
+    stream; ``capture()`` records them into a CUDA graph that ``replay()``
+    launches.
+    """
+
+    def __init__(self, layers: list[DecodeLayer], head: QWeight, ln_f: torch.Tensor, rows: int,
+                 eps: float = 1e-6, attn_cols: int | None = None):
+        if not layers:
+            raise ValueError("DecodeStack needs at least one layer")
+        dev = layers[0].wqkv.w.device
+        hidden = layers[0].wqkv.K
+        for i, l in enumerate(layers):
+            if l.wqkv.K != hidden or l.wo.N != hidden or l.wgu.K != hidden or l.wd.N != hidden:
+                raise ValueError(f"layer {i}: projections do not match hidden size {hidden}")
+            if l.wgu.N != 2 * l.wd.K or l.wgu.N % 2:
+                raise ValueError(f"layer {i}: gate+up N={l.wgu.N} does not match down K={l.wd.K}")
+        if head.K != hidden:
+            raise ValueError("head K does not match the hidden size")
+        self.layers, self.head, self.ln_f = layers, head, ln_f
+        self.rows, self.eps, self.hidden = rows, eps, hidden
+        self.attn_cols = attn_cols or hidden
+        if self.attn_cols != layers[0].wo.K or self.attn_cols > layers[0].wqkv.N:
+            raise ValueError("attention width must equal O's K and fit inside QKV's N")
+        bf = dict(device=dev, dtype=torch.bfloat16)
+        self.x = torch.zeros(rows, hidden, **bf)
+        self.qkv = torch.zeros(rows, max(l.wqkv.N for l in layers), **bf)
+        self.h = torch.zeros(rows, hidden, **bf)
+        self.act = torch.zeros(rows, max(l.wd.K for l in layers), **bf)
+        self.res = [torch.zeros(rows, hidden, **bf), torch.zeros(rows, hidden, **bf)]
+        self.logits = torch.zeros(rows, head.N, device=dev, dtype=torch.float32)
+        self.graph = None
+
+    @property
+    def weight_bytes(self) -> int:
+        b = self.head.nbytes + self.ln_f.numel() * 2
+        for l in self.layers:
+            b += l.wqkv.nbytes + l.wo.nbytes + l.wgu.nbytes + l.wd.nbytes + 2 * l.ln1.numel() * 2
+        return b
+
+    @property
+    def launches(self) -> int:
+        return 4 * len(self.layers) + 1
+
+    def _gemv(self, x, qw: QWeight, out, gamma=None, epilogue=_lib.EPI_NONE, residual=None):
+        _lib.gemv(x, qw.w, qw.wfmt, qw.N, scale=qw.scale, group=qw.group, gamma=gamma, eps=self.eps,
+                  epilogue=epilogue, residual=residual, out=out, flags=_lib.default_flags())
+
+    def run(self) -> torch.Tensor:
+        x = self.x
+        for i, l in enumerate(self.layers):
+            qkv = self.qkv[:, : l.wqkv.N]
+            self._gemv(x, l.wqkv, qkv, gamma=l.ln1)
+            self._gemv(qkv[:, : self.attn_cols], l.wo, self.h, epilogue=_lib.EPI_ADD_RESIDUAL, residual=x)
+            act = self.act[:, : l.wd.K]
+            self._gemv(self.h, l.wgu, act, gamma=l.ln2, epilogue=_lib.EPI_SILU_MUL)
+            y = self.res[i % 2]
+            self._gemv(act, l.wd, y, epilogue=_lib.EPI_ADD_RESIDUAL, residual=self.h)
+            x = y
+        self._gemv(x, self.head, self.logits, gamma=self.ln_f)
+        return self.logits
+
+    def capture(self) -> None:
+        """Warm up once (sizes the shared workspace), then record the step."""
+        self.run()
+        torch.cuda.synchronize()
+        st = torch.cuda.Stream()
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=st):
+                self.run()
+        torch.cuda.current_stream().wait_stream(st)
+        torch.cuda.synchronize()
+        self.graph = g
+
+    def replay(self) -> None:
+        if self.graph is None:
+            raise RuntimeError("capture() first")
+        self.graph.replay()

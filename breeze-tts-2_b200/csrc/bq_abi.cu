@@ -218,11 +218,11 @@ int32_t bq_gemv_workspace_bytes(const bq_gemv_desc* desc, size_t* bytes) {
     if (!bytes) return set_error(BQ_ERR_INVALID_ARG, "bytes is NULL");
     int rc = validate_gemv(desc);
     if (rc) return rc;
-    const int step = gemv2_rows_per_launch(desc);
+    const int step = gemv3_rows_per_launch(desc);
     int64_t need = 0;
     for (int row0 = 0; row0 < desc->M; row0 += step) {
-        Gemv2Plan pl;
-        rc = plan_gemv2(desc, std::min(step, desc->M - row0), &pl);
+        Gemv3Plan pl;
+        rc = plan_gemv3(desc, std::min(step, desc->M - row0), &pl);
         if (rc) return rc;
         need = std::max(need, pl.ws_bytes);
     }
@@ -238,10 +238,10 @@ int32_t bq_gemv(const bq_gemv_desc* desc, void* workspace, size_t workspace_byte
     const DeviceInfo* di = device_info();
     if (!di) return BQ_ERR_CUDA;
     if (di->major != 10) return set_error(BQ_ERR_DEVICE, "sm_%d%d device: this library is built for sm_100a", di->major, di->minor);
-    const int step = gemv2_rows_per_launch(desc);
+    const int step = gemv3_rows_per_launch(desc);
     for (int row0 = 0; row0 < desc->M; row0 += step) {
-        Gemv2Plan pl;
-        rc = plan_gemv2(desc, std::min(step, desc->M - row0), &pl);
+        Gemv3Plan pl;
+        rc = plan_gemv3(desc, std::min(step, desc->M - row0), &pl);
         if (rc) return rc;
         if (pl.ws_bytes > 0) {
             if (!workspace || int64_t(workspace_bytes) < pl.ws_bytes)
@@ -250,7 +250,7 @@ int32_t bq_gemv(const bq_gemv_desc* desc, void* workspace, size_t workspace_byte
             if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
                 return set_error(BQ_ERR_ALIGN, "workspace must be 256-byte aligned");
         }
-        rc = launch_gemv2(desc, pl, row0, workspace, static_cast<cudaStream_t>(stream));
+        rc = launch_gemv3(desc, pl, row0, workspace, static_cast<cudaStream_t>(stream));
         if (rc) return rc;
     }
     return BQ_OK;

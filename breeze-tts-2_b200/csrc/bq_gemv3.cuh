@@ -1,0 +1,853 @@
+// bq_gemv: decode GEMV for sm_100a, weights streamed by per-warp cp.async rings.
+//
+//   out[m, n] = epilogue( inv[m] * sum_k (x[m,k] * gamma[k]) * W[n, k] )
+//
+//  * Work split: a CTA owns a contiguous range of (unit, k-block) chunks in
+//    unit-major order; ranges end on unit boundaries when units are plentiful
+//    ("owned", no cross-CTA reduction), otherwise the last CTA to finish a
+//    unit sums its pieces. Each of the 8 warps takes a contiguous eighth of
+//    the k-blocks of every unit in the range.
+//  * Weights stream through a warp-private ring in shared memory, filled
+//    with 16-byte cp.async copies (the load/store path): the TMA unit pays
+//    ~150 cycles per box on this part, far too much for the kilobyte tiles
+//    of a GEMV. The first slots are issued before the programmatic-
+//    dependent-launch wait, so a dependent launch prefetches its weights
+//    while the previous kernel runs; completion is tracked per warp with
+//    cp.async groups, so warps never wait for each other until the final
+//    reduction.
+//  * A ring slot holds one k-block of up to UG units (a "unit group"), so the
+//    activation fragments of a k-block are loaded once for all its units.
+//  * Staging is row-parallel: lanes are split into row groups (32 / rows per
+//    row, rounded to a power of two) that reduce sum-of-squares and max|x*g|
+//    with a few shuffles, then rewrite the row as f16 scaled by a per-(warp,
+//    row) power of two. RMSNorm's 1/rms is applied to the accumulator.
+//  * int4 magic offsets (1024 + q, 1024 + 16 q) are removed once per group:
+//    an MMA with a 0/1 indicator operand gives the low- and high-nibble
+//    activation sums of each column directly in the lanes that need them.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "bq_device.cuh"
+#include "bq_host.h"
+
+namespace bq {
+
+struct Gemv3Params {
+    int32_t M, N, K, KB;
+    int32_t epi, group, x_dtype, out_dtype, res_dtype;
+    uint32_t flags;
+    float eps;
+    int32_t n_half;
+    int32_t tpu;         // tiles (16 rows) per unit: 1, or 2 (always 2 for SiLU*up)
+    int32_t n_units;
+    int32_t owned;       // 1: CTA ranges end on unit boundaries
+    int32_t grid;
+    int64_t total_chunks;
+    int32_t ug;          // units per ring slot
+    int32_t ring_slots;  // slots per consumer warp
+    int32_t slot_bytes;
+    int32_t nkbw;        // k-block slots per warp = ceil(KB / 8)
+    int32_t p_max;       // split mode: partial slots per unit
+    int32_t xrow_pitch;  // bytes per staged activation row (per warp)
+    int32_t x_bulk;      // bf16 x with 16-byte aligned rows: staged with 16-byte loads
+    int32_t upc;         // most units any CTA covers
+    int32_t group_shift; // log2(group) for int4
+    uint32_t smem_ring, smem_x, smem_gamma, smem_part, smem_misc;
+    const void* x;
+    const void* w;
+    int64_t ldx;
+    const void* gamma;
+    const void* scale;
+    const void* bias;
+    const void* residual;
+    int64_t ldr;
+    void* out;
+    int64_t ldo;
+    unsigned int* counters;
+    float* partials;
+};
+
+// Misc area (floats): ss[8][16], up[8][16], rowscale[4*32], rowbias[4*32],
+// res[4*32][16], then 8 warps x 16 zero bytes.
+constexpr int kMisc3Bytes = (8 * 16 + 8 * 16 + 128 + 128 + 128 * 16) * 4 + 8 * 16;
+constexpr int kConsumerThreads = 256;
+constexpr int kThreads3 = 256;
+constexpr int kMaxRing = 6;  // cp.async groups a warp keeps in flight
+
+template <int FMT>
+struct Fmt3;
+template <>
+struct Fmt3<BQ_W_BF16> {
+    static constexpr int kBoxes = 4;
+    static constexpr bool kInt4 = false, kF16 = false;
+};
+template <>
+struct Fmt3<BQ_W_INT4_TINYGEMM> {
+    static constexpr int kBoxes = 1;
+    static constexpr bool kInt4 = true, kF16 = true;
+    static constexpr int kOfs = 8;
+};
+template <>
+struct Fmt3<BQ_W_INT4_PLAIN> {
+    static constexpr int kBoxes = 1;
+    static constexpr bool kInt4 = true, kF16 = true;
+    static constexpr int kOfs = 0;
+};
+template <>
+struct Fmt3<BQ_W_FP8_E4M3> {
+    static constexpr int kBoxes = 2;
+    static constexpr bool kInt4 = false, kF16 = true;
+};
+template <>
+struct Fmt3<BQ_W_INT8> {
+    static constexpr int kBoxes = 2;
+    static constexpr bool kInt4 = false, kF16 = true;
+};
+
+// Units per ring slot at most: keeps the accumulators at <= 32 registers.
+template <int MT, int TPU>
+constexpr int ug_max() {
+    return (MT * TPU >= 4) ? 2 : 4;
+}
+
+__device__ __forceinline__ float bf16lo(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t u) { return __uint_as_float(u & 0xFFFF0000u); }
+
+// Bulk prefetch of a global range into L2 (TMA unit; 16-byte aligned, size a multiple of 16).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Waits until at most n of this thread's cp.async groups are still pending.
+__device__ __forceinline__ void cp_async_wait_upto(int n) {
+    switch (n) {
+        case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
+        case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
+        case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
+        case 3: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
+        case 4: asm volatile("cp.async.wait_group 4;" ::: "memory"); break;
+        case 5: asm volatile("cp.async.wait_group 5;" ::: "memory"); break;
+        default: asm volatile("cp.async.wait_group 6;" ::: "memory"); break;
+    }
+}
+// 16-byte copy, or 16 zero bytes when `ok` is false (src is then not read).
+__device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, bool ok) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(ok ? 16 : 0) : "memory");
+}
+
+template <int FMT, int MT, int TPU, int GPK>
+__global__ void __launch_bounds__(kThreads3, 2) gemv3_kernel(const Gemv3Params p) {
+    using F = Fmt3<FMT>;
+    constexpr int UGM = ug_max<MT, TPU>();
+    constexpr int NCH = MT == 1 ? 4 : 2;  // independent MMA chains per tile
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int KB = p.KB, M = p.M;
+    const uint32_t sbase = smem_u32(smem);
+    const int RS = p.ring_slots, UG = p.ug;
+    const int gpk_box = (FMT == BQ_W_INT4_TINYGEMM) ? (p.group >= 128 ? 1 : 128 / p.group) : 1;
+    const int szb = F::kInt4 ? ((64 * gpk_box + 127) / 128) * 128 : 0;
+    const int tile_bytes = F::kBoxes * kBoxBytes + szb;
+    const bool norm = p.gamma != nullptr;
+
+    // ---- this CTA's chunk range (32-bit: the host keeps grid * chunks < 2^32)
+    uint32_t cb, ce;
+    if (p.owned) {
+        cb = (blockIdx.x * uint32_t(p.n_units) / uint32_t(p.grid)) * uint32_t(KB);
+        ce = ((blockIdx.x + 1) * uint32_t(p.n_units) / uint32_t(p.grid)) * uint32_t(KB);
+    } else {
+        const uint32_t T = uint32_t(p.total_chunks);
+        cb = blockIdx.x * T / uint32_t(p.grid);
+        ce = (blockIdx.x + 1) * T / uint32_t(p.grid);
+    }
+    const int u_first = int(cb / uint32_t(KB));
+    const int u_last = int((ce - 1) / uint32_t(KB));
+    const int nu = u_last - u_first + 1;  // 1..upc
+    const int lo0 = int(cb - uint32_t(u_first) * KB), hi_last = int((ce - 1) - uint32_t(u_last) * KB);
+    const int ngroups = (nu + UG - 1) / UG;
+    auto valid = [&](int ul, int kb) {
+        return ul < nu && (ul > 0 || kb >= lo0) && (ul < nu - 1 || kb <= hi_last);
+    };
+    auto any_valid = [&](int g, int kb) {
+        bool v = false;
+#pragma unroll
+        for (int i = 0; i < UGM; ++i) v |= (i < UG) && valid(g * UG + i, kb);
+        return v;
+    };
+    // this warp's k-blocks: [kw0, kw0 + nkw), a contiguous eighth of K
+    const int kw0 = (warp * KB) >> 3, nkw = (((warp + 1) * KB) >> 3) - kw0;
+    // (group, k-slot) issue order: advance to the next entry with work
+    auto normalize = [&](int& g, int& j) {
+        while (g < ngroups) {
+            if (j < nkw && any_valid(g, kw0 + j)) return;
+            if (j + 1 < nkw) {
+                ++j;
+            } else {
+                j = 0;
+                ++g;
+            }
+        }
+    };
+    auto tile_row = [&](int unit, int tile) -> int {
+        if (p.epi == BQ_EPI_SILU_MUL) return tile == 0 ? 16 * unit : p.n_half + 16 * unit;
+        return (16 * TPU) * unit + 16 * tile;
+    };
+
+    const int pitch = p.xrow_pitch;
+    const uint32_t xs0 = sbase + p.smem_x;                        // [8][M + 1][pitch]
+    const uint32_t gs0 = sbase + p.smem_gamma;                    // [8][nkbw][256]
+    const uint32_t ring_w = sbase + p.smem_ring + warp * RS * p.slot_bytes;  // [RS][slot_bytes]
+
+    // ---- weight copies of one ring slot (whole warp; one cp.async group)
+    const uint8_t* wg = static_cast<const uint8_t*>(p.w);
+    const uint8_t* szg = static_cast<const uint8_t*>(p.scale);
+    auto issue = [&](int slot, int g, int j) {
+        const int kb = kw0 + j;
+        const uint32_t dst0 = ring_w + slot * p.slot_bytes;
+#pragma unroll
+        for (int i = 0; i < UGM; ++i) {
+            if (!(i < UG && valid(g * UG + i, kb))) continue;
+            const int unit = u_first + g * UG + i;
+#pragma unroll
+            for (int tile = 0; tile < TPU; ++tile) {
+                const int row = tile_row(unit, tile);
+                const uint32_t d = dst0 + (i * TPU + tile) * tile_bytes;
+                if constexpr (FMT == BQ_W_INT4_TINYGEMM) {
+                    // two 8-row tiles, 512 contiguous bytes each per k-block
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        const int pc = lane + 32 * q, nt = (row >> 3) + (pc >> 5);
+                        const bool ok = nt * 8 < p.N;
+                        cp_async16_zfill(d + pc * 16, wg + ((int64_t(ok ? nt : 0) * KB + kb) * 512 + (pc & 31) * 16), ok);
+                    }
+                } else {
+                    // row-major: 16 rows x RB bytes per k-block, stored as 64-byte boxes [b][16][64]
+                    constexpr int RB = (FMT == BQ_W_INT4_PLAIN) ? 64 : (FMT == BQ_W_BF16 ? 256 : 128);
+                    const int64_t ld = (FMT == BQ_W_INT4_PLAIN) ? p.K / 2 : (FMT == BQ_W_BF16 ? int64_t(p.K) * 2 : p.K);
+#pragma unroll
+                    for (int q = 0; q < RB / 32; ++q) {
+                        const int pc = lane + 32 * q, r = pc / (RB / 16), c = pc % (RB / 16);
+                        const bool ok = row + r < p.N;
+                        cp_async16_zfill(d + (c >> 2) * kBoxBytes + r * 64 + (c & 3) * 16,
+                                         wg + (int64_t(ok ? row + r : 0) * ld + int64_t(kb) * RB + c * 16), ok);
+                    }
+                }
+                if constexpr (F::kInt4) {
+                    // scale/zero pairs of the 16 rows: 64 contiguous bytes per group
+                    if (lane < 4 * gpk_box) {
+                        const int gi = lane >> 2;
+                        const int grp = p.group >= 128 ? (kb << 7) >> p.group_shift : kb * gpk_box + gi;
+                        const bool ok = row + 4 * (lane & 3) < p.N;  // 4 rows per 16 bytes; N % 8 == 0
+                        cp_async16_zfill(d + F::kBoxes * kBoxBytes + gi * 64 + (lane & 3) * 16,
+                                         szg + ((int64_t(grp) * p.N + (ok ? row : 0)) * 4 + (lane & 3) * 16), ok);
+                    }
+                }
+            }
+        }
+        cp_async_commit();
+    };
+
+    // ---- pull this CTA's whole weight slice into L2 before anything else:
+    // the rings then refill from L2, not HBM, after the dependent-launch wait
+    {
+        const int64_t row_bytes = (FMT == BQ_W_INT4_PLAIN || FMT == BQ_W_INT4_TINYGEMM)
+                                      ? p.K / 2
+                                      : (FMT == BQ_W_BF16 ? int64_t(p.K) * 2 : p.K);
+        int r0[2], r1[2], nr = 1;
+        if (p.epi == BQ_EPI_SILU_MUL) {
+            r0[0] = 16 * u_first;
+            r1[0] = min(p.n_half, 16 * (u_first + nu));
+            r0[1] = p.n_half + 16 * u_first;
+            r1[1] = min(p.N, p.n_half + 16 * (u_first + nu));
+            nr = 2;
+        } else {
+            r0[0] = 16 * TPU * u_first;
+            r1[0] = min(p.N, 16 * TPU * (u_first + nu));
+        }
+        if (threadIdx.x == 0) {
+            for (int q = 0; q < nr; ++q) {
+                int64_t off = int64_t(r0[q]) * row_bytes;
+                const int64_t end = int64_t(r1[q]) * row_bytes;
+                for (; off < end; off += 65536)
+                    bulk_prefetch_l2(wg + off, uint32_t(end - off < 65536 ? end - off : 65536));
+            }
+        }
+        if constexpr (F::kInt4) {
+            // scale/zero rows [r0, r1) of every group row: 128-byte lines
+            const int ngrp = p.K / p.group;
+            for (int q = 0; q < nr; ++q) {
+                const int lines = ((r1[q] - r0[q]) * 4 + 127) / 128 + 1;
+                for (int t = threadIdx.x; t < ngrp * lines; t += kConsumerThreads) {
+                    const int gr = t / lines, l = t - gr * lines;
+                    const int64_t a = (int64_t(gr) * p.N + r0[q]) * 4 + l * 128;
+                    if (a < (int64_t(gr) * p.N + r1[q]) * 4) prefetch_l2(szg + a);
+                }
+            }
+        }
+    }
+
+    // ======================================================= consumer warps
+    const int tq = lane & 3, tg = lane >> 2;
+    float* misc = reinterpret_cast<float*>(smem + p.smem_misc);
+    float* s_ss = misc;            // [8][16]
+    float* s_up = misc + 128;      // [8][16]
+    float* s_rscale = misc + 256;  // [128]
+    float* s_rbias = misc + 384;   // [128]
+    float* s_res = misc + 512;     // [128][16]
+    const uint32_t zero_blk = sbase + p.smem_misc + (512 + 128 * 16) * 4 + warp * 16;
+    if (lane < 4) reinterpret_cast<uint32_t*>(smem + p.smem_misc + (512 + 128 * 16) * 4 + warp * 16)[lane] = 0u;
+    uint8_t* xw_ptr = smem + p.smem_x + warp * (M + 1) * pitch;
+    const uint32_t xw = xs0 + warp * (M + 1) * pitch;
+    const uint8_t* xzero = xw_ptr + M * pitch;  // zero row: B fragments of rows >= M
+    for (int b = lane * 16; b < pitch; b += 32 * 16)
+        *reinterpret_cast<uint4*>(const_cast<uint8_t*>(xzero) + b) = make_uint4(0u, 0u, 0u, 0u);
+    for (int r = threadIdx.x; r < nu * 32; r += kConsumerThreads) {
+        const int ul = r >> 5, rr = r & 31, tile = rr >> 4;
+        float sc = 1.f, bi = 0.f;
+        if (tile < TPU) {
+            const int n = tile_row(u_first + ul, tile) + (rr & 15);
+            if (n < p.N) {
+                if constexpr (FMT == BQ_W_FP8_E4M3 || FMT == BQ_W_INT8) {
+                    sc = static_cast<const float*>(p.scale)[n];
+                    if (FMT == BQ_W_INT8 && (p.flags & BQ_FLAG_SCALE_ROUND_BF16))
+                        sc = __bfloat162float(__float2bfloat16_rn(sc));
+                }
+                if (p.bias) bi = load_act(p.bias, n, p.out_dtype);
+            }
+        }
+        s_rscale[r] = sc;
+        s_rbias[r] = bi;
+    }
+
+    // gamma (the oldest cp.async group), then the first ring slots: all
+    // static, so issued before the programmatic-dependent-launch wait
+    if (norm) {
+        const __nv_bfloat16* gam = static_cast<const __nv_bfloat16*>(p.gamma);
+        for (int s = lane; s < nkw * 16; s += 32)
+            cp_async16(gs0 + (warp * p.nkbw + (s >> 4)) * 256 + (s & 15) * 16, gam + (kw0 + (s >> 4)) * 128 + (s & 15) * 8);
+    }
+    cp_async_commit();
+    int ig = 0, ij = 0, issued = 0;
+    normalize(ig, ij);
+    for (; issued < RS && ig < ngroups; ++issued) {
+        issue(issued, ig, ij);
+        if (ij + 1 < nkw) {
+            ++ij;
+        } else {
+            ij = 0;
+            ++ig;
+        }
+        normalize(ig, ij);
+    }
+
+    pdl_launch_dependents();
+    pdl_wait();
+
+    if (p.epi == BQ_EPI_ADD_RESIDUAL) {
+        for (int r = threadIdx.x; r < nu * 32; r += kConsumerThreads) {
+            const int ul = r >> 5, rr = r & 31, tile = rr >> 4;
+            const int n = tile < TPU ? tile_row(u_first + ul, tile) + (rr & 15) : p.N;
+            for (int m = 0; m < M; ++m) s_res[r * 16 + m] = n < p.N ? load_act(p.residual, m * p.ldr + n, p.res_dtype) : 0.f;
+        }
+    }
+
+    if (p.x_bulk) {
+        // this warp's k-blocks of every row, 16 bytes per lane per load
+        const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(p.x);
+        const int per_row = nkw * 16, segs = M * per_row;
+        for (int s0 = 0; s0 < segs; s0 += 128) {
+            uint4 v[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int s = s0 + q * 32 + lane;
+                if (s < segs) {
+                    const int m = s / per_row, r = s - m * per_row;
+                    v[q] = __ldcg(reinterpret_cast<const uint4*>(xb + m * p.ldx + (kw0 + (r >> 4)) * 128 + (r & 15) * 8));
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int s = s0 + q * 32 + lane;
+                if (s < segs) {
+                    const int m = s / per_row, r = s - m * per_row;
+                    *reinterpret_cast<uint4*>(xw_ptr + m * pitch + (r >> 4) * 256 + (r & 15) * 16) = v[q];
+                }
+            }
+        }
+    }
+    cp_async_wait_upto(issued);  // gamma landed (weight groups may still be pending)
+    __syncwarp();
+
+    // ---- staging: row groups of kp lanes, 16-byte units (8 values = one 8-k group)
+    {
+        int lg = 0;
+        while ((1 << lg) < M) ++lg;   // rows rounded up to a power of two
+        const int kp_log = 5 - lg, kp = 1 << kp_log;
+        const int lm = lane >> kp_log, lk = lane & (kp - 1);
+        const int nunits = 16 * nkw;
+        const bool rowok = lm < M;
+        const uint8_t* grow = smem + p.smem_gamma + warp * p.nkbw * 256;
+        uint8_t* xrow = xw_ptr + lm * pitch;
+        auto load8 = [&](int t, float (&v)[8]) {
+            const int jj = t >> 4, off = jj * 256 + (t & 15) * 16;
+            if (p.x_bulk) {
+                const uint4 r = *reinterpret_cast<const uint4*>(xrow + off);
+                v[0] = bf16lo(r.x); v[1] = bf16hi(r.x); v[2] = bf16lo(r.y); v[3] = bf16hi(r.y);
+                v[4] = bf16lo(r.z); v[5] = bf16hi(r.z); v[6] = bf16lo(r.w); v[7] = bf16hi(r.w);
+            } else {
+                const int64_t base = int64_t(lm) * p.ldx + int64_t(kw0 + jj) * 128 + (t & 15) * 8;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] = load_act(p.x, base + e, p.x_dtype);
+            }
+            if (norm) {
+                const uint4 gv = *reinterpret_cast<const uint4*>(grow + off);
+                v[0] *= bf16lo(gv.x); v[1] *= bf16hi(gv.x); v[2] *= bf16lo(gv.y); v[3] *= bf16hi(gv.y);
+                v[4] *= bf16lo(gv.z); v[5] *= bf16hi(gv.z); v[6] *= bf16lo(gv.w); v[7] *= bf16hi(gv.w);
+            }
+        };
+        // pass 1: sum of squares of x (not x*gamma) and max |x * gamma|
+        float ss = 0.f, amax = 0.f;
+        if (rowok) {
+#pragma unroll 2
+            for (int t = lk; t < nunits; t += kp) {
+                const int jj = t >> 4, off = jj * 256 + (t & 15) * 16;
+                float v[8];
+                if (p.x_bulk) {
+                    const uint4 r = *reinterpret_cast<const uint4*>(xrow + off);
+                    v[0] = bf16lo(r.x); v[1] = bf16hi(r.x); v[2] = bf16lo(r.y); v[3] = bf16hi(r.y);
+                    v[4] = bf16lo(r.z); v[5] = bf16hi(r.z); v[6] = bf16lo(r.w); v[7] = bf16hi(r.w);
+                } else {
+                    const int64_t base = int64_t(lm) * p.ldx + int64_t(kw0 + jj) * 128 + (t & 15) * 8;
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) v[e] = load_act(p.x, base + e, p.x_dtype);
+                }
+                float gg[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
+                if (norm) {
+                    const uint4 gv = *reinterpret_cast<const uint4*>(grow + off);
+                    gg[0] = bf16lo(gv.x); gg[1] = bf16hi(gv.x); gg[2] = bf16lo(gv.y); gg[3] = bf16hi(gv.y);
+                    gg[4] = bf16lo(gv.z); gg[5] = bf16hi(gv.z); gg[6] = bf16lo(gv.w); gg[7] = bf16hi(gv.w);
+                }
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    ss = fmaf(v[e], v[e], ss);
+                    amax = fmaxf(amax, fabsf(v[e] * gg[e]));
+                }
+            }
+        }
+        for (int o = kp >> 1; o; o >>= 1) {
+            ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        }
+        int e = 0;
+        if (F::kF16 && amax > 0.f && amax < INFINITY) {
+            int ex;
+            frexpf(amax, &ex);
+            e = min(max(ex - 15, -100), 100);
+        }
+        const float down = __int_as_float((127 - e) << 23);
+        if (lk == 0 && lm < M) {
+            s_ss[warp * 16 + lm] = ss;
+            s_up[warp * 16 + lm] = __int_as_float((127 + e) << 23);
+        }
+        // pass 2: rewrite the row in place as f16 (bf16 for bf16 weights)
+        if (rowok) {
+#pragma unroll 2
+            for (int t = lk; t < nunits; t += kp) {
+                const int off = (t >> 4) * 256 + (t & 15) * 16;
+                float v[8];
+                load8(t, v);
+                uint4 o;
+                if constexpr (F::kInt4) {
+                    // activations that meet high-nibble operand lanes carry 1/16:
+                    // tinygemm k % 16 >= 8 (odd units), plain layout odd k
+                    float sc[8];
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                        sc[q] = ((FMT == BQ_W_INT4_TINYGEMM) ? (t & 1) : (q & 1)) ? down * 0.0625f : down;
+                    if constexpr (FMT == BQ_W_INT4_PLAIN) {
+                        // pair order {s0,s4},{s1,s5},{s2,s6},{s3,s7}
+                        o.x = pack_half2(v[0] * sc[0], v[4] * sc[4]);
+                        o.y = pack_half2(v[1] * sc[1], v[5] * sc[5]);
+                        o.z = pack_half2(v[2] * sc[2], v[6] * sc[6]);
+                        o.w = pack_half2(v[3] * sc[3], v[7] * sc[7]);
+                    } else {
+                        o.x = pack_half2(v[0] * sc[0], v[1] * sc[1]);
+                        o.y = pack_half2(v[2] * sc[2], v[3] * sc[3]);
+                        o.z = pack_half2(v[4] * sc[4], v[5] * sc[5]);
+                        o.w = pack_half2(v[6] * sc[6], v[7] * sc[7]);
+                    }
+                } else if constexpr (F::kF16) {
+                    o.x = pack_half2(v[0] * down, v[1] * down);
+                    o.y = pack_half2(v[2] * down, v[3] * down);
+                    o.z = pack_half2(v[4] * down, v[5] * down);
+                    o.w = pack_half2(v[6] * down, v[7] * down);
+                } else {
+                    o.x = pack_bf162(v[0], v[1]);
+                    o.y = pack_bf162(v[2], v[3]);
+                    o.z = pack_bf162(v[4], v[5]);
+                    o.w = pack_bf162(v[6], v[7]);
+                }
+                *reinterpret_cast<uint4*>(xrow + off) = o;
+            }
+        }
+    }
+    __syncwarp();
+
+    // activation fragments (B operand) of k-slot j, per M tile
+    auto load_bfrag = [&](int j, uint32_t (&bfr)[MT][16]) {
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+            if constexpr (FMT == BQ_W_INT4_TINYGEMM) {
+                const int m = 8 * mt + (lane & 7);
+                const int koff = ((lane >> 4) * 16) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const uint32_t a = m < M ? xw + m * pitch + (j * 128 + q * 32 + koff) * 2 : zero_blk;
+                    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                                 : "=r"(bfr[mt][4 * q]), "=r"(bfr[mt][4 * q + 1]), "=r"(bfr[mt][4 * q + 2]),
+                                   "=r"(bfr[mt][4 * q + 3])
+                                 : "r"(a)
+                                 : "memory");
+                }
+            } else {
+                const int m = 8 * mt + tg;
+                const uint8_t* row = (m < M ? xw_ptr + m * pitch : xzero) + j * 256;
+                uint4 v[4];
+                if constexpr (FMT == BQ_W_FP8_E4M3 || FMT == BQ_W_INT8) {
+                    v[0] = *reinterpret_cast<const uint4*>(row + (16 * tq) * 2);
+                    v[1] = *reinterpret_cast<const uint4*>(row + (16 * tq) * 2 + 16);
+                    v[2] = *reinterpret_cast<const uint4*>(row + (64 + 16 * tq) * 2);
+                    v[3] = *reinterpret_cast<const uint4*>(row + (64 + 16 * tq) * 2 + 16);
+                } else if constexpr (FMT == BQ_W_BF16) {
+#pragma unroll
+                    for (int h = 0; h < 4; ++h) v[h] = *reinterpret_cast<const uint4*>(row + (32 * h + 8 * tq) * 2);
+                } else {
+#pragma unroll
+                    for (int jj = 0; jj < 4; ++jj) v[jj] = *reinterpret_cast<const uint4*>(row + (32 * tq + 8 * jj) * 2);
+                }
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    bfr[mt][4 * h + 0] = v[h].x;
+                    bfr[mt][4 * h + 1] = v[h].y;
+                    bfr[mt][4 * h + 2] = v[h].z;
+                    bfr[mt][4 * h + 3] = v[h].w;
+                }
+            }
+        }
+    };
+
+    // ---- main loop: unit groups, then this warp's k-slots
+    float* part = reinterpret_cast<float*>(smem + p.smem_part);  // [upc][8 warps][TPU][MT][32][4]
+    int slot = 0, consumed = 0;
+#pragma unroll 1
+    for (int g = 0; g < ngroups; ++g) {
+        float acc[UGM][TPU][MT][4];
+#pragma unroll
+        for (int i = 0; i < UGM; ++i)
+#pragma unroll
+            for (int b = 0; b < TPU; ++b)
+#pragma unroll
+                for (int c = 0; c < MT; ++c)
+#pragma unroll
+                    for (int d = 0; d < 4; ++d) acc[i][b][c][d] = 0.f;
+#pragma unroll 1
+        for (int j = 0; j < nkw; ++j) {
+            const int kb = kw0 + j;
+            if (!any_valid(g, kb)) continue;
+            // this slot's group is complete once at most issued - 1 - consumed newer ones are pending
+            cp_async_wait_upto(issued - 1 - consumed);
+            __syncwarp();
+            {
+                const uint8_t* src0 = smem + p.smem_ring + (warp * RS + slot) * p.slot_bytes;
+                uint32_t bfr[MT][16];
+                load_bfrag(j, bfr);
+                // int4: per-group (A, X) of columns m0, m0+1 from indicator MMAs
+                float sA[GPK][MT][2], sX[GPK][MT][2];
+                if constexpr (F::kInt4) {
+#pragma unroll
+                    for (int sg = 0; sg < GPK; ++sg) {
+                        float c2[2][MT][4];
+#pragma unroll
+                        for (int h = 0; h < 2; ++h)
+#pragma unroll
+                            for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                                for (int d = 0; d < 4; ++d) c2[h][mt][d] = 0.f;
+#pragma unroll
+                        for (int ii = 0; ii < 8 / GPK; ++ii) {
+                            const int i = sg * (8 / GPK) + ii;
+#pragma unroll
+                            for (int mt = 0; mt < MT; ++mt)
+                                mma_f16(c2[ii & 1][mt], 0x3C003C00u, 0u, 0u, 0x3C003C00u, bfr[mt][2 * i],
+                                        bfr[mt][2 * i + 1]);
+                        }
+#pragma unroll
+                        for (int mt = 0; mt < MT; ++mt) {
+                            // c0/c1: low-nibble sums of columns m0, m0+1; c2/c3: high-nibble sums
+                            const float lo0 = c2[0][mt][0] + c2[1][mt][0], lo1 = c2[0][mt][1] + c2[1][mt][1];
+                            const float hi0 = c2[0][mt][2] + c2[1][mt][2], hi1 = c2[0][mt][3] + c2[1][mt][3];
+                            sX[sg][mt][0] = lo0 + 16.f * hi0;
+                            sX[sg][mt][1] = lo1 + 16.f * hi1;
+                            sA[sg][mt][0] = 1024.f * (lo0 + hi0) + float(F::kOfs) * sX[sg][mt][0];
+                            sA[sg][mt][1] = 1024.f * (lo1 + hi1) + float(F::kOfs) * sX[sg][mt][1];
+                        }
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < UGM; ++i) {
+                    if (!(i < UG && valid(g * UG + i, kb))) continue;
+#pragma unroll
+                    for (int tile = 0; tile < TPU; ++tile) {
+                        const uint8_t* src = src0 + (i * TPU + tile) * tile_bytes;
+                        if constexpr (F::kInt4) {
+                            const uint4 r0 = *reinterpret_cast<const uint4*>(src + lane * 16);
+                            const uint4 r1 = *reinterpret_cast<const uint4*>(src + 512 + lane * 16);
+                            const uint32_t w0[4] = {r0.x, r0.y, r0.z, r0.w};
+                            const uint32_t w1[4] = {r1.x, r1.y, r1.z, r1.w};
+                            const uint8_t* szs = src + kBoxBytes;
+#pragma unroll
+                            for (int sg = 0; sg < GPK; ++sg) {
+                                float c2[NCH][MT][4];
+#pragma unroll
+                                for (int h = 0; h < NCH; ++h)
+#pragma unroll
+                                    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                                        for (int d = 0; d < 4; ++d) c2[h][mt][d] = 0.f;
+#pragma unroll
+                                for (int ii = 0; ii < 8 / GPK; ++ii) {
+                                    const int ki = sg * (8 / GPK) + ii;
+                                    const uint32_t x0 = (ki & 1) ? (w0[ki >> 1] >> 8) : w0[ki >> 1];
+                                    const uint32_t x1 = (ki & 1) ? (w1[ki >> 1] >> 8) : w1[ki >> 1];
+                                    const uint32_t a0 = i4lo_raw(x0), a2 = i4hi_raw(x0);
+                                    const uint32_t a1 = i4lo_raw(x1), a3 = i4hi_raw(x1);
+#pragma unroll
+                                    for (int mt = 0; mt < MT; ++mt)
+                                        mma_f16(c2[ii % NCH][mt], a0, a1, a2, a3, bfr[mt][2 * ki], bfr[mt][2 * ki + 1]);
+                                }
+#pragma unroll
+                                for (int h = 1; h < NCH; ++h)
+#pragma unroll
+                                    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                                        for (int d = 0; d < 4; ++d) c2[0][mt][d] += c2[h][mt][d];
+                                const int gi = (p.group >= 128) ? 0 : sg;
+                                const uint32_t sz0 = *reinterpret_cast<const uint32_t*>(szs + gi * 64 + tg * 4);
+                                const uint32_t sz1 = *reinterpret_cast<const uint32_t*>(szs + gi * 64 + (tg + 8) * 4);
+                                const float s0 = bf16lo(sz0), z0 = bf16hi(sz0), s1 = bf16lo(sz1), z1 = bf16hi(sz1);
+#pragma unroll
+                                for (int mt = 0; mt < MT; ++mt) {
+                                    float* a = acc[i][tile][mt];
+                                    a[0] += s0 * (c2[0][mt][0] - sA[sg][mt][0]) + z0 * sX[sg][mt][0];
+                                    a[1] += s0 * (c2[0][mt][1] - sA[sg][mt][1]) + z0 * sX[sg][mt][1];
+                                    a[2] += s1 * (c2[0][mt][2] - sA[sg][mt][0]) + z1 * sX[sg][mt][0];
+                                    a[3] += s1 * (c2[0][mt][3] - sA[sg][mt][1]) + z1 * sX[sg][mt][1];
+                                }
+                            }
+                        } else {
+                            float c2[NCH][MT][4];
+#pragma unroll
+                            for (int h = 0; h < NCH; ++h)
+#pragma unroll
+                                for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                                    for (int d = 0; d < 4; ++d) c2[h][mt][d] = 0.f;
+#pragma unroll
+                            for (int b = 0; b < F::kBoxes; ++b) {
+                                const uint8_t* box = src + b * kBoxBytes;
+                                const uint4 r0 = *reinterpret_cast<const uint4*>(box + lane * 16);
+                                const uint4 r1 = *reinterpret_cast<const uint4*>(box + 512 + lane * 16);
+                                const uint32_t w0[4] = {r0.x, r0.y, r0.z, r0.w};
+                                const uint32_t w1[4] = {r1.x, r1.y, r1.z, r1.w};
+                                if constexpr (FMT == BQ_W_BF16) {
+#pragma unroll
+                                    for (int e2 = 0; e2 < 2; ++e2) {
+                                        const int ki = 2 * b + e2;
+#pragma unroll
+                                        for (int mt = 0; mt < MT; ++mt)
+                                            mma_bf16(c2[ki % NCH][mt], w0[2 * e2], w1[2 * e2], w0[2 * e2 + 1], w1[2 * e2 + 1],
+                                                     bfr[mt][2 * ki], bfr[mt][2 * ki + 1]);
+                                    }
+                                } else {
+#pragma unroll
+                                    for (int q = 0; q < 4; ++q) {
+                                        const int ki = 4 * b + q;
+                                        uint32_t a0, a1, a2, a3;
+                                        if constexpr (FMT == BQ_W_FP8_E4M3) {
+                                            a0 = e4m3x2_to_f16x2(uint16_t(w0[q] & 0xFFFF));
+                                            a2 = e4m3x2_to_f16x2(uint16_t(w0[q] >> 16));
+                                            a1 = e4m3x2_to_f16x2(uint16_t(w1[q] & 0xFFFF));
+                                            a3 = e4m3x2_to_f16x2(uint16_t(w1[q] >> 16));
+                                        } else {
+                                            const uint32_t x0 = w0[q] ^ 0x80808080u, x1 = w1[q] ^ 0x80808080u;
+                                            a0 = i8pair_to_f16x2(x0, 0x4140u);
+                                            a2 = i8pair_to_f16x2(x0, 0x4342u);
+                                            a1 = i8pair_to_f16x2(x1, 0x4140u);
+                                            a3 = i8pair_to_f16x2(x1, 0x4342u);
+                                        }
+#pragma unroll
+                                        for (int mt = 0; mt < MT; ++mt)
+                                            mma_f16(c2[ki % NCH][mt], a0, a1, a2, a3, bfr[mt][2 * ki], bfr[mt][2 * ki + 1]);
+                                    }
+                                }
+                            }
+#pragma unroll
+                            for (int h = 0; h < NCH; ++h)
+#pragma unroll
+                                for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                                    for (int d = 0; d < 4; ++d) acc[i][tile][mt][d] += c2[h][mt][d];
+                        }
+                    }
+                }
+            }
+            __syncwarp();  // every lane is done reading the slot: refill it
+            ++consumed;
+            if (ig < ngroups) {
+                issue(slot, ig, ij);
+                ++issued;
+                if (ij + 1 < nkw) {
+                    ++ij;
+                } else {
+                    ij = 0;
+                    ++ig;
+                }
+                normalize(ig, ij);
+            }
+            if (++slot == RS) slot = 0;
+        }
+        // this group's partials, back to true scale (zeros for units this warp never saw)
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+            const int m0 = 8 * mt + 2 * tq;
+            const float u0 = m0 < M ? s_up[warp * 16 + m0] : 0.f;
+            const float u1 = m0 + 1 < M ? s_up[warp * 16 + m0 + 1] : 0.f;
+#pragma unroll
+            for (int i = 0; i < UGM; ++i) {
+                const int ul = g * UG + i;
+                if (!(i < UG && ul < nu)) continue;
+#pragma unroll
+                for (int tile = 0; tile < TPU; ++tile) {
+                    float4 v = make_float4(acc[i][tile][mt][0] * u0, acc[i][tile][mt][1] * u1,
+                                           acc[i][tile][mt][2] * u0, acc[i][tile][mt][3] * u1);
+                    *reinterpret_cast<float4*>(part + ((((ul * 8 + warp) * TPU + tile) * MT + mt) * 32 + lane) * 4) = v;
+                }
+            }
+        }
+    }
+    __syncthreads();
+
+    // ---- reduce over warps, norm factor, epilogue. Task = (ul, mt).
+#pragma unroll 1
+    for (int task = warp; task < nu * MT; task += 8) {
+        const int ul = task / MT, mt = task - (task / MT) * MT;
+        const int unit = u_first + ul;
+        float v[TPU][4];
+#pragma unroll
+        for (int tile = 0; tile < TPU; ++tile) {
+            float4 q[8];
+#pragma unroll
+            for (int w = 0; w < 8; ++w)
+                q[w] = *reinterpret_cast<const float4*>(part + ((((ul * 8 + w) * TPU + tile) * MT + mt) * 32 + lane) * 4);
+            v[tile][0] = ((q[0].x + q[1].x) + (q[2].x + q[3].x)) + ((q[4].x + q[5].x) + (q[6].x + q[7].x));
+            v[tile][1] = ((q[0].y + q[1].y) + (q[2].y + q[3].y)) + ((q[4].y + q[5].y) + (q[6].y + q[7].y));
+            v[tile][2] = ((q[0].z + q[1].z) + (q[2].z + q[3].z)) + ((q[4].z + q[5].z) + (q[6].z + q[7].z));
+            v[tile][3] = ((q[0].w + q[1].w) + (q[2].w + q[3].w)) + ((q[4].w + q[5].w) + (q[6].w + q[7].w));
+        }
+        const int m0 = 8 * mt + 2 * tq;
+        const bool full = (ul > 0 || lo0 == 0) && (ul < nu - 1 || hi_last == KB - 1);
+        if (!full) {
+            // split mode: pieces = CTAs covering the unit, fixed summation order
+            const uint32_t c_first = uint32_t(unit) * KB, c_last = c_first + KB - 1;
+            const uint32_t T = uint32_t(p.total_chunks);
+            const int cta_f = int(((c_first + 1) * uint32_t(p.grid) - 1) / T);
+            const int cta_l = int(((c_last + 1) * uint32_t(p.grid) - 1) / T);
+            const int npieces = cta_l - cta_f + 1;
+            const int me = int(blockIdx.x) - cta_f;
+            float* base = p.partials + (int64_t(unit) * p.p_max) * (TPU * 2 * 128);
+            float* mine = base + int64_t(me) * (TPU * 2 * 128);
+#pragma unroll
+            for (int tile = 0; tile < TPU; ++tile)
+                __stcg(reinterpret_cast<float4*>(mine + ((tile * 2 + mt) * 32 + lane) * 4),
+                       make_float4(v[tile][0], v[tile][1], v[tile][2], v[tile][3]));
+            __threadfence();
+            __syncwarp();
+            unsigned int old = 0;
+            if (lane == 0) old = atomicAdd(p.counters + unit * 2 + mt, 1u);
+            old = __shfl_sync(0xffffffffu, old, 0);
+            if (old != unsigned(npieces - 1)) continue;
+            __threadfence();
+            float t[TPU][4];
+#pragma unroll
+            for (int tile = 0; tile < TPU; ++tile)
+#pragma unroll
+                for (int d = 0; d < 4; ++d) t[tile][d] = 0.f;
+            for (int q = 0; q < npieces; ++q) {
+#pragma unroll
+                for (int tile = 0; tile < TPU; ++tile) {
+                    float4 x4;
+                    if (q == me)
+                        x4 = make_float4(v[tile][0], v[tile][1], v[tile][2], v[tile][3]);
+                    else
+                        x4 = ldcg_f4(base + int64_t(q) * (TPU * 2 * 128) + ((tile * 2 + mt) * 32 + lane) * 4);
+                    t[tile][0] += x4.x;
+                    t[tile][1] += x4.y;
+                    t[tile][2] += x4.z;
+                    t[tile][3] += x4.w;
+                }
+            }
+            if (lane == 0) atomicExch(p.counters + unit * 2 + mt, 0u);
+#pragma unroll
+            for (int tile = 0; tile < TPU; ++tile)
+#pragma unroll
+                for (int d = 0; d < 4; ++d) v[tile][d] = t[tile][d];
+        }
+        float inv0 = 1.f, inv1 = 1.f;
+        if (norm) {
+            // lanes 0-15: row sums of squares over the 8 warps, then 1/rms per row
+            float a = 0.f;
+            if (lane < M) {
+#pragma unroll
+                for (int w = 0; w < 8; ++w) a += s_ss[w * 16 + lane];
+            }
+            const float invl = rsqrtf(a / float(p.K) + p.eps);
+            inv0 = __shfl_sync(0xffffffffu, invl, m0 & 31);
+            inv1 = __shfl_sync(0xffffffffu, invl, (m0 + 1) & 31);
+        }
+#pragma unroll
+        for (int tile = 0; tile < TPU; ++tile)
+#pragma unroll
+            for (int d = 0; d < 4; ++d) {
+                const int rr = tile * 16 + tg + (d >> 1) * 8;
+                v[tile][d] = v[tile][d] * ((d & 1) ? inv1 : inv0) * s_rscale[ul * 32 + rr] + s_rbias[ul * 32 + rr];
+            }
+        if (p.epi == BQ_EPI_SILU_MUL) {
+#pragma unroll
+            for (int d = 0; d < 4; ++d) {
+                const int n = 16 * unit + tg + (d >> 1) * 8;
+                const int m = m0 + (d & 1);
+                if (n < p.n_half && m < M)
+                    store_act(p.out, m * p.ldo + n, p.out_dtype, silu(v[0][d]) * v[TPU - 1][d]);
+            }
+        } else {
+#pragma unroll
+            for (int tile = 0; tile < TPU; ++tile)
+#pragma unroll
+                for (int d = 0; d < 4; ++d) {
+                    const int rr = tile * 16 + tg + (d >> 1) * 8;
+                    const int n = tile_row(unit, tile) + tg + (d >> 1) * 8;
+                    const int m = m0 + (d & 1);
+                    if (n < p.N && m < M) {
+                        float o = v[tile][d];
+                        if (p.epi == BQ_EPI_ADD_RESIDUAL) o += s_res[(ul * 32 + rr) * 16 + m];
+                        store_act(p.out, m * p.ldo + n, p.out_dtype, o);
+                    }
+                }
+        }
+    }
+}
+
+}  // namespace bq

@@ -1,0 +1,223 @@
+// Host planning and launch of the v3 GEMV kernel (bq_gemv3.cuh).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+
+#include "bq_gemv3.cuh"
+#include "bq_gemv3_kinst.h"
+#include "bq_host.h"
+
+namespace bq {
+
+namespace {
+constexpr uint32_t kTargetSmem = 110 * 1024;  // leaves room for a co-resident dependent CTA
+constexpr int64_t kXBudget = 136 * 1024;       // staged activations per CTA
+inline uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
+int boxes(int fmt) { return fmt == BQ_W_BF16 ? 4 : (fmt == BQ_W_FP8_E4M3 || fmt == BQ_W_INT8) ? 2 : 1; }
+bool int4fmt(int fmt) { return fmt == BQ_W_INT4_TINYGEMM || fmt == BQ_W_INT4_PLAIN; }
+int gpk_of(const bq_gemv_desc* d) { return (d->wfmt == BQ_W_INT4_TINYGEMM && d->group < 128) ? 128 / d->group : 1; }
+int tile_bytes(int fmt, int gpk) { return boxes(fmt) * kBoxBytes + (int4fmt(fmt) ? int(align_up(64 * gpk, 128)) : 0); }
+}  // namespace
+
+int gemv3_rows_per_launch(const bq_gemv_desc* d) {
+    const DeviceInfo* dev = device_info();
+    const int optin = dev ? dev->smem_optin : 232448;
+    const int KB = d->K / kKB;
+    const int nkbw = (KB + 7) / 8;
+    const int64_t pitch = nkbw * 256 + 16;
+    // smallest ring that still double-buffers: two slots of one two-tile unit per warp
+    const int64_t ring = 8 * 2 * 2 * int64_t(tile_bytes(d->wfmt, gpk_of(d)));
+    const int64_t extra = 8 * nkbw * 256 + 4 * 8 * 2 * 2 * 512;  // gamma, partials
+    const int64_t budget = std::min<int64_t>(kXBudget, optin - ring - kMisc3Bytes - extra - 2048);
+    const int r = int(budget / (8 * pitch)) - 1;  // one zero row per warp
+    return std::max(1, std::min(16, r));
+}
+
+int plan_gemv3(const bq_gemv_desc* d, int rows, Gemv3Plan* pl) {
+    const DeviceInfo* dev = device_info();
+    if (!dev) return BQ_ERR_CUDA;
+    const int fmt = d->wfmt;
+    const int SMs = dev->sm_count;
+    const int KB = d->K / kKB;
+    Gemv3Plan P;
+    std::memset(&P, 0, sizeof(P));
+    P.rows = rows;
+    P.mt = rows > 8 ? 2 : 1;
+    P.nkbw = (KB + 7) / 8;
+    P.xrow_pitch = P.nkbw * 256 + 16;
+    P.gpk = gpk_of(d);
+
+    int64_t U;
+    if (d->epilogue == BQ_EPI_SILU_MUL) {
+        P.tpu = 2;
+        U = (d->N / 2 + 15) / 16;
+    } else {
+        const int64_t u32 = (d->N + 31) / 32, u16 = (d->N + 15) / 16;
+        auto rows_per_cta = [&](int64_t u, int r) {
+            const int64_t g = std::min<int64_t>(SMs, u);
+            return ((u + g - 1) / g) * r;
+        };
+        P.tpu = rows_per_cta(u16, 16) < rows_per_cta(u32, 32) ? 1 : 2;
+        U = P.tpu == 1 ? u16 : u32;
+    }
+    if (2 * U > kMaxUnits) return set_error(BQ_ERR_SHAPE, "N=%d too large for one launch", d->N);
+    P.n_units = int(U);
+    const int64_t T = U * KB;
+    P.total_chunks = T;
+    if ((T + 1) * int64_t(std::max(SMs, int((U + 3) / 4))) >= (int64_t(1) << 32))
+        return set_error(BQ_ERR_SHAPE, "GEMV too large for one launch (N=%d, K=%d)", d->N, d->K);
+    int upc_need;
+    if (U >= SMs / 2) {
+        P.owned = 1;
+        int64_t G = std::min<int64_t>(SMs, U);
+        if ((U + G - 1) / G > 4) G = (U + 3) / 4;
+        P.grid = int(G);
+        upc_need = int((U + G - 1) / G);
+    } else {
+        P.owned = 0;
+        const int64_t G = std::min<int64_t>(SMs, T);
+        P.grid = int(G);
+        const int64_t per = (T + G - 1) / G;
+        upc_need = int(std::min<int64_t>(U, (per - 1 + KB - 1) / KB + 1));
+        const int64_t cmin = T / G;
+        P.p_max = int(std::min<int64_t>(G, (KB - 1 + cmin - 1) / cmin + 1));
+    }
+    if (upc_need > 4) return set_error(BQ_ERR_SHAPE, "internal: %d units per CTA", upc_need);
+    P.upc = upc_need;
+    const int ugm = (P.mt * P.tpu >= 4) ? 2 : 4;
+    const uint32_t x_bytes = uint32_t(8 * (rows + 1) * P.xrow_pitch);  // + one zero row per warp
+    const uint32_t gamma_bytes = uint32_t(8 * P.nkbw * 256);
+    const uint32_t part_bytes = uint32_t(P.upc * 8 * P.tpu * P.mt * 512);
+    auto layout = [&](int ug, int rs) {
+        const uint32_t slot = uint32_t(ug * P.tpu * tile_bytes(fmt, P.gpk));
+        uint32_t o = 0;
+        P.smem_ring = o;
+        o += 8 * rs * slot;
+        o = align_up(o, 16);
+        P.smem_x = o;
+        o += x_bytes;
+        o = align_up(o, 16);
+        P.smem_gamma = o;
+        o += gamma_bytes;
+        o = align_up(o, 16);
+        P.smem_part = o;
+        o += part_bytes;
+        o = align_up(o, 16);
+        P.smem_misc = o;
+        o += kMisc3Bytes;
+        return o;
+    };
+    // Largest unit group that still double-buffers within the co-residency
+    // target; the deepest ring for it. Else one unit per slot, as deep as
+    // the device allows.
+    int ug = 0, rs = 0;
+    for (int u = std::min(ugm, P.upc); u >= 1 && !ug; --u) {
+        const int max_seq = std::min(kMaxRing, ((P.upc + u - 1) / u) * P.nkbw);
+        const int need = std::min(2, max_seq);
+        if (layout(u, need) > kTargetSmem) continue;
+        ug = u;
+        rs = need;
+        while (rs < max_seq && layout(u, rs + 1) <= kTargetSmem) ++rs;
+    }
+    if (!ug) {
+        ug = 1;
+        const int max_seq = std::min(kMaxRing, P.upc * P.nkbw);
+        rs = std::min(2, max_seq);
+        while (rs > 1 && layout(1, rs) > uint32_t(dev->smem_optin)) --rs;
+    }
+    const uint32_t total = layout(ug, rs);
+    if (total > uint32_t(dev->smem_optin))
+        return set_error(BQ_ERR_SHAPE, "GEMV does not fit in shared memory (K=%d, rows=%d)", d->K, rows);
+    P.ug = ug;
+    P.slot_bytes = ug * P.tpu * tile_bytes(fmt, P.gpk);
+    P.ring_slots = rs;
+    P.smem_total = total;
+    P.ws_bytes = P.owned ? 0 : kCounterBytes + int64_t(U) * P.p_max * P.tpu * 2 * 128 * 4;
+    *pl = P;
+    return BQ_OK;
+}
+
+int launch_gemv3(const bq_gemv_desc* d, const Gemv3Plan& pl, int row0, void* workspace, cudaStream_t stream) {
+    const int fmt = d->wfmt;
+    const void* fn = nullptr;
+    if (int4fmt(fmt))
+        fn = gemv3_kernel_int4(fmt, pl.mt, pl.tpu, pl.gpk);
+    else if (fmt == BQ_W_BF16)
+        fn = gemv3_kernel_bf16(pl.mt, pl.tpu);
+    else
+        fn = gemv3_kernel_f8(fmt, pl.mt, pl.tpu);
+    if (!fn) return set_error(BQ_ERR_FORMAT, "no GEMV kernel for format %d (group %d)", fmt, d->group);
+
+    Gemv3Params p;
+    std::memset(&p, 0, sizeof(p));
+    p.M = pl.rows;
+    p.N = d->N;
+    p.K = d->K;
+    p.KB = d->K / kKB;
+    p.epi = d->epilogue;
+    p.group = d->group;
+    p.x_dtype = d->x_dtype;
+    p.out_dtype = d->out_dtype;
+    p.res_dtype = d->res_dtype;
+    p.flags = d->flags;
+    p.eps = d->eps;
+    p.n_half = d->N / 2;
+    p.tpu = pl.tpu;
+    p.n_units = pl.n_units;
+    p.owned = pl.owned;
+    p.grid = pl.grid;
+    p.total_chunks = pl.total_chunks;
+    p.ug = pl.ug;
+    p.ring_slots = pl.ring_slots;
+    p.slot_bytes = pl.slot_bytes;
+    p.nkbw = pl.nkbw;
+    p.p_max = pl.p_max;
+    p.xrow_pitch = pl.xrow_pitch;
+    p.upc = pl.upc;
+    p.smem_ring = pl.smem_ring;
+    p.smem_x = pl.smem_x;
+    p.smem_gamma = pl.smem_gamma;
+    p.smem_part = pl.smem_part;
+    p.smem_misc = pl.smem_misc;
+    p.group_shift = 0;
+    while ((1 << p.group_shift) < d->group) ++p.group_shift;
+    const int xs = dtype_size(d->x_dtype), os = dtype_size(d->out_dtype), rsz = dtype_size(d->res_dtype);
+    p.x = static_cast<const char*>(d->x) + int64_t(row0) * d->ldx * xs;
+    p.x_bulk = (d->x_dtype == BQ_DT_BF16 && (reinterpret_cast<uintptr_t>(p.x) & 15) == 0 && (d->ldx % 8) == 0) ? 1 : 0;
+    p.ldx = d->ldx;
+    p.w = d->w;
+    p.gamma = d->gamma;
+    p.scale = d->scale;
+    p.bias = d->bias;
+    p.residual = d->residual ? static_cast<const char*>(d->residual) + int64_t(row0) * d->ldr * rsz : nullptr;
+    p.ldr = d->ldr;
+    p.out = static_cast<char*>(d->out) + int64_t(row0) * d->ldo * os;
+    p.ldo = d->ldo;
+    if (!pl.owned) {
+        p.counters = static_cast<unsigned int*>(workspace);
+        p.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes);
+    }
+    int rc = ensure_smem_attr(fn, pl.smem_total);
+    if (rc) return rc;
+
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(pl.grid);
+    cfg.blockDim = dim3(kThreads3);
+    cfg.dynamicSmemBytes = pl.smem_total;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    if (d->flags & BQ_FLAG_PDL) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    void* args[] = {&p};
+    cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
+    if (e != cudaSuccess) return set_error(BQ_ERR_CUDA, "GEMV launch failed: %s", cudaGetErrorString(e));
+    return BQ_OK;
+}
+
+}  // namespace bq

@@ -1,0 +1,23 @@
+// Instantiation helper for the v3 GEMV kernel: one dispatcher per format file
+// so the kernel variants compile in parallel.
+#pragma once
+#include "bq_gemv3.cuh"
+
+namespace bq {
+
+template <int FMT, int MT, int TPU, int GPK>
+inline const void* k3() {
+    return reinterpret_cast<const void*>(&gemv3_kernel<FMT, MT, TPU, GPK>);
+}
+
+template <int FMT, int GPK>
+inline const void* k3_select(int mt, int tpu) {
+    if (mt == 1) return tpu == 1 ? k3<FMT, 1, 1, GPK>() : k3<FMT, 1, 2, GPK>();
+    return tpu == 1 ? k3<FMT, 2, 1, GPK>() : k3<FMT, 2, 2, GPK>();
+}
+
+const void* gemv3_kernel_int4(int fmt, int mt, int tpu, int gpk);
+const void* gemv3_kernel_f8(int fmt, int mt, int tpu);
+const void* gemv3_kernel_bf16(int mt, int tpu);
+
+}  // namespace bq

@@ -51,6 +51,19 @@ int gemv2_rows_per_launch(const bq_gemv_desc* d);
 int plan_gemv2(const bq_gemv_desc* d, int rows, Gemv2Plan* pl);
 int launch_gemv2(const bq_gemv_desc* d, const Gemv2Plan& pl, int row0, void* workspace, cudaStream_t stream);
 
+struct Gemv3Plan {
+    int rows, mt, upc, tpu, gpk, ug;
+    int grid, owned, n_units, ring_slots, slot_bytes, nkbw, p_max, xrow_pitch;
+    int64_t total_chunks, ws_bytes;
+    uint32_t smem_ring, smem_x, smem_gamma, smem_part, smem_misc, smem_total;
+};
+
+// GEMV (per-warp cp.async weight rings, unit-group slots): rows per launch,
+// plan, launch.
+int gemv3_rows_per_launch(const bq_gemv_desc* d);
+int plan_gemv3(const bq_gemv_desc* d, int rows, Gemv3Plan* pl);
+int launch_gemv3(const bq_gemv_desc* d, const Gemv3Plan& pl, int row0, void* workspace, cudaStream_t stream);
+
 int plan_gemv(const bq_gemv_desc* d, int rows, GemvPlan* pl);
 int launch_gemv(const bq_gemv_desc* d, const GemvPlan& pl, int row0, int rows, void* workspace,
                 cudaStream_t stream);
