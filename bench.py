@@ -266,40 +266,48 @@ def decode_step_bench(device, world: int, local_rank: int, replays: int = 10, wa
     for fmt in DECODE_FORMATS:
         layers, head, ln_f = synthetic_stack(fmt, DECODE_LAYERS, device, seed=7)
         for rows in DECODE_ROWS:
-            st = DecodeStack(layers, head, ln_f, rows=rows)
-            st.x.copy_(torch.randn(rows, st.hidden, device=device, generator=torch.Generator(device=device)
-                                   .manual_seed(rows)).to(torch.bfloat16))
-            st.capture()
-            for _ in range(warmup):
-                st.replay()
-            torch.cuda.synchronize(device)
-            if world > 1:
-                import torch.distributed as dist
+            entry = {"format": fmt, "rows": rows}
+            for mode in ("per_op", "chain"):
+                try:
+                    st = DecodeStack(layers, head, ln_f, rows=rows, chain=(mode == "chain"))
+                except (RuntimeError, ValueError) as e:  # chain limits (rows per pass) are reported, not hidden
+                    entry[mode] = {"unavailable": str(e)[:160]}
+                    continue
+                st.x.copy_(torch.randn(rows, st.hidden, device=device, generator=torch.Generator(device=device)
+                                       .manual_seed(rows)).to(torch.bfloat16))
+                st.capture()
+                for _ in range(warmup):
+                    st.replay()
+                torch.cuda.synchronize(device)
+                if world > 1:
+                    import torch.distributed as dist
 
-                dist.barrier(device_ids=[local_rank])
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(cur)
-            for _ in range(replays):
-                st.replay()
-            e1.record(cur)
-            torch.cuda.synchronize(device)
-            t = torch.tensor([e0.elapsed_time(e1) / replays], device=device, dtype=torch.float64)
-            if world > 1:
-                import torch.distributed as dist
+                    dist.barrier(device_ids=[local_rank])
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(cur)
+                for _ in range(replays):
+                    st.replay()
+                e1.record(cur)
+                torch.cuda.synchronize(device)
+                t = torch.tensor([e0.elapsed_time(e1) / replays], device=device, dtype=torch.float64)
+                if world > 1:
+                    import torch.distributed as dist
 
-                dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            step_us = float(t.item()) * 1e3
-            wb = st.weight_bytes
-            results.append({"format": fmt, "rows": rows, "step_us": round(step_us, 1),
-                            "us_per_row": round(step_us / rows, 2),
-                            "GBps": round(wb / step_us / 1e3, 1), "weight_bytes": wb,
-                            "finite": bool(torch.isfinite(st.logits).all().item())})
-            del st
+                    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                step_us = float(t.item()) * 1e3
+                wb = st.weight_bytes
+                entry[mode] = {"step_us": round(step_us, 1), "us_per_row": round(step_us / rows, 2),
+                               "GBps": round(wb / step_us / 1e3, 1), "launches": st.launches,
+                               "finite": bool(torch.isfinite(st.logits).all().item())}
+                entry["weight_bytes"] = wb
+                del st
+            results.append(entry)
         del layers, head, ln_f
         torch.cuda.empty_cache()
     return {"what": f"{DECODE_LAYERS} layers x (QKV 2048->6144 +RMSNorm, O 2048->2048 +residual, "
                     "gate+up 2048->16384 +RMSNorm +SiLU*up, down 8192->2048 +residual) + head 2048->8192 "
-                    "+RMSNorm (fp32 logits); one CUDA graph of 113 bq_gemv launches with PDL",
+                    "+RMSNorm (fp32 logits); per_op = one CUDA graph of 113 bq_gemv launches with PDL, chain = "
+                    "one cooperative bq_gemv_chain launch",
             "launches_per_step": 4 * DECODE_LAYERS + 1, "replays_timed": replays,
             "l2_policy": "weights 1-1.9 GB per step >> L2", "results": results}
 

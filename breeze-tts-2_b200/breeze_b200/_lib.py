@@ -57,6 +57,12 @@ _SIGS = {
     "bq_gemv_workspace_bytes": (ctypes.c_int32, [ctypes.POINTER(GemvDesc), ctypes.POINTER(ctypes.c_size_t)]),
     "bq_gemv": (ctypes.c_int32, [ctypes.POINTER(GemvDesc), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     "bq_gemv_noalloc": (ctypes.c_int32, [ctypes.POINTER(GemvDesc), ctypes.c_void_p]),
+    "bq_gemv_chain_workspace_bytes": (ctypes.c_int32, [ctypes.POINTER(GemvDesc), ctypes.c_int32,
+                                                       ctypes.POINTER(ctypes.c_size_t)]),
+    "bq_gemv_chain_prepare": (ctypes.c_int32, [ctypes.POINTER(GemvDesc), ctypes.c_int32, ctypes.c_void_p,
+                                               ctypes.c_size_t]),
+    "bq_gemv_chain_launch": (ctypes.c_int32, [ctypes.POINTER(GemvDesc), ctypes.c_int32, ctypes.c_void_p,
+                                              ctypes.c_size_t, ctypes.c_void_p]),
     "bq_int4_tinygemm_pack": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
                                                ctypes.c_int32, ctypes.c_void_p]),
     "bq_int4_tinygemm_unpack": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
@@ -234,6 +240,44 @@ def gemv(x: torch.Tensor, w: torch.Tensor, wfmt: int, n: int, *, scale=None, gro
     ws = WORKSPACE.get(dev, need.value)
     check(lib.bq_gemv(ctypes.byref(d), ws.data_ptr(), ws.numel(), _stream(dev)), "bq_gemv")
     return out
+
+
+def gemv_desc(x: torch.Tensor, w: torch.Tensor, wfmt: int, n: int, *, out: torch.Tensor, scale=None,
+              group: int = 128, gamma=None, eps: float = 1e-6, epilogue: int = EPI_NONE, residual=None,
+              bias=None, flags: int = 0) -> GemvDesc:
+    """Descriptor of one GEMV over existing device tensors (for chains)."""
+    _require_cuda(x, w, scale, gamma, residual, bias, out)
+    _rowmajor(x, "x")
+    _rowmajor(out, "out")
+    if residual is not None:
+        _rowmajor(residual, "residual")
+    if gamma is not None and gamma.dtype != torch.bfloat16:
+        raise ValueError("chain descriptors need a bf16 gamma")
+    return make_desc(x, w, wfmt, n, scale=scale, group=group, gamma=gamma, eps=eps, epilogue=epilogue,
+                     residual=residual, bias=bias, out=out, flags=flags)
+
+
+class GemvChain:
+    """A list of GEMVs run as one cooperative launch (bq_gemv_chain_*).
+
+    The descriptors' tensors must stay alive and in place; ``launch()`` is
+    capture-safe once the chain is built (``prepare`` runs here, outside any
+    capture).
+    """
+
+    def __init__(self, descs: list[GemvDesc], device: torch.device):
+        lib = load()
+        self.n = len(descs)
+        self._arr = (GemvDesc * self.n)(*descs)
+        need = ctypes.c_size_t(0)
+        check(lib.bq_gemv_chain_workspace_bytes(self._arr, self.n, ctypes.byref(need)), "bq_gemv_chain_workspace_bytes")
+        self.ws = torch.zeros(max(int(need.value), 256), dtype=torch.uint8, device=device)
+        check(lib.bq_gemv_chain_prepare(self._arr, self.n, self.ws.data_ptr(), self.ws.numel()), "bq_gemv_chain_prepare")
+        self.device = device
+
+    def launch(self) -> None:
+        check(load().bq_gemv_chain_launch(self._arr, self.n, self.ws.data_ptr(), self.ws.numel(), _stream(self.device)),
+              "bq_gemv_chain_launch")
 
 
 def dequant(w: torch.Tensor, wfmt: int, n: int, k: int, *, scale=None, group: int = 128) -> torch.Tensor:

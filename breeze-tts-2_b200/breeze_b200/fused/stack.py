@@ -143,7 +143,7 @@ class DecodeStack:
     """
 
     def __init__(self, layers: list[DecodeLayer], head: QWeight, ln_f: torch.Tensor, rows: int,
-                 eps: float = 1e-6, attn_cols: int | None = None):
+                 eps: float = 1e-6, attn_cols: int | None = None, chain: bool = False):
         if not layers:
             raise ValueError("DecodeStack needs at least one layer")
         dev = layers[0].wqkv.w.device
@@ -168,6 +168,12 @@ class DecodeStack:
         self.res = [torch.zeros(rows, hidden, **bf), torch.zeros(rows, hidden, **bf)]
         self.logits = torch.zeros(rows, head.N, device=dev, dtype=torch.float32)
         self.graph = None
+        self.chain = None
+        if chain:
+            descs = [_lib.gemv_desc(x, qw.w, qw.wfmt, qw.N, out=out, scale=qw.scale, group=qw.group, gamma=g,
+                                    eps=eps, epilogue=epi, residual=res, flags=_lib.default_flags())
+                     for x, qw, out, g, epi, res in self._ops()]
+            self.chain = _lib.GemvChain(descs, dev)
 
     @property
     def weight_bytes(self) -> int:
@@ -178,24 +184,33 @@ class DecodeStack:
 
     @property
     def launches(self) -> int:
-        return 4 * len(self.layers) + 1
+        return 1 if self.chain is not None else 4 * len(self.layers) + 1
 
-    def _gemv(self, x, qw: QWeight, out, gamma=None, epilogue=_lib.EPI_NONE, residual=None):
-        _lib.gemv(x, qw.w, qw.wfmt, qw.N, scale=qw.scale, group=qw.group, gamma=gamma, eps=self.eps,
-                  epilogue=epilogue, residual=residual, out=out, flags=_lib.default_flags())
-
-    def run(self) -> torch.Tensor:
+    def _ops(self):
+        """(x, weight, out, gamma, epilogue, residual) of every launch, in order."""
+        ops = []
         x = self.x
         for i, l in enumerate(self.layers):
             qkv = self.qkv[:, : l.wqkv.N]
-            self._gemv(x, l.wqkv, qkv, gamma=l.ln1)
-            self._gemv(qkv[:, : self.attn_cols], l.wo, self.h, epilogue=_lib.EPI_ADD_RESIDUAL, residual=x)
+            ops.append((x, l.wqkv, qkv, l.ln1, _lib.EPI_NONE, None))
+            ops.append((qkv[:, : self.attn_cols], l.wo, self.h, None, _lib.EPI_ADD_RESIDUAL, x))
             act = self.act[:, : l.wd.K]
-            self._gemv(self.h, l.wgu, act, gamma=l.ln2, epilogue=_lib.EPI_SILU_MUL)
+            ops.append((self.h, l.wgu, act, l.ln2, _lib.EPI_SILU_MUL, None))
             y = self.res[i % 2]
-            self._gemv(act, l.wd, y, epilogue=_lib.EPI_ADD_RESIDUAL, residual=self.h)
+            ops.append((act, l.wd, y, None, _lib.EPI_ADD_RESIDUAL, self.h))
             x = y
-        self._gemv(x, self.head, self.logits, gamma=self.ln_f)
+        ops.append((x, self.head, self.logits, self.ln_f, _lib.EPI_NONE, None))
+        return ops
+
+    def run(self) -> torch.Tensor:
+        """Enqueue the step: one bq_gemv launch per projection, or the whole
+        step as one decode-chain launch (``chain=True``)."""
+        if self.chain is not None:
+            self.chain.launch()
+            return self.logits
+        for x, qw, out, gamma, epi, res in self._ops():
+            _lib.gemv(x, qw.w, qw.wfmt, qw.N, scale=qw.scale, group=qw.group, gamma=gamma, eps=self.eps,
+                      epilogue=epi, residual=res, out=out, flags=_lib.default_flags())
         return self.logits
 
     def capture(self) -> None:

@@ -66,7 +66,11 @@ int ensure_smem_attr(const void* fn, uint32_t bytes) {
     }
     const DeviceInfo* di = device_info();
     if (!di) return BQ_ERR_CUDA;
-    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, di->smem_optin);
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, fn);
+    if (e != cudaSuccess) return set_error(BQ_ERR_CUDA, "cudaFuncGetAttributes: %s", cudaGetErrorString(e));
+    // static shared memory counts against the same opt-in limit
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, di->smem_optin - int(fa.sharedSizeBytes));
     if (e != cudaSuccess) return set_error(BQ_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     (void)bytes;
     std::lock_guard<std::mutex> lk(g_mu);

@@ -68,9 +68,10 @@ struct Gemv3Params {
     float* partials;
 };
 
-// Misc area (floats): ss[8][16], up[8][16], rowscale[4*32], rowbias[4*32],
-// res[4*32][16], then 8 warps x 16 zero bytes.
-constexpr int kMisc3Bytes = (8 * 16 + 8 * 16 + 128 + 128 + 128 * 16) * 4 + 8 * 16;
+// Misc area: floats ss[8][16], up[8][16], rowscale[4*32], rowbias[4*32],
+// then 8 warps x 16 zero bytes, then the residual rows res[upc*32][M].
+constexpr int kMiscFixedBytes = (8 * 16 + 8 * 16 + 128 + 128) * 4 + 8 * 16;
+constexpr int misc3_bytes(int upc, int rows) { return kMiscFixedBytes + upc * 32 * rows * 4; }
 constexpr int kConsumerThreads = 256;
 constexpr int kThreads3 = 256;
 constexpr int kMaxRing = 6;  // cp.async groups a warp keeps in flight
@@ -138,12 +139,25 @@ __device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, 
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(ok ? 16 : 0) : "memory");
 }
 
+// Phases of one CTA's share of a GEMV. A single launch runs them all in order;
+// the decode-chain kernel interleaves the phases of consecutive GEMVs.
+constexpr int kPhL2 = 1;       // bulk L2 prefetch of the CTA's weight slice
+constexpr int kPhPrefill = 2;  // gamma and the first ring slots (static data only)
+constexpr int kPhPdl = 4;      // programmatic-dependent-launch trigger and wait
+constexpr int kPhRun = 8;      // activations, staging, main loop, partials (ends in a block barrier)
+constexpr int kPhEpi = 16;     // cross-warp reduction, norm factor, epilogue, stores
+constexpr int kPhAll = 31;
+
+struct RingState {
+    int issued, ig, ij;  // ring slots issued so far; next (group, k-slot) to issue
+};
+
 template <int FMT, int MT, int TPU, int GPK>
-__global__ void __launch_bounds__(kThreads3, 2) gemv3_kernel(const Gemv3Params p) {
+__device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, const int cta, const int phases,
+                                         RingState& rst) {
     using F = Fmt3<FMT>;
     constexpr int UGM = ug_max<MT, TPU>();
     constexpr int NCH = MT == 1 ? 4 : 2;  // independent MMA chains per tile
-    extern __shared__ __align__(1024) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int KB = p.KB, M = p.M;
     const uint32_t sbase = smem_u32(smem);
@@ -156,12 +170,12 @@ __global__ void __launch_bounds__(kThreads3, 2) gemv3_kernel(const Gemv3Params p
     // ---- this CTA's chunk range (32-bit: the host keeps grid * chunks < 2^32)
     uint32_t cb, ce;
     if (p.owned) {
-        cb = (blockIdx.x * uint32_t(p.n_units) / uint32_t(p.grid)) * uint32_t(KB);
-        ce = ((blockIdx.x + 1) * uint32_t(p.n_units) / uint32_t(p.grid)) * uint32_t(KB);
+        cb = (uint32_t(cta) * uint32_t(p.n_units) / uint32_t(p.grid)) * uint32_t(KB);
+        ce = ((uint32_t(cta) + 1) * uint32_t(p.n_units) / uint32_t(p.grid)) * uint32_t(KB);
     } else {
         const uint32_t T = uint32_t(p.total_chunks);
-        cb = blockIdx.x * T / uint32_t(p.grid);
-        ce = (blockIdx.x + 1) * T / uint32_t(p.grid);
+        cb = uint32_t(cta) * T / uint32_t(p.grid);
+        ce = (uint32_t(cta) + 1) * T / uint32_t(p.grid);
     }
     const int u_first = int(cb / uint32_t(KB));
     const int u_last = int((ce - 1) / uint32_t(KB));
@@ -197,7 +211,7 @@ __global__ void __launch_bounds__(kThreads3, 2) gemv3_kernel(const Gemv3Params p
     };
 
     const int pitch = p.xrow_pitch;
-    const uint32_t xs0 = sbase + p.smem_x;                        // [8][M + 1][pitch]
+    const uint32_t xs0 = sbase + p.smem_x;                        // [8][M * pitch + 256]
     const uint32_t gs0 = sbase + p.smem_gamma;                    // [8][nkbw][256]
     const uint32_t ring_w = sbase + p.smem_ring + warp * RS * p.slot_bytes;  // [RS][slot_bytes]
 
@@ -252,7 +266,7 @@ __global__ void __launch_bounds__(kThreads3, 2) gemv3_kernel(const Gemv3Params p
 
     // ---- pull this CTA's whole weight slice into L2 before anything else:
     // the rings then refill from L2, not HBM, after the dependent-launch wait
-    {
+    if (phases & kPhL2) {
         const int64_t row_bytes = (FMT == BQ_W_INT4_PLAIN || FMT == BQ_W_INT4_TINYGEMM)
                                       ? p.K / 2
                                       : (FMT == BQ_W_BF16 ? int64_t(p.K) * 2 : p.K);
@@ -296,14 +310,49 @@ __global__ void __launch_bounds__(kThreads3, 2) gemv3_kernel(const Gemv3Params p
     float* s_up = misc + 128;      // [8][16]
     float* s_rscale = misc + 256;  // [128]
     float* s_rbias = misc + 384;   // [128]
-    float* s_res = misc + 512;     // [128][16]
-    const uint32_t zero_blk = sbase + p.smem_misc + (512 + 128 * 16) * 4 + warp * 16;
-    if (lane < 4) reinterpret_cast<uint32_t*>(smem + p.smem_misc + (512 + 128 * 16) * 4 + warp * 16)[lane] = 0u;
-    uint8_t* xw_ptr = smem + p.smem_x + warp * (M + 1) * pitch;
-    const uint32_t xw = xs0 + warp * (M + 1) * pitch;
-    const uint8_t* xzero = xw_ptr + M * pitch;  // zero row: B fragments of rows >= M
-    for (int b = lane * 16; b < pitch; b += 32 * 16)
-        *reinterpret_cast<uint4*>(const_cast<uint8_t*>(xzero) + b) = make_uint4(0u, 0u, 0u, 0u);
+    float* s_res = misc + 512 + 32;  // [nu*32][M], after the zero blocks
+    const uint32_t zero_blk = sbase + p.smem_misc + 512 * 4 + warp * 16;
+    float* part = reinterpret_cast<float*>(smem + p.smem_part);  // [upc][8 warps][TPU][MT][32][4]
+    // per warp: M staged rows, then one zero k-block read by the B fragments of rows >= M
+    uint8_t* xw_ptr = smem + p.smem_x + warp * (M * pitch + 256);
+    const uint32_t xw = xs0 + warp * (M * pitch + 256);
+    const uint8_t* xzero = xw_ptr + M * pitch;
+
+    if (phases & kPhPrefill) {
+        // gamma (the oldest cp.async group), then the first ring slots: all
+        // static, so issued before the inputs are known to be ready
+        if (norm) {
+            const __nv_bfloat16* gam = static_cast<const __nv_bfloat16*>(p.gamma);
+            for (int s = lane; s < nkw * 16; s += 32)
+                cp_async16(gs0 + (warp * p.nkbw + (s >> 4)) * 256 + (s & 15) * 16,
+                           gam + (kw0 + (s >> 4)) * 128 + (s & 15) * 8);
+        }
+        cp_async_commit();
+        rst.ig = 0;
+        rst.ij = 0;
+        rst.issued = 0;
+        normalize(rst.ig, rst.ij);
+        for (; rst.issued < RS && rst.ig < ngroups; ++rst.issued) {
+            issue(rst.issued, rst.ig, rst.ij);
+            if (rst.ij + 1 < nkw) {
+                ++rst.ij;
+            } else {
+                rst.ij = 0;
+                ++rst.ig;
+            }
+            normalize(rst.ig, rst.ij);
+        }
+    }
+
+    if (phases & kPhPdl) {
+        pdl_launch_dependents();
+        pdl_wait();
+    }
+
+    if (phases & kPhRun) {
+    int issued = rst.issued, ig = rst.ig, ij = rst.ij;
+    if (lane < 4) reinterpret_cast<uint32_t*>(smem + p.smem_misc + 512 * 4 + warp * 16)[lane] = 0u;
+    if (lane < 16) reinterpret_cast<uint4*>(const_cast<uint8_t*>(xzero))[lane] = make_uint4(0u, 0u, 0u, 0u);
     for (int r = threadIdx.x; r < nu * 32; r += kConsumerThreads) {
         const int ul = r >> 5, rr = r & 31, tile = rr >> 4;
         float sc = 1.f, bi = 0.f;
@@ -322,35 +371,11 @@ __global__ void __launch_bounds__(kThreads3, 2) gemv3_kernel(const Gemv3Params p
         s_rbias[r] = bi;
     }
 
-    // gamma (the oldest cp.async group), then the first ring slots: all
-    // static, so issued before the programmatic-dependent-launch wait
-    if (norm) {
-        const __nv_bfloat16* gam = static_cast<const __nv_bfloat16*>(p.gamma);
-        for (int s = lane; s < nkw * 16; s += 32)
-            cp_async16(gs0 + (warp * p.nkbw + (s >> 4)) * 256 + (s & 15) * 16, gam + (kw0 + (s >> 4)) * 128 + (s & 15) * 8);
-    }
-    cp_async_commit();
-    int ig = 0, ij = 0, issued = 0;
-    normalize(ig, ij);
-    for (; issued < RS && ig < ngroups; ++issued) {
-        issue(issued, ig, ij);
-        if (ij + 1 < nkw) {
-            ++ij;
-        } else {
-            ij = 0;
-            ++ig;
-        }
-        normalize(ig, ij);
-    }
-
-    pdl_launch_dependents();
-    pdl_wait();
-
     if (p.epi == BQ_EPI_ADD_RESIDUAL) {
         for (int r = threadIdx.x; r < nu * 32; r += kConsumerThreads) {
             const int ul = r >> 5, rr = r & 31, tile = rr >> 4;
             const int n = tile < TPU ? tile_row(u_first + ul, tile) + (rr & 15) : p.N;
-            for (int m = 0; m < M; ++m) s_res[r * 16 + m] = n < p.N ? load_act(p.residual, m * p.ldr + n, p.res_dtype) : 0.f;
+            for (int m = 0; m < M; ++m) s_res[r * M + m] = n < p.N ? load_act(p.residual, m * p.ldr + n, p.res_dtype) : 0.f;
         }
     }
 
@@ -514,7 +539,7 @@ __global__ void __launch_bounds__(kThreads3, 2) gemv3_kernel(const Gemv3Params p
                 }
             } else {
                 const int m = 8 * mt + tg;
-                const uint8_t* row = (m < M ? xw_ptr + m * pitch : xzero) + j * 256;
+                const uint8_t* row = m < M ? xw_ptr + m * pitch + j * 256 : xzero;
                 uint4 v[4];
                 if constexpr (FMT == BQ_W_FP8_E4M3 || FMT == BQ_W_INT8) {
                     v[0] = *reinterpret_cast<const uint4*>(row + (16 * tq) * 2);
@@ -540,7 +565,6 @@ __global__ void __launch_bounds__(kThreads3, 2) gemv3_kernel(const Gemv3Params p
     };
 
     // ---- main loop: unit groups, then this warp's k-slots
-    float* part = reinterpret_cast<float*>(smem + p.smem_part);  // [upc][8 warps][TPU][MT][32][4]
     int slot = 0, consumed = 0;
 #pragma unroll 1
     for (int g = 0; g < ngroups; ++g) {
@@ -739,7 +763,9 @@ __global__ void __launch_bounds__(kThreads3, 2) gemv3_kernel(const Gemv3Params p
         }
     }
     __syncthreads();
+    }  // kPhRun
 
+    if (!(phases & kPhEpi)) return;
     // ---- reduce over warps, norm factor, epilogue. Task = (ul, mt).
 #pragma unroll 1
     for (int task = warp; task < nu * MT; task += 8) {
@@ -766,7 +792,7 @@ __global__ void __launch_bounds__(kThreads3, 2) gemv3_kernel(const Gemv3Params p
             const int cta_f = int(((c_first + 1) * uint32_t(p.grid) - 1) / T);
             const int cta_l = int(((c_last + 1) * uint32_t(p.grid) - 1) / T);
             const int npieces = cta_l - cta_f + 1;
-            const int me = int(blockIdx.x) - cta_f;
+            const int me = cta - cta_f;
             float* base = p.partials + (int64_t(unit) * p.p_max) * (TPU * 2 * 128);
             float* mine = base + int64_t(me) * (TPU * 2 * 128);
 #pragma unroll
@@ -842,12 +868,105 @@ __global__ void __launch_bounds__(kThreads3, 2) gemv3_kernel(const Gemv3Params p
                     const int m = m0 + (d & 1);
                     if (n < p.N && m < M) {
                         float o = v[tile][d];
-                        if (p.epi == BQ_EPI_ADD_RESIDUAL) o += s_res[(ul * 32 + rr) * 16 + m];
+                        if (p.epi == BQ_EPI_ADD_RESIDUAL) o += s_res[(ul * 32 + rr) * M + m];
                         store_act(p.out, m * p.ldo + n, p.out_dtype, o);
                     }
                 }
         }
     }
 }
+
+template <int FMT, int MT, int TPU, int GPK>
+__global__ void __launch_bounds__(kThreads3, 2) gemv3_kernel(const Gemv3Params p) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    RingState rst;
+    gemv_cta<FMT, MT, TPU, GPK>(p, smem, int(blockIdx.x), kPhAll, rst);
+}
+
+// ---------------------------------------------------------------- decode chain
+// One cooperative launch runs a list of GEMVs (a decode step's projections).
+// Two CTAs per SM, every CTA resident; between GEMVs a grid barrier. While a
+// GEMV runs, the next one's weight slice is pulled into L2, and as soon as
+// its main loop ends the next one's gamma and first ring slots are issued,
+// so the barrier is all that separates two projections.
+
+// Sense-reversing grid barrier on {count, generation}: bounded wait, error
+// word on timeout. The counter returns to zero after every barrier, so the
+// pair needs no reset between launches.
+__device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void grid_barrier(unsigned int* bar, unsigned int nblocks) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned int my = ld_acquire_u32(bar + 1);
+        __threadfence();
+        const unsigned int old = atomicAdd(bar, 1u);
+        if (old == nblocks - 1) {
+            atomicExch(bar, 0u);
+            __threadfence();
+            atomicAdd(bar + 1, 1u);
+        } else {
+            const long long t0 = clock64();
+            while (ld_acquire_u32(bar + 1) == my) {
+                if (clock64() - t0 > kWaitCycles) {
+                    atomicOr(&g_device_error, BQ_DEVERR_WAIT_TIMEOUT_BIT);
+                    break;
+                }
+            }
+        }
+        __threadfence();
+    }
+    __syncthreads();
+}
+
+template <int FMT, int MT, int GPK>
+__global__ void __launch_bounds__(kThreads3, 2)
+    gemv_chain_kernel(const Gemv3Params* __restrict__ ops, int n_ops, unsigned int* bar) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    __shared__ __align__(16) Gemv3Params sp[2];
+    auto load_op = [&](int i) {
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(ops + i);
+        uint32_t* dst = reinterpret_cast<uint32_t*>(&sp[i & 1]);
+        for (int t = threadIdx.x; t < int(sizeof(Gemv3Params) / 4); t += blockDim.x) dst[t] = __ldg(src + t);
+        __syncthreads();
+    };
+    RingState rs[2];
+    load_op(0);
+    // Step sequence (one call site per tile count keeps the code compact):
+    //   0: L2 + prefill of op 0, then the dependent-launch wait
+    //   per op i: L2 of op i+1, run op i, prefill op i+1, epilogue op i, grid barrier
+    for (int s = 0; s < 4 * n_ops + 1; ++s) {
+        int op, ph;
+        if (s == 0) {
+            op = 0;
+            ph = kPhL2 | kPhPrefill;
+        } else {
+            const int i = (s - 1) >> 2, k = (s - 1) & 3;
+            op = (k == 0 || k == 2) ? i + 1 : i;
+            ph = k == 0 ? kPhL2 : k == 1 ? kPhRun : k == 2 ? kPhPrefill : kPhEpi;
+            if (op >= n_ops) continue;
+            if (k == 0) load_op(op);
+        }
+        const Gemv3Params& p = sp[op & 1];
+        if (int(blockIdx.x) < p.grid) {
+            if (p.tpu == 1)
+                gemv_cta<FMT, MT, 1, GPK>(p, smem, int(blockIdx.x), ph, rs[op & 1]);
+            else
+                gemv_cta<FMT, MT, 2, GPK>(p, smem, int(blockIdx.x), ph, rs[op & 1]);
+        }
+        if (s == 0) {
+            pdl_launch_dependents();
+            pdl_wait();  // the first GEMV's inputs may come from a preceding kernel
+        } else if (((s - 1) & 3) == 3 && ((s - 1) >> 2) + 1 < n_ops) {
+            grid_barrier(bar, gridDim.x);
+        }
+    }
+}
+
+// Host: kernel parameters of one launch from a descriptor and its plan.
+void fill_gemv3_params(const bq_gemv_desc* d, const Gemv3Plan& pl, int row0, void* workspace, Gemv3Params* out);
 
 }  // namespace bq

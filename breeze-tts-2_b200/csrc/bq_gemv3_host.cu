@@ -20,6 +20,9 @@ int gpk_of(const bq_gemv_desc* d) { return (d->wfmt == BQ_W_INT4_TINYGEMM && d->
 int tile_bytes(int fmt, int gpk) { return boxes(fmt) * kBoxBytes + (int4fmt(fmt) ? int(align_up(64 * gpk, 128)) : 0); }
 }  // namespace
 
+int gemv3_tile_bytes(int fmt, int gpk) { return tile_bytes(fmt, gpk); }
+int gemv3_gpk(const bq_gemv_desc* d) { return gpk_of(d); }
+
 int gemv3_rows_per_launch(const bq_gemv_desc* d) {
     const DeviceInfo* dev = device_info();
     const int optin = dev ? dev->smem_optin : 232448;
@@ -29,16 +32,16 @@ int gemv3_rows_per_launch(const bq_gemv_desc* d) {
     // smallest ring that still double-buffers: two slots of one two-tile unit per warp
     const int64_t ring = 8 * 2 * 2 * int64_t(tile_bytes(d->wfmt, gpk_of(d)));
     const int64_t extra = 8 * nkbw * 256 + 4 * 8 * 2 * 2 * 512;  // gamma, partials
-    const int64_t budget = std::min<int64_t>(kXBudget, optin - ring - kMisc3Bytes - extra - 2048);
-    const int r = int(budget / (8 * pitch)) - 1;  // one zero row per warp
+    const int64_t budget = std::min<int64_t>(kXBudget, optin - ring - misc3_bytes(4, 16) - extra - 2048 - 8 * 256);
+    const int r = int(budget / (8 * pitch));
     return std::max(1, std::min(16, r));
 }
 
-int plan_gemv3(const bq_gemv_desc* d, int rows, Gemv3Plan* pl) {
+int plan_gemv3(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int slots) {
     const DeviceInfo* dev = device_info();
     if (!dev) return BQ_ERR_CUDA;
     const int fmt = d->wfmt;
-    const int SMs = dev->sm_count;
+    const int SMs = slots > 0 ? slots : dev->sm_count;  // CTA slots the work is spread over
     const int KB = d->K / kKB;
     Gemv3Plan P;
     std::memset(&P, 0, sizeof(P));
@@ -86,8 +89,8 @@ int plan_gemv3(const bq_gemv_desc* d, int rows, Gemv3Plan* pl) {
     if (upc_need > 4) return set_error(BQ_ERR_SHAPE, "internal: %d units per CTA", upc_need);
     P.upc = upc_need;
     const int ugm = (P.mt * P.tpu >= 4) ? 2 : 4;
-    const uint32_t x_bytes = uint32_t(8 * (rows + 1) * P.xrow_pitch);  // + one zero row per warp
-    const uint32_t gamma_bytes = uint32_t(8 * P.nkbw * 256);
+    const uint32_t x_bytes = uint32_t(8 * (rows * P.xrow_pitch + 256));  // + one zero k-block per warp
+    const uint32_t gamma_bytes = d->gamma ? uint32_t(8 * P.nkbw * 256) : 0u;
     const uint32_t part_bytes = uint32_t(P.upc * 8 * P.tpu * P.mt * 512);
     auto layout = [&](int ug, int rs) {
         const uint32_t slot = uint32_t(ug * P.tpu * tile_bytes(fmt, P.gpk));
@@ -105,7 +108,7 @@ int plan_gemv3(const bq_gemv_desc* d, int rows, Gemv3Plan* pl) {
         o += part_bytes;
         o = align_up(o, 16);
         P.smem_misc = o;
-        o += kMisc3Bytes;
+        o += misc3_bytes(P.upc, rows);
         return o;
     };
     // Largest unit group that still double-buffers within the co-residency
@@ -138,18 +141,8 @@ int plan_gemv3(const bq_gemv_desc* d, int rows, Gemv3Plan* pl) {
     return BQ_OK;
 }
 
-int launch_gemv3(const bq_gemv_desc* d, const Gemv3Plan& pl, int row0, void* workspace, cudaStream_t stream) {
-    const int fmt = d->wfmt;
-    const void* fn = nullptr;
-    if (int4fmt(fmt))
-        fn = gemv3_kernel_int4(fmt, pl.mt, pl.tpu, pl.gpk);
-    else if (fmt == BQ_W_BF16)
-        fn = gemv3_kernel_bf16(pl.mt, pl.tpu);
-    else
-        fn = gemv3_kernel_f8(fmt, pl.mt, pl.tpu);
-    if (!fn) return set_error(BQ_ERR_FORMAT, "no GEMV kernel for format %d (group %d)", fmt, d->group);
-
-    Gemv3Params p;
+void fill_gemv3_params(const bq_gemv_desc* d, const Gemv3Plan& pl, int row0, void* workspace, Gemv3Params* out) {
+    Gemv3Params& p = *out;
     std::memset(&p, 0, sizeof(p));
     p.M = pl.rows;
     p.N = d->N;
@@ -198,6 +191,21 @@ int launch_gemv3(const bq_gemv_desc* d, const Gemv3Plan& pl, int row0, void* wor
         p.counters = static_cast<unsigned int*>(workspace);
         p.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes);
     }
+}
+
+int launch_gemv3(const bq_gemv_desc* d, const Gemv3Plan& pl, int row0, void* workspace, cudaStream_t stream) {
+    const int fmt = d->wfmt;
+    const void* fn = nullptr;
+    if (int4fmt(fmt))
+        fn = gemv3_kernel_int4(fmt, pl.mt, pl.tpu, pl.gpk);
+    else if (fmt == BQ_W_BF16)
+        fn = gemv3_kernel_bf16(pl.mt, pl.tpu);
+    else
+        fn = gemv3_kernel_f8(fmt, pl.mt, pl.tpu);
+    if (!fn) return set_error(BQ_ERR_FORMAT, "no GEMV kernel for format %d (group %d)", fmt, d->group);
+
+    Gemv3Params p;
+    fill_gemv3_params(d, pl, row0, workspace, &p);
     int rc = ensure_smem_attr(fn, pl.smem_total);
     if (rc) return rc;
 

@@ -61,7 +61,9 @@ struct Gemv3Plan {
 // GEMV (per-warp cp.async weight rings, unit-group slots): rows per launch,
 // plan, launch.
 int gemv3_rows_per_launch(const bq_gemv_desc* d);
-int plan_gemv3(const bq_gemv_desc* d, int rows, Gemv3Plan* pl);
+int plan_gemv3(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int slots = 0);
+int gemv3_tile_bytes(int fmt, int gpk);
+int gemv3_gpk(const bq_gemv_desc* d);
 int launch_gemv3(const bq_gemv_desc* d, const Gemv3Plan& pl, int row0, void* workspace, cudaStream_t stream);
 
 int plan_gemv(const bq_gemv_desc* d, int rows, GemvPlan* pl);

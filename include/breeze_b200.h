@@ -135,6 +135,24 @@ int32_t bq_gemv(const bq_gemv_desc* desc, void* workspace, size_t workspace_byte
  * kernels can overlap on the GPU race and must be serialized. */
 int32_t bq_gemv_noalloc(const bq_gemv_desc* desc, void* stream);
 
+/* ---- decode chain: a list of GEMVs in one launch ------------------------ */
+/* Runs descs[0..n) in order as one cooperative launch (two CTAs per SM, a
+ * grid barrier between GEMVs, the next GEMV's weights prefetched while the
+ * current one runs). Replaces the per-projection rms_gemv / Int4Linear
+ * launches of one decode step (models/fused/layer.py:87-98 over every layer,
+ * as captured by cudagraph/backbone_graph.py:254-285); a GEMV may read any
+ * earlier GEMV's output. Every GEMV of a chain has the same weight format,
+ * group and M, and its M rows must fit one pass (BQ_ERR_SHAPE otherwise).
+ * The workspace (size from bq_gemv_chain_workspace_bytes, 256-byte aligned)
+ * holds the op table and barrier words: bq_gemv_chain_prepare writes it
+ * (synchronously, outside stream capture), after which
+ * bq_gemv_chain_launch is capture-safe and may be replayed. Re-prepare when
+ * any pointer in the descriptors changes. No counterpart in the reference. */
+int32_t bq_gemv_chain_workspace_bytes(const bq_gemv_desc* descs, int32_t n, size_t* bytes);
+int32_t bq_gemv_chain_prepare(const bq_gemv_desc* descs, int32_t n, void* workspace, size_t workspace_bytes);
+int32_t bq_gemv_chain_launch(const bq_gemv_desc* descs, int32_t n, void* workspace, size_t workspace_bytes,
+                             void* stream);
+
 /* ---- layouts and dequantization ---------------------------------------- */
 /* (N, K/2) uint8 odd-k-low -> tinygemm int32 [N/8, K/(16*ikt), 32, ikt/2].
  * Replaces torch._convert_weight_to_int4pack (models/int4_linear.py:59). */
