@@ -107,10 +107,12 @@ int plan_chain(const bq_gemv_desc* descs, int n, ChainPlan* cp) {
         for (int i = 0; i < n && ok; ++i) {
             Gemv3Plan& pl = cp->ops[i];
             const int ugm = (pl.mt * pl.tpu >= 4) ? 2 : 4;
+            const int kps = pl.mt == 1 ? 2 : 1;
+            const int nkp = (pl.nkbw + kps - 1) / kps;
             int ug = std::min(ugm, pl.upc), rs = 0;
             for (; ug >= 1; --ug) {
-                const int slot = ug * pl.tpu * tb;
-                const int max_seq = std::min(kMaxRing, ((pl.upc + ug - 1) / ug) * pl.nkbw);
+                const int slot = kps * ug * pl.tpu * tb;
+                const int max_seq = std::min(kMaxRing, ((pl.upc + ug - 1) / ug) * nkp);
                 rs = std::min<int>(max_seq, int(ring_w / uint32_t(slot)));
                 if (rs >= std::min(min_rs, max_seq)) break;
             }
@@ -119,7 +121,7 @@ int plan_chain(const bq_gemv_desc* descs, int n, ChainPlan* cp) {
                 break;
             }
             pl.ug = ug;
-            pl.slot_bytes = ug * pl.tpu * tb;
+            pl.slot_bytes = kps * ug * pl.tpu * tb;
             pl.ring_slots = rs;
             pl.smem_ring = 0;
             pl.smem_x = smem_x;

@@ -146,7 +146,11 @@ constexpr int kPhPrefill = 2;  // gamma and the first ring slots (static data on
 constexpr int kPhPdl = 4;      // programmatic-dependent-launch trigger and wait
 constexpr int kPhRun = 8;      // activations, staging, main loop, partials (ends in a block barrier)
 constexpr int kPhEpi = 16;     // cross-warp reduction, norm factor, epilogue, stores
-constexpr int kPhAll = 31;
+constexpr int kPhRing = 32;    // with kPhPrefill: also issue the first ring slots
+// The first ring slots go out before the dependent-launch wait: issuing them
+// costs ~1 us of load/store-path instructions per warp, which the previous
+// kernel's run hides (issued after the wait, they sit on the critical path).
+constexpr int kPhAll = kPhL2 | kPhPrefill | kPhRing | kPhPdl | kPhRun | kPhEpi;
 
 struct RingState {
     int issued, ig, ij;  // ring slots issued so far; next (group, k-slot) to issue
@@ -158,6 +162,7 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
     using F = Fmt3<FMT>;
     constexpr int UGM = ug_max<MT, TPU>();
     constexpr int NCH = MT == 1 ? 4 : 2;  // independent MMA chains per tile
+    constexpr int KPS = MT == 1 ? 2 : 1;  // k-blocks per ring slot
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int KB = p.KB, M = p.M;
     const uint32_t sbase = smem_u32(smem);
@@ -191,13 +196,21 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
         for (int i = 0; i < UGM; ++i) v |= (i < UG) && valid(g * UG + i, kb);
         return v;
     };
-    // this warp's k-blocks: [kw0, kw0 + nkw), a contiguous eighth of K
+    // this warp's k-blocks: [kw0, kw0 + nkw), a contiguous eighth of K; a ring
+    // slot carries KPS consecutive ones (index jp)
     const int kw0 = (warp * KB) >> 3, nkw = (((warp + 1) * KB) >> 3) - kw0;
-    // (group, k-slot) issue order: advance to the next entry with work
+    const int nkp = (nkw + KPS - 1) / KPS;
+    auto pair_valid = [&](int g, int jp) {
+        bool v = false;
+#pragma unroll
+        for (int kk = 0; kk < KPS; ++kk) v |= (jp * KPS + kk < nkw) && any_valid(g, kw0 + jp * KPS + kk);
+        return v;
+    };
+    // (group, slot) issue order: advance to the next entry with work
     auto normalize = [&](int& g, int& j) {
         while (g < ngroups) {
-            if (j < nkw && any_valid(g, kw0 + j)) return;
-            if (j + 1 < nkw) {
+            if (j < nkp && pair_valid(g, j)) return;
+            if (j + 1 < nkp) {
                 ++j;
             } else {
                 j = 0;
@@ -218,23 +231,31 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
     // ---- weight copies of one ring slot (whole warp; one cp.async group)
     const uint8_t* wg = static_cast<const uint8_t*>(p.w);
     const uint8_t* szg = static_cast<const uint8_t*>(p.scale);
-    auto issue = [&](int slot, int g, int j) {
-        const int kb = kw0 + j;
+    // Layout of a slot: [kk][i][tile] tiles of tile_bytes. Items that are not
+    // in this CTA's range (range ends, a short last group, an odd k-block
+    // count) are zero-filled, so the consumer processes every item of the slot
+    // without branches and they add nothing.
+    auto issue = [&](int slot, int g, int jp) {
         const uint32_t dst0 = ring_w + slot * p.slot_bytes;
 #pragma unroll
+        for (int kk = 0; kk < KPS; ++kk)
+#pragma unroll
         for (int i = 0; i < UGM; ++i) {
-            if (!(i < UG && valid(g * UG + i, kb))) continue;
-            const int unit = u_first + g * UG + i;
+            if (!(i < UG)) continue;
+            const int jj = jp * KPS + kk;
+            const int kb = kw0 + (jj < nkw ? jj : nkw - 1);
+            const bool item = jj < nkw && valid(g * UG + i, kb);
+            const int unit = item ? u_first + g * UG + i : u_first;
 #pragma unroll
             for (int tile = 0; tile < TPU; ++tile) {
                 const int row = tile_row(unit, tile);
-                const uint32_t d = dst0 + (i * TPU + tile) * tile_bytes;
+                const uint32_t d = dst0 + ((kk * UG + i) * TPU + tile) * tile_bytes;
                 if constexpr (FMT == BQ_W_INT4_TINYGEMM) {
                     // two 8-row tiles, 512 contiguous bytes each per k-block
 #pragma unroll
                     for (int q = 0; q < 2; ++q) {
                         const int pc = lane + 32 * q, nt = (row >> 3) + (pc >> 5);
-                        const bool ok = nt * 8 < p.N;
+                        const bool ok = item && nt * 8 < p.N;
                         cp_async16_zfill(d + pc * 16, wg + ((int64_t(ok ? nt : 0) * KB + kb) * 512 + (pc & 31) * 16), ok);
                     }
                 } else {
@@ -244,7 +265,7 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
 #pragma unroll
                     for (int q = 0; q < RB / 32; ++q) {
                         const int pc = lane + 32 * q, r = pc / (RB / 16), c = pc % (RB / 16);
-                        const bool ok = row + r < p.N;
+                        const bool ok = item && row + r < p.N;
                         cp_async16_zfill(d + (c >> 2) * kBoxBytes + r * 64 + (c & 3) * 16,
                                          wg + (int64_t(ok ? row + r : 0) * ld + int64_t(kb) * RB + c * 16), ok);
                     }
@@ -254,7 +275,7 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
                     if (lane < 4 * gpk_box) {
                         const int gi = lane >> 2;
                         const int grp = p.group >= 128 ? (kb << 7) >> p.group_shift : kb * gpk_box + gi;
-                        const bool ok = row + 4 * (lane & 3) < p.N;  // 4 rows per 16 bytes; N % 8 == 0
+                        const bool ok = item && row + 4 * (lane & 3) < p.N;  // 4 rows per 16 bytes; N % 8 == 0
                         cp_async16_zfill(d + F::kBoxes * kBoxBytes + gi * 64 + (lane & 3) * 16,
                                          szg + ((int64_t(grp) * p.N + (ok ? row : 0)) * 4 + (lane & 3) * 16), ok);
                     }
@@ -303,6 +324,23 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
         }
     }
 
+    auto fill_ring = [&](RingState& r) {
+        r.ig = 0;
+        r.ij = 0;
+        r.issued = 0;
+        normalize(r.ig, r.ij);
+        for (; r.issued < RS && r.ig < ngroups; ++r.issued) {
+            issue(r.issued, r.ig, r.ij);
+            if (r.ij + 1 < nkp) {
+                ++r.ij;
+            } else {
+                r.ij = 0;
+                ++r.ig;
+            }
+            normalize(r.ig, r.ij);
+        }
+    };
+
     // ======================================================= consumer warps
     const int tq = lane & 3, tg = lane >> 2;
     float* misc = reinterpret_cast<float*>(smem + p.smem_misc);
@@ -330,18 +368,8 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
         cp_async_commit();
         rst.ig = 0;
         rst.ij = 0;
-        rst.issued = 0;
-        normalize(rst.ig, rst.ij);
-        for (; rst.issued < RS && rst.ig < ngroups; ++rst.issued) {
-            issue(rst.issued, rst.ig, rst.ij);
-            if (rst.ij + 1 < nkw) {
-                ++rst.ij;
-            } else {
-                rst.ij = 0;
-                ++rst.ig;
-            }
-            normalize(rst.ig, rst.ij);
-        }
+        rst.issued = -1;  // ring not filled yet
+        if (phases & kPhRing) fill_ring(rst);
     }
 
     if (phases & kPhPdl) {
@@ -350,7 +378,6 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
     }
 
     if (phases & kPhRun) {
-    int issued = rst.issued, ig = rst.ig, ij = rst.ij;
     if (lane < 4) reinterpret_cast<uint32_t*>(smem + p.smem_misc + 512 * 4 + warp * 16)[lane] = 0u;
     if (lane < 16) reinterpret_cast<uint4*>(const_cast<uint8_t*>(xzero))[lane] = make_uint4(0u, 0u, 0u, 0u);
     for (int r = threadIdx.x; r < nu * 32; r += kConsumerThreads) {
@@ -403,6 +430,8 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
             }
         }
     }
+    if (rst.issued < 0) fill_ring(rst);
+    int issued = rst.issued, ig = rst.ig, ij = rst.ij;
     cp_async_wait_upto(issued);  // gamma landed (weight groups may still be pending)
     __syncwarp();
 
@@ -578,19 +607,25 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
 #pragma unroll
                     for (int d = 0; d < 4; ++d) acc[i][b][c][d] = 0.f;
 #pragma unroll 1
-        for (int j = 0; j < nkw; ++j) {
-            const int kb = kw0 + j;
-            if (!any_valid(g, kb)) continue;
+        for (int jp = 0; jp < nkp; ++jp) {
+            if (!pair_valid(g, jp)) continue;
             // this slot's group is complete once at most issued - 1 - consumed newer ones are pending
             cp_async_wait_upto(issued - 1 - consumed);
             __syncwarp();
             {
                 const uint8_t* src0 = smem + p.smem_ring + (warp * RS + slot) * p.slot_bytes;
-                uint32_t bfr[MT][16];
-                load_bfrag(j, bfr);
+                uint32_t bfr[KPS][MT][16];
                 // int4: per-group (A, X) of columns m0, m0+1 from indicator MMAs
-                float sA[GPK][MT][2], sX[GPK][MT][2];
+                float sA[KPS][GPK][MT][2], sX[KPS][GPK][MT][2];
+#pragma unroll
+                for (int kk = 0; kk < KPS; ++kk) {
+                    // a k-block past this warp's range reads real activations against zero-filled weights
+                    const int jj = jp * KPS + kk < nkw ? jp * KPS + kk : nkw - 1;
+                    load_bfrag(jj, bfr[kk]);
+                }
                 if constexpr (F::kInt4) {
+#pragma unroll
+                    for (int kk = 0; kk < KPS; ++kk)
 #pragma unroll
                     for (int sg = 0; sg < GPK; ++sg) {
                         float c2[2][MT][4];
@@ -605,27 +640,29 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
                             const int i = sg * (8 / GPK) + ii;
 #pragma unroll
                             for (int mt = 0; mt < MT; ++mt)
-                                mma_f16(c2[ii & 1][mt], 0x3C003C00u, 0u, 0u, 0x3C003C00u, bfr[mt][2 * i],
-                                        bfr[mt][2 * i + 1]);
+                                mma_f16(c2[ii & 1][mt], 0x3C003C00u, 0u, 0u, 0x3C003C00u, bfr[kk][mt][2 * i],
+                                        bfr[kk][mt][2 * i + 1]);
                         }
 #pragma unroll
                         for (int mt = 0; mt < MT; ++mt) {
                             // c0/c1: low-nibble sums of columns m0, m0+1; c2/c3: high-nibble sums
                             const float lo0 = c2[0][mt][0] + c2[1][mt][0], lo1 = c2[0][mt][1] + c2[1][mt][1];
                             const float hi0 = c2[0][mt][2] + c2[1][mt][2], hi1 = c2[0][mt][3] + c2[1][mt][3];
-                            sX[sg][mt][0] = lo0 + 16.f * hi0;
-                            sX[sg][mt][1] = lo1 + 16.f * hi1;
-                            sA[sg][mt][0] = 1024.f * (lo0 + hi0) + float(F::kOfs) * sX[sg][mt][0];
-                            sA[sg][mt][1] = 1024.f * (lo1 + hi1) + float(F::kOfs) * sX[sg][mt][1];
+                            sX[kk][sg][mt][0] = lo0 + 16.f * hi0;
+                            sX[kk][sg][mt][1] = lo1 + 16.f * hi1;
+                            sA[kk][sg][mt][0] = 1024.f * (lo0 + hi0) + float(F::kOfs) * sX[kk][sg][mt][0];
+                            sA[kk][sg][mt][1] = 1024.f * (lo1 + hi1) + float(F::kOfs) * sX[kk][sg][mt][1];
                         }
                     }
                 }
 #pragma unroll
                 for (int i = 0; i < UGM; ++i) {
-                    if (!(i < UG && valid(g * UG + i, kb))) continue;
+                    if (!(i < UG)) continue;
 #pragma unroll
-                    for (int tile = 0; tile < TPU; ++tile) {
-                        const uint8_t* src = src0 + (i * TPU + tile) * tile_bytes;
+                    for (int tile = 0; tile < TPU; ++tile)
+#pragma unroll
+                    for (int kk = 0; kk < KPS; ++kk) {
+                        const uint8_t* src = src0 + ((kk * UG + i) * TPU + tile) * tile_bytes;
                         if constexpr (F::kInt4) {
                             const uint4 r0 = *reinterpret_cast<const uint4*>(src + lane * 16);
                             const uint4 r1 = *reinterpret_cast<const uint4*>(src + 512 + lane * 16);
@@ -650,7 +687,7 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
                                     const uint32_t a1 = i4lo_raw(x1), a3 = i4hi_raw(x1);
 #pragma unroll
                                     for (int mt = 0; mt < MT; ++mt)
-                                        mma_f16(c2[ii % NCH][mt], a0, a1, a2, a3, bfr[mt][2 * ki], bfr[mt][2 * ki + 1]);
+                                        mma_f16(c2[ii % NCH][mt], a0, a1, a2, a3, bfr[kk][mt][2 * ki], bfr[kk][mt][2 * ki + 1]);
                                 }
 #pragma unroll
                                 for (int h = 1; h < NCH; ++h)
@@ -665,10 +702,10 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
 #pragma unroll
                                 for (int mt = 0; mt < MT; ++mt) {
                                     float* a = acc[i][tile][mt];
-                                    a[0] += s0 * (c2[0][mt][0] - sA[sg][mt][0]) + z0 * sX[sg][mt][0];
-                                    a[1] += s0 * (c2[0][mt][1] - sA[sg][mt][1]) + z0 * sX[sg][mt][1];
-                                    a[2] += s1 * (c2[0][mt][2] - sA[sg][mt][0]) + z1 * sX[sg][mt][0];
-                                    a[3] += s1 * (c2[0][mt][3] - sA[sg][mt][1]) + z1 * sX[sg][mt][1];
+                                    a[0] += s0 * (c2[0][mt][0] - sA[kk][sg][mt][0]) + z0 * sX[kk][sg][mt][0];
+                                    a[1] += s0 * (c2[0][mt][1] - sA[kk][sg][mt][1]) + z0 * sX[kk][sg][mt][1];
+                                    a[2] += s1 * (c2[0][mt][2] - sA[kk][sg][mt][0]) + z1 * sX[kk][sg][mt][0];
+                                    a[3] += s1 * (c2[0][mt][3] - sA[kk][sg][mt][1]) + z1 * sX[kk][sg][mt][1];
                                 }
                             }
                         } else {
@@ -693,7 +730,7 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
 #pragma unroll
                                         for (int mt = 0; mt < MT; ++mt)
                                             mma_bf16(c2[ki % NCH][mt], w0[2 * e2], w1[2 * e2], w0[2 * e2 + 1], w1[2 * e2 + 1],
-                                                     bfr[mt][2 * ki], bfr[mt][2 * ki + 1]);
+                                                     bfr[kk][mt][2 * ki], bfr[kk][mt][2 * ki + 1]);
                                     }
                                 } else {
 #pragma unroll
@@ -714,7 +751,7 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
                                         }
 #pragma unroll
                                         for (int mt = 0; mt < MT; ++mt)
-                                            mma_f16(c2[ki % NCH][mt], a0, a1, a2, a3, bfr[mt][2 * ki], bfr[mt][2 * ki + 1]);
+                                            mma_f16(c2[ki % NCH][mt], a0, a1, a2, a3, bfr[kk][mt][2 * ki], bfr[kk][mt][2 * ki + 1]);
                                     }
                                 }
                             }
@@ -733,7 +770,7 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
             if (ig < ngroups) {
                 issue(slot, ig, ij);
                 ++issued;
-                if (ij + 1 < nkw) {
+                if (ij + 1 < nkp) {
                     ++ij;
                 } else {
                     ij = 0;
@@ -942,11 +979,11 @@ __global__ void __launch_bounds__(kThreads3, 2)
         int op, ph;
         if (s == 0) {
             op = 0;
-            ph = kPhL2 | kPhPrefill;
+            ph = kPhL2 | kPhPrefill | kPhRing;
         } else {
             const int i = (s - 1) >> 2, k = (s - 1) & 3;
             op = (k == 0 || k == 2) ? i + 1 : i;
-            ph = k == 0 ? kPhL2 : k == 1 ? kPhRun : k == 2 ? kPhPrefill : kPhEpi;
+            ph = k == 0 ? kPhL2 : k == 1 ? kPhRun : k == 2 ? (kPhPrefill | kPhRing) : kPhEpi;
             if (op >= n_ops) continue;
             if (k == 0) load_op(op);
         }

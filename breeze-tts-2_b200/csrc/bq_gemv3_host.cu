@@ -89,11 +89,13 @@ int plan_gemv3(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int slots) {
     if (upc_need > 4) return set_error(BQ_ERR_SHAPE, "internal: %d units per CTA", upc_need);
     P.upc = upc_need;
     const int ugm = (P.mt * P.tpu >= 4) ? 2 : 4;
+    const int kps = P.mt == 1 ? 2 : 1;             // k-blocks per ring slot (kernel's KPS)
+    const int nkp = (P.nkbw + kps - 1) / kps;      // ring slots per unit group and warp
     const uint32_t x_bytes = uint32_t(8 * (rows * P.xrow_pitch + 256));  // + one zero k-block per warp
     const uint32_t gamma_bytes = d->gamma ? uint32_t(8 * P.nkbw * 256) : 0u;
     const uint32_t part_bytes = uint32_t(P.upc * 8 * P.tpu * P.mt * 512);
     auto layout = [&](int ug, int rs) {
-        const uint32_t slot = uint32_t(ug * P.tpu * tile_bytes(fmt, P.gpk));
+        const uint32_t slot = uint32_t(kps * ug * P.tpu * tile_bytes(fmt, P.gpk));
         uint32_t o = 0;
         P.smem_ring = o;
         o += 8 * rs * slot;
@@ -116,7 +118,7 @@ int plan_gemv3(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int slots) {
     // the device allows.
     int ug = 0, rs = 0;
     for (int u = std::min(ugm, P.upc); u >= 1 && !ug; --u) {
-        const int max_seq = std::min(kMaxRing, ((P.upc + u - 1) / u) * P.nkbw);
+        const int max_seq = std::min(kMaxRing, ((P.upc + u - 1) / u) * nkp);
         const int need = std::min(2, max_seq);
         if (layout(u, need) > kTargetSmem) continue;
         ug = u;
@@ -125,7 +127,7 @@ int plan_gemv3(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int slots) {
     }
     if (!ug) {
         ug = 1;
-        const int max_seq = std::min(kMaxRing, P.upc * P.nkbw);
+        const int max_seq = std::min(kMaxRing, P.upc * nkp);
         rs = std::min(2, max_seq);
         while (rs > 1 && layout(1, rs) > uint32_t(dev->smem_optin)) --rs;
     }
@@ -133,7 +135,7 @@ int plan_gemv3(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int slots) {
     if (total > uint32_t(dev->smem_optin))
         return set_error(BQ_ERR_SHAPE, "GEMV does not fit in shared memory (K=%d, rows=%d)", d->K, rows);
     P.ug = ug;
-    P.slot_bytes = ug * P.tpu * tile_bytes(fmt, P.gpk);
+    P.slot_bytes = kps * ug * P.tpu * tile_bytes(fmt, P.gpk);
     P.ring_slots = rs;
     P.smem_total = total;
     P.ws_bytes = P.owned ? 0 : kCounterBytes + int64_t(U) * P.p_max * P.tpu * 2 * 128 * 4;
