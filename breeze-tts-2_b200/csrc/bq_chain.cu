@@ -77,7 +77,7 @@ int plan_chain(const bq_gemv_desc* descs, int n, ChainPlan* cp) {
             std::min<uint32_t>(uint32_t(dev->smem_optin) - 1024u, (233472u - 1024u * per_sm) / per_sm - 1024u);
         cp->grid = slots;
         cp->ops.assign(n, Gemv3Plan());
-        uint32_t x_max = 0, g_max = 0, part_max = 0;
+        uint32_t x_max = 0, g_max = 0, part_max = 0, xs_max = 0;
         int64_t split_need = 0;
         bool ok = true;
         for (int i = 0; i < n && ok; ++i) {
@@ -89,6 +89,8 @@ int plan_chain(const bq_gemv_desc* descs, int n, ChainPlan* cp) {
             const Gemv3Plan& pl = cp->ops[i];
             x_max = std::max<uint32_t>(x_max, uint32_t(8 * (M * pl.xrow_pitch + 256)));
             if (d->gamma) g_max = std::max<uint32_t>(g_max, uint32_t(8 * pl.nkbw * 256));
+            if (cp->fmt == BQ_W_INT4_TINYGEMM || cp->fmt == BQ_W_INT4_PLAIN)
+                xs_max = std::max<uint32_t>(xs_max, uint32_t(8 * pl.nkbw * pl.gpk * pl.mt * 64));
             part_max = std::max<uint32_t>(part_max, uint32_t(pl.upc * 8 * pl.tpu * pl.mt * 512));
             split_need = std::max(split_need, pl.ws_bytes);
         }
@@ -97,11 +99,12 @@ int plan_chain(const bq_gemv_desc* descs, int n, ChainPlan* cp) {
         int upc_max = 1;
         for (int i = 0; i < n; ++i) upc_max = std::max(upc_max, cp->ops[i].upc);
         const uint32_t misc = misc3_bytes(upc_max, M);
-        const uint32_t fixed = align_up(x_max, 16) + align_up(g_max, 16) + align_up(part_max, 16) + misc;
+        const uint32_t fixed = align_up(x_max, 16) + align_up(xs_max, 16) + align_up(g_max, 16) + align_up(part_max, 16) + misc;
         if (fixed >= budget) continue;
         const uint32_t ring_w = ((budget - fixed) / 8) / 128 * 128;  // ring bytes per warp
         const uint32_t smem_x = 8 * ring_w;
-        const uint32_t smem_gamma = align_up(smem_x + x_max, 16);
+        const uint32_t smem_xsum = align_up(smem_x + x_max, 16);
+        const uint32_t smem_gamma = align_up(smem_xsum + xs_max, 16);
         const uint32_t smem_part = align_up(smem_gamma + g_max, 16);
         const uint32_t smem_misc = align_up(smem_part + part_max, 16);
         for (int i = 0; i < n && ok; ++i) {
@@ -125,6 +128,7 @@ int plan_chain(const bq_gemv_desc* descs, int n, ChainPlan* cp) {
             pl.ring_slots = rs;
             pl.smem_ring = 0;
             pl.smem_x = smem_x;
+            pl.smem_xsum = smem_xsum;
             pl.smem_gamma = smem_gamma;
             pl.smem_part = smem_part;
             pl.smem_misc = smem_misc;

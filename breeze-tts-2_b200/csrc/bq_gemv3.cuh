@@ -15,15 +15,17 @@
 //    while the previous kernel runs; completion is tracked per warp with
 //    cp.async groups, so warps never wait for each other until the final
 //    reduction.
-//  * A ring slot holds one k-block of up to UG units (a "unit group"), so the
-//    activation fragments of a k-block are loaded once for all its units.
+//  * A ring slot holds KPS k-blocks of up to UG units (a "unit group"), so
+//    the activation fragments of a k-block are loaded once for all its units;
+//    items outside the CTA's range are zero-filled and computed branch-free.
 //  * Staging is row-parallel: lanes are split into row groups (32 / rows per
 //    row, rounded to a power of two) that reduce sum-of-squares and max|x*g|
 //    with a few shuffles, then rewrite the row as f16 scaled by a per-(warp,
 //    row) power of two. RMSNorm's 1/rms is applied to the accumulator.
 //  * int4 magic offsets (1024 + q, 1024 + 16 q) are removed once per group:
 //    an MMA with a 0/1 indicator operand gives the low- and high-nibble
-//    activation sums of each column directly in the lanes that need them.
+//    activation sums of each column; they are computed once per k-block
+//    after staging and kept in shared memory.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -53,7 +55,7 @@ struct Gemv3Params {
     int32_t x_bulk;      // bf16 x with 16-byte aligned rows: staged with 16-byte loads
     int32_t upc;         // most units any CTA covers
     int32_t group_shift; // log2(group) for int4
-    uint32_t smem_ring, smem_x, smem_gamma, smem_part, smem_misc;
+    uint32_t smem_ring, smem_x, smem_xsum, smem_gamma, smem_part, smem_misc;
     const void* x;
     const void* w;
     int64_t ldx;
@@ -593,6 +595,48 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
         }
     };
 
+    // ---- int4: per-group (A, X) of columns m0, m0+1 for every k-block of this
+    // warp, once: an MMA with a 0/1 indicator A operand sums the low-nibble
+    // (rows 0-7) and high-nibble (rows 8-15) activations of each column.
+    // Lanes tg == 0 keep {A(m0), X(m0), A(m0+1), X(m0+1)} in shared memory.
+    float4* xsum4 = reinterpret_cast<float4*>(smem + p.smem_xsum) + warp * (p.nkbw * GPK * MT * 4);
+    if constexpr (F::kInt4) {
+#pragma unroll 2
+        for (int j = 0; j < nkw; ++j) {
+            uint32_t bf[MT][16];
+            load_bfrag(j, bf);
+#pragma unroll
+            for (int sg = 0; sg < GPK; ++sg) {
+                float c2[2][MT][4];
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                        for (int d = 0; d < 4; ++d) c2[h][mt][d] = 0.f;
+#pragma unroll
+                for (int ii = 0; ii < 8 / GPK; ++ii) {
+                    const int i = sg * (8 / GPK) + ii;
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt)
+                        mma_f16(c2[ii & 1][mt], 0x3C003C00u, 0u, 0u, 0x3C003C00u, bf[mt][2 * i], bf[mt][2 * i + 1]);
+                }
+                if (tg == 0) {
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt) {
+                        const float lo0 = c2[0][mt][0] + c2[1][mt][0], lo1 = c2[0][mt][1] + c2[1][mt][1];
+                        const float hi0 = c2[0][mt][2] + c2[1][mt][2], hi1 = c2[0][mt][3] + c2[1][mt][3];
+                        const float x0 = lo0 + 16.f * hi0, x1 = lo1 + 16.f * hi1;
+                        xsum4[((j * GPK + sg) * MT + mt) * 4 + tq] =
+                            make_float4(1024.f * (lo0 + hi0) + float(F::kOfs) * x0, x0,
+                                        1024.f * (lo1 + hi1) + float(F::kOfs) * x1, x1);
+                    }
+                }
+            }
+        }
+        __syncwarp();
+    }
+
     // ---- main loop: unit groups, then this warp's k-slots
     int slot = 0, consumed = 0;
 #pragma unroll 1
@@ -625,34 +669,18 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
                 }
                 if constexpr (F::kInt4) {
 #pragma unroll
-                    for (int kk = 0; kk < KPS; ++kk)
+                    for (int kk = 0; kk < KPS; ++kk) {
+                        const int jj = jp * KPS + kk < nkw ? jp * KPS + kk : nkw - 1;
 #pragma unroll
-                    for (int sg = 0; sg < GPK; ++sg) {
-                        float c2[2][MT][4];
+                        for (int sg = 0; sg < GPK; ++sg)
 #pragma unroll
-                        for (int h = 0; h < 2; ++h)
-#pragma unroll
-                            for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-                                for (int d = 0; d < 4; ++d) c2[h][mt][d] = 0.f;
-#pragma unroll
-                        for (int ii = 0; ii < 8 / GPK; ++ii) {
-                            const int i = sg * (8 / GPK) + ii;
-#pragma unroll
-                            for (int mt = 0; mt < MT; ++mt)
-                                mma_f16(c2[ii & 1][mt], 0x3C003C00u, 0u, 0u, 0x3C003C00u, bfr[kk][mt][2 * i],
-                                        bfr[kk][mt][2 * i + 1]);
-                        }
-#pragma unroll
-                        for (int mt = 0; mt < MT; ++mt) {
-                            // c0/c1: low-nibble sums of columns m0, m0+1; c2/c3: high-nibble sums
-                            const float lo0 = c2[0][mt][0] + c2[1][mt][0], lo1 = c2[0][mt][1] + c2[1][mt][1];
-                            const float hi0 = c2[0][mt][2] + c2[1][mt][2], hi1 = c2[0][mt][3] + c2[1][mt][3];
-                            sX[kk][sg][mt][0] = lo0 + 16.f * hi0;
-                            sX[kk][sg][mt][1] = lo1 + 16.f * hi1;
-                            sA[kk][sg][mt][0] = 1024.f * (lo0 + hi0) + float(F::kOfs) * sX[kk][sg][mt][0];
-                            sA[kk][sg][mt][1] = 1024.f * (lo1 + hi1) + float(F::kOfs) * sX[kk][sg][mt][1];
-                        }
+                            for (int mt = 0; mt < MT; ++mt) {
+                                const float4 ax = xsum4[((jj * GPK + sg) * MT + mt) * 4 + tq];
+                                sA[kk][sg][mt][0] = ax.x;
+                                sX[kk][sg][mt][0] = ax.y;
+                                sA[kk][sg][mt][1] = ax.z;
+                                sX[kk][sg][mt][1] = ax.w;
+                            }
                     }
                 }
 #pragma unroll

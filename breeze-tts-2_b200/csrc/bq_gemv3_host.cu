@@ -31,7 +31,7 @@ int gemv3_rows_per_launch(const bq_gemv_desc* d) {
     const int64_t pitch = nkbw * 256 + 16;
     // smallest ring that still double-buffers: two slots of one two-tile unit per warp
     const int64_t ring = 8 * 2 * 2 * int64_t(tile_bytes(d->wfmt, gpk_of(d)));
-    const int64_t extra = 8 * nkbw * 256 + 4 * 8 * 2 * 2 * 512;  // gamma, partials
+    const int64_t extra = 8 * nkbw * 256 + 4 * 8 * 2 * 2 * 512 + 8 * nkbw * 4 * 2 * 64;  // gamma, partials, group sums
     const int64_t budget = std::min<int64_t>(kXBudget, optin - ring - misc3_bytes(4, 16) - extra - 2048 - 8 * 256);
     const int r = int(budget / (8 * pitch));
     return std::max(1, std::min(16, r));
@@ -93,6 +93,7 @@ int plan_gemv3(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int slots) {
     const int nkp = (P.nkbw + kps - 1) / kps;      // ring slots per unit group and warp
     const uint32_t x_bytes = uint32_t(8 * (rows * P.xrow_pitch + 256));  // + one zero k-block per warp
     const uint32_t gamma_bytes = d->gamma ? uint32_t(8 * P.nkbw * 256) : 0u;
+    const uint32_t xsum_bytes = int4fmt(fmt) ? uint32_t(8 * P.nkbw * P.gpk * P.mt * 64) : 0u;
     const uint32_t part_bytes = uint32_t(P.upc * 8 * P.tpu * P.mt * 512);
     auto layout = [&](int ug, int rs) {
         const uint32_t slot = uint32_t(kps * ug * P.tpu * tile_bytes(fmt, P.gpk));
@@ -102,6 +103,9 @@ int plan_gemv3(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int slots) {
         o = align_up(o, 16);
         P.smem_x = o;
         o += x_bytes;
+        o = align_up(o, 16);
+        P.smem_xsum = o;
+        o += xsum_bytes;
         o = align_up(o, 16);
         P.smem_gamma = o;
         o += gamma_bytes;
@@ -172,6 +176,7 @@ void fill_gemv3_params(const bq_gemv_desc* d, const Gemv3Plan& pl, int row0, voi
     p.upc = pl.upc;
     p.smem_ring = pl.smem_ring;
     p.smem_x = pl.smem_x;
+    p.smem_xsum = pl.smem_xsum;
     p.smem_gamma = pl.smem_gamma;
     p.smem_part = pl.smem_part;
     p.smem_misc = pl.smem_misc;

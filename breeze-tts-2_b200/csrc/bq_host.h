@@ -55,7 +55,7 @@ struct Gemv3Plan {
     int rows, mt, upc, tpu, gpk, ug;
     int grid, owned, n_units, ring_slots, slot_bytes, nkbw, p_max, xrow_pitch;
     int64_t total_chunks, ws_bytes;
-    uint32_t smem_ring, smem_x, smem_gamma, smem_part, smem_misc, smem_total;
+    uint32_t smem_ring, smem_x, smem_xsum, smem_gamma, smem_part, smem_misc, smem_total;
 };
 
 // GEMV (per-warp cp.async weight rings, unit-group slots): rows per launch,
