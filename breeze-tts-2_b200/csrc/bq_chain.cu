@@ -91,7 +91,8 @@ int plan_chain(const bq_gemv_desc* descs, int n, ChainPlan* cp) {
             if (d->gamma) g_max = std::max<uint32_t>(g_max, uint32_t(8 * pl.nkbw * 256));
             if (cp->fmt == BQ_W_INT4_TINYGEMM || cp->fmt == BQ_W_INT4_PLAIN)
                 xs_max = std::max<uint32_t>(xs_max, uint32_t(8 * pl.nkbw * pl.gpk * pl.mt * 64));
-            part_max = std::max<uint32_t>(part_max, uint32_t(pl.upc * 8 * pl.tpu * pl.mt * 512));
+            const int nq = M >= 7 ? 4 : (M + 1) / 2;
+            part_max = std::max<uint32_t>(part_max, uint32_t(pl.upc * 8 * pl.tpu * pl.mt * 128 * nq));
             split_need = std::max(split_need, pl.ws_bytes);
         }
         if (!ok) continue;

@@ -352,7 +352,13 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
     float* s_rbias = misc + 384;   // [128]
     float* s_res = misc + 512 + 32;  // [nu*32][M], after the zero blocks
     const uint32_t zero_blk = sbase + p.smem_misc + 512 * 4 + warp * 16;
-    float* part = reinterpret_cast<float*>(smem + p.smem_part);  // [upc][8 warps][TPU][MT][32][4]
+    // per-warp partial sums [upc][8 warps][TPU][MT][8 tg][nq tq][4]: only the lanes
+    // whose columns 2tq, 2tq+1 can hold a real row (tq < nq = min(4, ceil(M/2)))
+    float* part = reinterpret_cast<float*>(smem + p.smem_part);
+    const int nq = M >= 7 ? 4 : (M + 1) >> 1;
+    auto part_at = [&](int ul, int w, int tile, int mt) {
+        return reinterpret_cast<float4*>(part) + (((((ul * 8 + w) * TPU + tile) * MT + mt) * 8 + tg) * nq + tq);
+    };
     // per warp: M staged rows, then one zero k-block read by the B fragments of rows >= M
     uint8_t* xw_ptr = smem + p.smem_x + warp * (M * pitch + 256);
     const uint32_t xw = xs0 + warp * (M * pitch + 256);
@@ -820,9 +826,9 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
                 if (!(i < UG && ul < nu)) continue;
 #pragma unroll
                 for (int tile = 0; tile < TPU; ++tile) {
-                    float4 v = make_float4(acc[i][tile][mt][0] * u0, acc[i][tile][mt][1] * u1,
-                                           acc[i][tile][mt][2] * u0, acc[i][tile][mt][3] * u1);
-                    *reinterpret_cast<float4*>(part + ((((ul * 8 + warp) * TPU + tile) * MT + mt) * 32 + lane) * 4) = v;
+                    if (tq < nq)
+                        *part_at(ul, warp, tile, mt) = make_float4(acc[i][tile][mt][0] * u0, acc[i][tile][mt][1] * u1,
+                                                                   acc[i][tile][mt][2] * u0, acc[i][tile][mt][3] * u1);
                 }
             }
         }
@@ -841,8 +847,7 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
         for (int tile = 0; tile < TPU; ++tile) {
             float4 q[8];
 #pragma unroll
-            for (int w = 0; w < 8; ++w)
-                q[w] = *reinterpret_cast<const float4*>(part + ((((ul * 8 + w) * TPU + tile) * MT + mt) * 32 + lane) * 4);
+            for (int w = 0; w < 8; ++w) q[w] = tq < nq ? *part_at(ul, w, tile, mt) : make_float4(0.f, 0.f, 0.f, 0.f);
             v[tile][0] = ((q[0].x + q[1].x) + (q[2].x + q[3].x)) + ((q[4].x + q[5].x) + (q[6].x + q[7].x));
             v[tile][1] = ((q[0].y + q[1].y) + (q[2].y + q[3].y)) + ((q[4].y + q[5].y) + (q[6].y + q[7].y));
             v[tile][2] = ((q[0].z + q[1].z) + (q[2].z + q[3].z)) + ((q[4].z + q[5].z) + (q[6].z + q[7].z));

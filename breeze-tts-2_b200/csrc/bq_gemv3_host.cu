@@ -31,7 +31,8 @@ int gemv3_rows_per_launch(const bq_gemv_desc* d) {
     const int64_t pitch = nkbw * 256 + 16;
     // smallest ring that still double-buffers: two slots of one two-tile unit per warp
     const int64_t ring = 8 * 2 * 2 * int64_t(tile_bytes(d->wfmt, gpk_of(d)));
-    const int64_t extra = 8 * nkbw * 256 + 4 * 8 * 2 * 2 * 512 + 8 * nkbw * 4 * 2 * 64;  // gamma, partials, group sums
+    const int64_t xsum = int4fmt(d->wfmt) ? 8 * nkbw * gpk_of(d) * 2 * 64 : 0;  // int4 group sums
+    const int64_t extra = 8 * nkbw * 256 + 4 * 8 * 2 * 2 * 512 + xsum;           // gamma, partials
     const int64_t budget = std::min<int64_t>(kXBudget, optin - ring - misc3_bytes(4, 16) - extra - 2048 - 8 * 256);
     const int r = int(budget / (8 * pitch));
     return std::max(1, std::min(16, r));
@@ -94,7 +95,8 @@ int plan_gemv3(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int slots) {
     const uint32_t x_bytes = uint32_t(8 * (rows * P.xrow_pitch + 256));  // + one zero k-block per warp
     const uint32_t gamma_bytes = d->gamma ? uint32_t(8 * P.nkbw * 256) : 0u;
     const uint32_t xsum_bytes = int4fmt(fmt) ? uint32_t(8 * P.nkbw * P.gpk * P.mt * 64) : 0u;
-    const uint32_t part_bytes = uint32_t(P.upc * 8 * P.tpu * P.mt * 512);
+    const int nq = rows >= 7 ? 4 : (rows + 1) / 2;  // lane groups holding real columns
+    const uint32_t part_bytes = uint32_t(P.upc * 8 * P.tpu * P.mt * 128 * nq);
     auto layout = [&](int ug, int rs) {
         const uint32_t slot = uint32_t(kps * ug * P.tpu * tile_bytes(fmt, P.gpk));
         uint32_t o = 0;
