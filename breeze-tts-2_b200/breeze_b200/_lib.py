@@ -46,6 +46,19 @@ class GemvDesc(ctypes.Structure):
     ]
 
 
+class AttnDesc(ctypes.Structure):
+    """bq_attn_desc (include/breeze_b200.h)."""
+
+    _fields_ = [
+        ("B", ctypes.c_int32), ("HQ", ctypes.c_int32), ("HKV", ctypes.c_int32), ("D", ctypes.c_int32),
+        ("S", ctypes.c_int32), ("mask_dtype", ctypes.c_int32), ("eps", ctypes.c_float), ("flags", ctypes.c_uint32),
+        ("qkv", ctypes.c_void_p), ("ldqkv", ctypes.c_int64), ("cos", ctypes.c_void_p), ("sin", ctypes.c_void_p),
+        ("ldcs", ctypes.c_int64), ("pos", ctypes.c_void_p), ("k_cache", ctypes.c_void_p), ("v_cache", ctypes.c_void_p),
+        ("mask", ctypes.c_void_p), ("ldm", ctypes.c_int64), ("q_norm", ctypes.c_void_p), ("k_norm", ctypes.c_void_p),
+        ("out", ctypes.c_void_p), ("ldo", ctypes.c_int64),
+    ]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -63,6 +76,8 @@ _SIGS = {
                                                ctypes.c_size_t]),
     "bq_gemv_chain_launch": (ctypes.c_int32, [ctypes.POINTER(GemvDesc), ctypes.c_int32, ctypes.c_void_p,
                                               ctypes.c_size_t, ctypes.c_void_p]),
+    "bq_attention_workspace_bytes": (ctypes.c_int32, [ctypes.POINTER(AttnDesc), ctypes.POINTER(ctypes.c_size_t)]),
+    "bq_attention_step": (ctypes.c_int32, [ctypes.POINTER(AttnDesc), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     "bq_int4_tinygemm_pack": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
                                                ctypes.c_int32, ctypes.c_void_p]),
     "bq_int4_tinygemm_unpack": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
@@ -180,6 +195,10 @@ class Workspace:
 
 
 WORKSPACE = Workspace()
+# bq_attention_step keeps its own counters at the start of its workspace;
+# bq_gemv's arrival counters (also at the start) must stay zero at rest, so
+# the two never share a buffer.
+ATTN_WORKSPACE = Workspace()
 
 
 def make_desc(x: torch.Tensor, w: torch.Tensor, wfmt: int, n: int, *, scale=None, group: int = 128, gamma=None,
@@ -278,6 +297,76 @@ class GemvChain:
     def launch(self) -> None:
         check(load().bq_gemv_chain_launch(self._arr, self.n, self.ws.data_ptr(), self.ws.numel(), _stream(self.device)),
               "bq_gemv_chain_launch")
+
+
+_MASKS: dict = {}
+
+
+def additive_mask(mask: torch.Tensor, b: int, s: int) -> torch.Tensor:
+    """(B, 1, Q, S) additive float or bool mask -> (B, S) additive, as the
+    reference's _additive_mask (models/fused/kernels.py:492-502): bool masks
+    become 0 / -1e30 fp32 once per static buffer."""
+    if mask.dtype != torch.bool:
+        m = mask.reshape(b, -1)
+        return m[:, :s] if m.shape[1] != s else m
+    key = (mask.data_ptr(), tuple(mask.shape), str(mask.device))
+    m2 = _MASKS.get(key)
+    if m2 is None:
+        m2 = torch.where(mask.reshape(b, -1)[:, :s], 0.0, -1e30).float().contiguous()
+        _MASKS[key] = m2
+    return m2
+
+
+def attention_step(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, cache_position: torch.Tensor,
+                   keys: torch.Tensor, values: torch.Tensor, mask: torch.Tensor | None, q_norm_w=None, k_norm_w=None,
+                   eps: float = 1e-6, out: torch.Tensor | None = None, flags: int = 0) -> torch.Tensor:
+    """One decode-attention step through bq_attention_step (see the header)."""
+    dev = _require_cuda(qkv, cos, sin, cache_position, keys, values, mask, q_norm_w, k_norm_w, out)
+    b = qkv.shape[0]
+    _, hkv, s, d = keys.shape
+    hq = (qkv.shape[1] - 2 * hkv * d) // d
+    for t, name in ((qkv, "qkv"), (keys, "keys"), (values, "values")):
+        if t.dtype != torch.bfloat16:
+            raise ValueError(f"{name} must be bf16")
+    if not keys.is_contiguous() or not values.is_contiguous():
+        raise ValueError("the KV caches must be contiguous (B, HKV, S, D)")
+    qkv = _rowmajor(qkv, "qkv")
+    cos2 = cos.reshape(cos.shape[0], -1).to(torch.bfloat16)
+    sin2 = sin.reshape(sin.shape[0], -1).to(torch.bfloat16)
+    if cos2.stride(1) != 1 or sin2.stride(1) != 1 or cos2.stride(0) != sin2.stride(0):
+        raise ValueError("cos / sin rows must be contiguous with equal strides")
+    if cache_position.dtype != torch.int64:
+        raise ValueError("cache_position must be int64")
+    if out is None:
+        out = torch.empty(b, hq * d, device=dev, dtype=torch.bfloat16)
+    out = _rowmajor(out, "out")
+    ad = AttnDesc()
+    ad.B, ad.HQ, ad.HKV, ad.D, ad.S = b, hq, hkv, d, s
+    ad.eps, ad.flags = eps, flags
+    ad.qkv, ad.ldqkv = qkv.data_ptr(), qkv.stride(0)
+    ad.cos, ad.sin = cos2.data_ptr(), sin2.data_ptr()
+    ad.ldcs = cos2.stride(0) if cos2.shape[0] == b else 0
+    ad.pos = cache_position.data_ptr()
+    ad.k_cache, ad.v_cache = keys.data_ptr(), values.data_ptr()
+    m2 = None
+    if mask is not None:
+        m2 = additive_mask(mask, b, s)
+        if m2.dtype not in (torch.bfloat16, torch.float32):
+            m2 = m2.float()
+        if m2.stride(1) != 1:
+            m2 = m2.contiguous()
+        ad.mask, ad.ldm = m2.data_ptr(), m2.stride(0)
+        ad.mask_dtype = _DT[m2.dtype]
+    if q_norm_w is not None:
+        ad.q_norm = q_norm_w.to(torch.bfloat16).data_ptr()
+        ad.k_norm = k_norm_w.to(torch.bfloat16).data_ptr()
+    ad.out, ad.ldo = out.data_ptr(), out.stride(0)
+    lib = load()
+    need = ctypes.c_size_t(0)
+    check(lib.bq_attention_workspace_bytes(ctypes.byref(ad), ctypes.byref(need)), "bq_attention_workspace_bytes")
+    ws = ATTN_WORKSPACE.get(dev, need.value)
+    check(lib.bq_attention_step(ctypes.byref(ad), ws.data_ptr(), ws.numel(), _stream(dev)), "bq_attention_step")
+    return out
 
 
 def dequant(w: torch.Tensor, wfmt: int, n: int, k: int, *, scale=None, group: int = 128) -> torch.Tensor:

@@ -124,6 +124,16 @@ def rms_gemv(x, fw: FusedWeight, norm_weight=None, eps: float = 1e-6, epilogue: 
                      out_dtype=torch.bfloat16 if residual is None else residual.dtype, flags=_lib.default_flags())
 
 
+def attention_step(qkv, cos, sin, cache_position, keys, values, mask, q_norm_w=None, k_norm_w=None, eps=1e-6,
+                   out=None, q_buf=None):  # noqa: ARG001 - q_buf: API parity (the kernel keeps q on chip)
+    """qkv (B, (HQ+2HKV)*D) bf16 -> attention output (B, HQ*D) bf16, with the
+    new k/v written into the static cache (B, HKV, S, D); same signature as
+    models/fused/kernels.py:505-536. One bq_attention_step launch replaces the
+    reference's three Triton kernels."""
+    return _lib.attention_step(qkv, cos, sin, cache_position, keys, values, mask, q_norm_w, k_norm_w, eps, out,
+                               flags=_lib.default_flags())
+
+
 def rmsnorm(x, w, eps=1e-6, out=None):
     """Standalone RMSNorm (models/fused/kernels.py:552-557)."""
     return _lib.rmsnorm(x, w, eps, out)

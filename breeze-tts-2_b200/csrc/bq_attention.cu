@@ -1,0 +1,387 @@
+// Decode attention step for sm_100a (bq_attention_step): per-head q/k RMSNorm,
+// RoPE, KV-cache write and split-sequence flash-decode with the combine
+// fused into the same launch (the last CTA of a (row, kv head) to finish
+// merges the splits, fixed order). Replaces qkv_rope_cache_kernel,
+// attn_decode_kernel and attn_combine_kernel (models/fused/kernels.py:376-536).
+//
+// Grid (splits, HKV, B), 128 threads. A CTA owns one kv head of one batch
+// row and a contiguous slice of the cache positions [0, pos]; it computes its
+// G = HQ / HKV query heads and the new k / v itself, so no CTA reads the
+// cache at `pos` before it is written (the split holding `pos` uses the new
+// values from registers and is the one that writes them back).
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+
+#include "bq_device.cuh"
+#include "bq_host.h"
+
+namespace bq {
+
+namespace {
+
+constexpr int kAttnThreads = 128;
+constexpr int kMaxG = 8;  // query heads per kv head
+
+struct AttnParams {
+    int32_t B, HQ, HKV, S, G, splits, mask_dtype, has_norm;
+    float eps, scale;
+    const __nv_bfloat16* qkv;
+    int64_t ldqkv;
+    const __nv_bfloat16* cos;
+    const __nv_bfloat16* sin;
+    int64_t ldcs;
+    const int64_t* pos;
+    __nv_bfloat16* kc;
+    __nv_bfloat16* vc;
+    const void* mask;
+    int64_t ldm;
+    const __nv_bfloat16* qn;
+    const __nv_bfloat16* kn;
+    __nv_bfloat16* out;
+    int64_t ldo;
+    unsigned int* counters;  // [B][HKV]
+    float* partials;         // [B][HKV][splits][G][D + 2]
+};
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Lane holds dims [lane * DPL, lane * DPL + DPL). Per-head RMSNorm (optional)
+// and RoPE with rotate_half: the partner of dim i is i +- D/2, held by
+// lane ^ 16.
+template <int DPL>
+__device__ __forceinline__ void norm_rope(float (&v)[DPL], const __nv_bfloat16* w, float eps, bool norm,
+                                          const float (&c)[DPL], const float (&s)[DPL], int lane) {
+    constexpr int D = 32 * DPL;
+    if (norm) {
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) ss += v[e] * v[e];
+        ss = warp_sum(ss);
+        const float inv = 1.0f / sqrtf(ss / float(D) + eps);
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) v[e] = v[e] * inv * __bfloat162float(w[lane * DPL + e]);
+    }
+    float rot[DPL];
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) {
+        const float partner = __shfl_xor_sync(0xffffffffu, v[e], 16);
+        rot[e] = lane < 16 ? -partner : partner;
+    }
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) v[e] = v[e] * c[e] + rot[e] * s[e];
+}
+
+template <int DPL>
+__device__ __forceinline__ void load_row(const __nv_bfloat16* p, float (&v)[DPL]) {
+    if constexpr (DPL == 4) {
+        const uint2 r = *reinterpret_cast<const uint2*>(p);
+        v[0] = __uint_as_float(r.x << 16);
+        v[1] = __uint_as_float(r.x & 0xFFFF0000u);
+        v[2] = __uint_as_float(r.y << 16);
+        v[3] = __uint_as_float(r.y & 0xFFFF0000u);
+    } else {
+        const uint32_t r = *reinterpret_cast<const uint32_t*>(p);
+        v[0] = __uint_as_float(r << 16);
+        v[1] = __uint_as_float(r & 0xFFFF0000u);
+    }
+}
+
+template <int DPL>
+__global__ void __launch_bounds__(kAttnThreads) attention_step_kernel(const AttnParams p) {
+    constexpr int D = 32 * DPL;
+    __shared__ float s_q[kMaxG][D];
+    __shared__ float s_k[D], s_v[D];
+    __shared__ float s_red[4][kMaxG][D + 2];
+    __shared__ unsigned int s_last;
+    const int sp = blockIdx.x, j = blockIdx.y, b = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = p.G;
+
+    pdl_launch_dependents();
+    pdl_wait();  // qkv comes from the preceding projection
+
+    const int64_t pos = *p.pos;
+    if (pos < 0 || pos >= p.S) {  // a position outside the cache: flag it, touch nothing
+        if (threadIdx.x == 0 && sp == 0 && j == 0 && b == 0) atomicOr(&g_device_error, BQ_DEVERR_POSITION_BIT);
+        return;
+    }
+    const int kv_len = int(pos) + 1;
+    const int per = (kv_len + p.splits - 1) / p.splits;
+    const int s_lo = sp * per, s_hi = min(s_lo + per, kv_len);
+    const bool holds_pos = pos >= s_lo && pos < s_hi;
+
+    float c[DPL], s[DPL];
+    {
+        const __nv_bfloat16* cp = p.cos + int64_t(b) * p.ldcs + lane * DPL;
+        const __nv_bfloat16* sn = p.sin + int64_t(b) * p.ldcs + lane * DPL;
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) {
+            c[e] = __bfloat162float(cp[e]);
+            s[e] = __bfloat162float(sn[e]);
+        }
+    }
+    const __nv_bfloat16* row = p.qkv + int64_t(b) * p.ldqkv;
+    // query heads of this kv head, scaled by D^-0.5 (kept in fp32, as the reference's q buffer)
+    for (int g = warp; g < G; g += 4) {
+        float v[DPL];
+        const __nv_bfloat16* q = row + (j * G + g) * D + lane * DPL;
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) v[e] = __bfloat162float(q[e]);
+        norm_rope<DPL>(v, p.qn, p.eps, p.has_norm, c, s, lane);
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) s_q[g][lane * DPL + e] = v[e] * p.scale;
+    }
+    // the new k (normed, roped, rounded to the cache dtype) and v
+    if (warp == 0) {
+        float v[DPL];
+        const __nv_bfloat16* k = row + (p.HQ + j) * D + lane * DPL;
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) v[e] = __bfloat162float(k[e]);
+        norm_rope<DPL>(v, p.kn, p.eps, p.has_norm, c, s, lane);
+        const __nv_bfloat16* vv = row + (p.HQ + p.HKV + j) * D + lane * DPL;
+        const int64_t at = ((int64_t(b) * p.HKV + j) * p.S + pos) * D + lane * DPL;
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) {
+            const __nv_bfloat16 kb = __float2bfloat16_rn(v[e]);
+            s_k[lane * DPL + e] = __bfloat162float(kb);
+            s_v[lane * DPL + e] = __bfloat162float(vv[e]);
+            if (holds_pos) {
+                p.kc[at + e] = kb;
+                p.vc[at + e] = vv[e];
+            }
+        }
+    }
+    __syncthreads();
+
+    // ---- online softmax over this split's positions; warp w takes s = s_lo + w (mod 4)
+    float qr[kMaxG][DPL], m[kMaxG], l[kMaxG], acc[kMaxG][DPL];
+#pragma unroll
+    for (int g = 0; g < kMaxG; ++g) {
+        m[g] = -1e30f;
+        l[g] = 0.f;
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) {
+            qr[g][e] = g < G ? s_q[g][lane * DPL + e] : 0.f;
+            acc[g][e] = 0.f;
+        }
+    }
+    const int64_t kv_base = (int64_t(b) * p.HKV + j) * p.S * D + lane * DPL;
+    for (int t = s_lo + warp; t < s_hi; t += 4) {
+        float kr[DPL], vr[DPL];
+        if (t == pos) {
+#pragma unroll
+            for (int e = 0; e < DPL; ++e) {
+                kr[e] = s_k[lane * DPL + e];
+                vr[e] = s_v[lane * DPL + e];
+            }
+        } else {
+            load_row<DPL>(p.kc + kv_base + int64_t(t) * D, kr);
+            load_row<DPL>(p.vc + kv_base + int64_t(t) * D, vr);
+        }
+        float mk = 0.f;
+        if (p.mask) {
+            mk = p.mask_dtype == BQ_DT_BF16
+                     ? __bfloat162float(static_cast<const __nv_bfloat16*>(p.mask)[int64_t(b) * p.ldm + t])
+                     : static_cast<const float*>(p.mask)[int64_t(b) * p.ldm + t];
+        }
+#pragma unroll
+        for (int g = 0; g < kMaxG; ++g) {
+            if (g >= G) break;
+            float d = 0.f;
+#pragma unroll
+            for (int e = 0; e < DPL; ++e) d = fmaf(qr[g][e], kr[e], d);
+            const float score = warp_sum(d) + mk;
+            const float m_new = fmaxf(m[g], score);
+            const float alpha = __expf(m[g] - m_new), pr = __expf(score - m_new);
+            l[g] = l[g] * alpha + pr;
+#pragma unroll
+            for (int e = 0; e < DPL; ++e) acc[g][e] = fmaf(acc[g][e], alpha, pr * vr[e]);
+            m[g] = m_new;
+        }
+    }
+    // ---- merge the 4 warps
+#pragma unroll
+    for (int g = 0; g < kMaxG; ++g) {
+        if (g >= G) break;
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) s_red[warp][g][lane * DPL + e] = acc[g][e];
+        if (lane == 0) {
+            s_red[warp][g][D] = m[g];
+            s_red[warp][g][D + 1] = l[g];
+        }
+    }
+    __syncthreads();
+    // thread t < G * D: (head g, dim d); fixed warp order
+    const float* red = &s_red[0][0][0];
+    constexpr int HS = kMaxG * (D + 2);  // stride between warps
+    for (int t = threadIdx.x; t < G * D; t += kAttnThreads) {
+        const int g = t / D, d = t - g * D;
+        float mm = -1e30f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) mm = fmaxf(mm, red[w * HS + g * (D + 2) + D]);
+        float ll = 0.f, aa = 0.f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const float f = __expf(red[w * HS + g * (D + 2) + D] - mm);
+            ll += red[w * HS + g * (D + 2) + D + 1] * f;
+            aa += red[w * HS + g * (D + 2) + d] * f;
+        }
+        if (p.splits == 1) {
+            p.out[int64_t(b) * p.ldo + (j * G + g) * D + d] = __float2bfloat16_rn(aa / ll);
+        } else {
+            float* part = p.partials + (((int64_t(b) * p.HKV + j) * p.splits + sp) * G + g) * (D + 2);
+            __stcg(part + d, aa);
+            if (d == 0) {
+                __stcg(part + D, mm);
+                __stcg(part + D + 1, ll);
+            }
+        }
+    }
+    if (p.splits == 1) return;
+    // ---- the last split to finish merges all splits (fixed order)
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned int old = atomicAdd(p.counters + b * p.HKV + j, 1u);
+        s_last = old == unsigned(p.splits - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const float* base = p.partials + ((int64_t(b) * p.HKV + j) * p.splits) * G * (D + 2);
+    for (int t = threadIdx.x; t < G * D; t += kAttnThreads) {
+        const int g = t / D, d = t - g * D;
+        float mm = -1e30f;
+        for (int q = 0; q < p.splits; ++q) mm = fmaxf(mm, __ldcg(base + (q * G + g) * (D + 2) + D));
+        float ll = 0.f, aa = 0.f;
+        for (int q = 0; q < p.splits; ++q) {
+            const float* pq = base + (q * G + g) * (D + 2);
+            const float f = __expf(__ldcg(pq + D) - mm);
+            ll += __ldcg(pq + D + 1) * f;
+            aa += __ldcg(pq + d) * f;
+        }
+        p.out[int64_t(b) * p.ldo + (j * G + g) * D + d] = __float2bfloat16_rn(aa / ll);
+    }
+    if (threadIdx.x == 0) atomicExch(p.counters + b * p.HKV + j, 0u);
+}
+
+int attn_splits(const bq_attn_desc* d, int sm_count) {
+    // enough CTAs to cover the SMs, each over >= 32 positions of the cache
+    const int items = d->B * d->HKV;
+    int sp = (2 * sm_count + items - 1) / items;
+    sp = std::min(sp, std::max(1, d->S / 32));
+    return std::max(1, std::min(sp, 32));
+}
+
+int validate_attn(const bq_attn_desc* d) {
+    if (!d) return set_error(BQ_ERR_INVALID_ARG, "desc is NULL");
+    if (d->B < 1 || d->HQ < 1 || d->HKV < 1 || d->S < 1)
+        return set_error(BQ_ERR_SHAPE, "B, HQ, HKV, S must be positive");
+    if (d->D != 64 && d->D != 128) return set_error(BQ_ERR_SHAPE, "head dim %d not supported (64 or 128)", d->D);
+    if (d->HQ % d->HKV || d->HQ / d->HKV > kMaxG)
+        return set_error(BQ_ERR_SHAPE, "HQ=%d must be a multiple of HKV=%d, at most %d query heads per kv head", d->HQ,
+                         d->HKV, kMaxG);
+    if (!d->qkv || !d->cos || !d->sin || !d->pos || !d->k_cache || !d->v_cache || !d->out)
+        return set_error(BQ_ERR_INVALID_ARG, "qkv, cos, sin, pos, caches and out must be non-NULL");
+    if ((d->q_norm == nullptr) != (d->k_norm == nullptr))
+        return set_error(BQ_ERR_INVALID_ARG, "q_norm and k_norm must be given together");
+    if (d->mask && d->mask_dtype != BQ_DT_BF16 && d->mask_dtype != BQ_DT_F32)
+        return set_error(BQ_ERR_INVALID_ARG, "mask must be bf16 or f32 (additive)");
+    const int vec = d->D / 32 * 2;  // bytes per lane of a row
+    if ((reinterpret_cast<uintptr_t>(d->k_cache) | reinterpret_cast<uintptr_t>(d->v_cache)) % vec)
+        return set_error(BQ_ERR_ALIGN, "caches must be %d-byte aligned", vec);
+    if (d->ldqkv < int64_t(d->HQ + 2 * d->HKV) * d->D) return set_error(BQ_ERR_SHAPE, "ldqkv too small");
+    if (d->ldo < int64_t(d->HQ) * d->D) return set_error(BQ_ERR_SHAPE, "ldo too small");
+    return BQ_OK;
+}
+
+}  // namespace
+
+}  // namespace bq
+
+using namespace bq;
+
+extern "C" {
+
+int32_t bq_attention_workspace_bytes(const bq_attn_desc* d, size_t* bytes) {
+    if (!bytes) return set_error(BQ_ERR_INVALID_ARG, "bytes is NULL");
+    int rc = validate_attn(d);
+    if (rc) return rc;
+    const DeviceInfo* dev = device_info();
+    if (!dev) return BQ_ERR_CUDA;
+    const int sp = attn_splits(d, dev->sm_count);
+    const int G = d->HQ / d->HKV;
+    const size_t counters = (size_t(d->B) * d->HKV * 4 + 255) / 256 * 256;
+    *bytes = sp == 1 ? 0 : counters + size_t(d->B) * d->HKV * sp * G * (d->D + 2) * 4;
+    return BQ_OK;
+}
+
+int32_t bq_attention_step(const bq_attn_desc* d, void* workspace, size_t workspace_bytes, void* stream) {
+    int rc = validate_attn(d);
+    if (rc) return rc;
+    const DeviceInfo* dev = device_info();
+    if (!dev) return BQ_ERR_CUDA;
+    if (dev->major != 10) return set_error(BQ_ERR_DEVICE, "sm_%d%d device: this library is built for sm_100a", dev->major, dev->minor);
+    AttnParams p;
+    std::memset(&p, 0, sizeof(p));
+    p.B = d->B;
+    p.HQ = d->HQ;
+    p.HKV = d->HKV;
+    p.S = d->S;
+    p.G = d->HQ / d->HKV;
+    p.splits = attn_splits(d, dev->sm_count);
+    p.mask_dtype = d->mask_dtype;
+    p.has_norm = d->q_norm != nullptr;
+    p.eps = d->eps;
+    p.scale = 1.0f / sqrtf(float(d->D));
+    p.qkv = static_cast<const __nv_bfloat16*>(d->qkv);
+    p.ldqkv = d->ldqkv;
+    p.cos = static_cast<const __nv_bfloat16*>(d->cos);
+    p.sin = static_cast<const __nv_bfloat16*>(d->sin);
+    p.ldcs = d->ldcs;
+    p.pos = d->pos;
+    p.kc = static_cast<__nv_bfloat16*>(d->k_cache);
+    p.vc = static_cast<__nv_bfloat16*>(d->v_cache);
+    p.mask = d->mask;
+    p.ldm = d->ldm;
+    p.qn = static_cast<const __nv_bfloat16*>(d->q_norm);
+    p.kn = static_cast<const __nv_bfloat16*>(d->k_norm);
+    p.out = static_cast<__nv_bfloat16*>(d->out);
+    p.ldo = d->ldo;
+    if (p.splits > 1) {
+        const size_t counters = (size_t(d->B) * d->HKV * 4 + 255) / 256 * 256;
+        const size_t need = counters + size_t(d->B) * d->HKV * p.splits * p.G * (d->D + 2) * 4;
+        if (!workspace || workspace_bytes < need)
+            return set_error(BQ_ERR_WORKSPACE, "attention workspace of %zu bytes given, %zu needed", workspace_bytes, need);
+        if (reinterpret_cast<uintptr_t>(workspace) & 255) return set_error(BQ_ERR_ALIGN, "workspace must be 256-byte aligned");
+        p.counters = static_cast<unsigned int*>(workspace);
+        p.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + counters);
+    }
+    const void* fn = d->D == 128 ? reinterpret_cast<const void*>(&attention_step_kernel<4>)
+                                 : reinterpret_cast<const void*>(&attention_step_kernel<2>);
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(p.splits, d->HKV, d->B);
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    if (d->flags & BQ_FLAG_PDL) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    void* args[] = {&p};
+    cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
+    if (e != cudaSuccess) return set_error(BQ_ERR_CUDA, "attention launch failed: %s", cudaGetErrorString(e));
+    return BQ_OK;
+}
+
+}  // extern "C"

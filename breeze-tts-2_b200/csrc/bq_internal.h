@@ -7,6 +7,7 @@
 #include "breeze_b200.h"
 
 #define BQ_DEVERR_WAIT_TIMEOUT_BIT 1u
+#define BQ_DEVERR_POSITION_BIT 2u
 
 namespace bq {
 

@@ -51,7 +51,8 @@ extern "C" {
 #define BQ_ERR_DEVICE -7       /* device is not sm_100 (B200 class)            */
 
 /* Device-side error bits, read with bq_device_status(). */
-#define BQ_DEVERR_WAIT_TIMEOUT 1u /* a bounded mbarrier wait gave up */
+#define BQ_DEVERR_WAIT_TIMEOUT 1u /* a bounded device wait gave up */
+#define BQ_DEVERR_POSITION 2u     /* bq_attention_step saw a cache position outside [0, S) */
 
 /* ---- enums --------------------------------------------------------------- */
 /* Weight formats. */
@@ -152,6 +153,41 @@ int32_t bq_gemv_chain_workspace_bytes(const bq_gemv_desc* descs, int32_t n, size
 int32_t bq_gemv_chain_prepare(const bq_gemv_desc* descs, int32_t n, void* workspace, size_t workspace_bytes);
 int32_t bq_gemv_chain_launch(const bq_gemv_desc* descs, int32_t n, void* workspace, size_t workspace_bytes,
                              void* stream);
+
+/* ---- decode attention step --------------------------------------------- */
+/* One decode step of attention for a static KV cache: per-head RMSNorm of q
+ * and k (when q_norm / k_norm are given), RoPE (rotate_half), the new k and v
+ * written into the caches at *pos, then softmax((q * D^-0.5) k^T + mask) v
+ * over cache positions [0, *pos] with grouped-query heads (q head h reads kv
+ * head h / (HQ / HKV)). Replaces attention_step and its three Triton
+ * kernels (models/fused/kernels.py:376-536), called from
+ * FusedDecoderLayer.forward (models/fused/layer.py:89-90). */
+typedef struct bq_attn_desc {
+    int32_t B, HQ, HKV, D, S;   /* batch rows, q heads, kv heads, head dim (64 or 128), cache length */
+    int32_t mask_dtype;         /* BQ_DT_BF16 or BQ_DT_F32; additive (B, S) mask, may be NULL */
+    float eps;                  /* RMSNorm epsilon */
+    uint32_t flags;             /* BQ_FLAG_PDL */
+    const void* qkv;            /* (B, (HQ + 2 HKV) D) bf16: [q heads | k heads | v heads] */
+    int64_t ldqkv;
+    const void* cos;            /* (B or 1, D) bf16 */
+    const void* sin;
+    int64_t ldcs;               /* row stride of cos / sin; 0 broadcasts one row */
+    const int64_t* pos;         /* device pointer to the cache position */
+    void* k_cache;              /* (B, HKV, S, D) bf16, written at pos */
+    void* v_cache;
+    const void* mask;
+    int64_t ldm;
+    const void* q_norm;         /* (D) bf16 or NULL */
+    const void* k_norm;
+    void* out;                  /* (B, HQ D) bf16 */
+    int64_t ldo;
+} bq_attn_desc;
+
+/* The workspace (256-byte aligned) starts with arrival counters that the
+ * kernel leaves at zero; do not share it with bq_gemv's workspace, whose own
+ * counters must stay zero between calls. */
+int32_t bq_attention_workspace_bytes(const bq_attn_desc* desc, size_t* bytes);
+int32_t bq_attention_step(const bq_attn_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- layouts and dequantization ---------------------------------------- */
 /* (N, K/2) uint8 odd-k-low -> tinygemm int32 [N/8, K/(16*ikt), 32, ikt/2].

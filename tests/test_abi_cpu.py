@@ -115,3 +115,21 @@ def test_no_cpu_fallback():
     w = torch.randn(64, 256, dtype=torch.bfloat16)
     with pytest.raises(RuntimeError, match="CUDA"):
         _lib.gemv(x, w, _lib.W_BF16, 64)
+
+
+def test_attention_desc_validation_without_gpu(lib):
+    """Host-side validation of bq_attention_step needs no GPU."""
+    import ctypes
+
+    from breeze_b200 import _lib as L
+
+    d = L.AttnDesc()
+    need = ctypes.c_size_t(0)
+    assert lib.bq_attention_workspace_bytes(ctypes.byref(d), ctypes.byref(need)) == L.BQ_ERR_SHAPE
+    d.B, d.HQ, d.HKV, d.D, d.S = 1, 16, 16, 96, 64
+    assert lib.bq_attention_workspace_bytes(ctypes.byref(d), ctypes.byref(need)) == L.BQ_ERR_SHAPE
+    assert b"head dim" in lib.bq_last_error_string()
+    d.D, d.HKV = 128, 3
+    assert lib.bq_attention_workspace_bytes(ctypes.byref(d), ctypes.byref(need)) == L.BQ_ERR_SHAPE
+    d.HKV = 16
+    assert lib.bq_attention_step(ctypes.byref(d), None, 0, None) == L.BQ_ERR_INVALID_ARG

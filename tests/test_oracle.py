@@ -157,3 +157,37 @@ def test_oracle_detects_a_planted_layout_bug(golden):
     src = torch.from_numpy(d["in_16_256_8"])
     swapped = ((src & 15) << 4) | (src >> 4)
     assert not (quant.tinygemm_pack(swapped, 8).numpy() == d["out_16_256_8"]).all()
+
+
+# ---------------------------------------------------------------- attention
+def _attn_case(golden, tag):
+    d = golden("attention_step.npz")
+    bf = torch.bfloat16
+    B, HQ, HKV, D, S = (int(v) for v in d[f"shape_{tag}"])
+    return dict(
+        qkv=from_bits(d[f"qkv_{tag}"], bf), k=from_bits(d[f"k_{tag}"], bf), v=from_bits(d[f"v_{tag}"], bf),
+        qn=from_bits(d[f"qn_{tag}"], bf), kn=from_bits(d[f"kn_{tag}"], bf), cos=from_bits(d[f"cos_{tag}"], bf),
+        sin=from_bits(d[f"sin_{tag}"], bf), mask=from_bits(d[f"mask_{tag}"], bf), pos=int(d[f"pos_{tag}"][0]),
+        out=from_bits(d[f"out_{tag}"], bf), k_after=from_bits(d[f"k_after_{tag}"], bf),
+        v_after=from_bits(d[f"v_after_{tag}"], bf), shape=(B, HQ, HKV, D, S))
+
+
+@pytest.mark.parametrize("tag", ["c0", "c1"])
+def test_attention_step_matches_reference(golden, tag):
+    """The oracle against the reference's Triton attention_step recorded on a
+    B200 (one split at S=64, eight splits at S=320, a padded row)."""
+    from oracle import attention
+
+    c = _attn_case(golden, tag)
+    keys, values = c["k"].clone(), c["v"].clone()
+    out, keys, values = attention.attention_step(c["qkv"], c["cos"], c["sin"], c["pos"], keys, values, c["mask"],
+                                                 c["qn"], c["kn"], 1e-6)
+    # cache writes: v copied exactly, k within one bf16 ulp (fp32 sum order)
+    assert torch.equal(values[:, :, c["pos"]], c["v_after"])
+    kd = (keys[:, :, c["pos"]].float() - c["k_after"].float()).abs()
+    assert (kd <= c["k_after"].float().abs() * 2 ** -7 + 1e-6).all()
+    assert gemv.max_rel_err(out.float(), c["out"].float()) < 1e-2
+    # every other cache position is untouched
+    other = torch.ones(keys.shape[2], dtype=torch.bool)
+    other[c["pos"]] = False
+    assert torch.equal(keys[:, :, other], c["k"][:, :, other])
