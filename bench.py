@@ -267,9 +267,10 @@ def decode_step_bench(device, world: int, local_rank: int, replays: int = 10, wa
         layers, head, ln_f = synthetic_stack(fmt, DECODE_LAYERS, device, seed=7)
         for rows in DECODE_ROWS:
             entry = {"format": fmt, "rows": rows}
-            for mode in ("per_op", "chain"):
+            for mode in ("per_op", "chain", "attn"):
                 try:
-                    st = DecodeStack(layers, head, ln_f, rows=rows, chain=(mode == "chain"))
+                    st = DecodeStack(layers, head, ln_f, rows=rows, chain=(mode == "chain"),
+                                     attention=(mode == "attn"))
                 except (RuntimeError, ValueError) as e:  # chain limits (rows per pass) are reported, not hidden
                     entry[mode] = {"unavailable": str(e)[:160]}
                     continue
@@ -297,7 +298,7 @@ def decode_step_bench(device, world: int, local_rank: int, replays: int = 10, wa
                 step_us = float(t.item()) * 1e3
                 wb = st.weight_bytes
                 entry[mode] = {"step_us": round(step_us, 1), "us_per_row": round(step_us / rows, 2),
-                               "GBps": round(wb / step_us / 1e3, 1), "launches": st.launches,
+                               "GBps": round((wb + st.kv_bytes) / step_us / 1e3, 1), "launches": st.launches,
                                "finite": bool(torch.isfinite(st.logits).all().item())}
                 entry["weight_bytes"] = wb
                 del st
@@ -307,7 +308,8 @@ def decode_step_bench(device, world: int, local_rank: int, replays: int = 10, wa
     return {"what": f"{DECODE_LAYERS} layers x (QKV 2048->6144 +RMSNorm, O 2048->2048 +residual, "
                     "gate+up 2048->16384 +RMSNorm +SiLU*up, down 8192->2048 +residual) + head 2048->8192 "
                     "+RMSNorm (fp32 logits); per_op = one CUDA graph of 113 bq_gemv launches with PDL, chain = "
-                    "one cooperative bq_gemv_chain launch",
+                    "one cooperative bq_gemv_chain launch, attn = per_op plus the decode attention step per layer "
+                    "(16 q / 16 kv heads of 128, kv_len 256; 141 launches)",
             "launches_per_step": 4 * DECODE_LAYERS + 1, "replays_timed": replays,
             "l2_policy": "weights 1-1.9 GB per step >> L2", "results": results}
 

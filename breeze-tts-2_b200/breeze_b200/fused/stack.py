@@ -10,9 +10,11 @@ Per decoder layer, in the order of the reference's FusedDecoderLayer.forward
 
 then the output head ``logits = rms_gemv(x, Whead, ln_f)`` in fp32 (the
 reference keeps its output heads in fp32, cudagraph/backbone_graph.py:70).
-``attn`` is the attention output; this chain has no attention kernel, so the
-first ``attn_cols`` columns of ``qkv`` (the query block) stand in for it,
-which keeps the data dependency QKV -> O of the real step.
+``attn`` is the attention output: with ``attention=True`` each layer runs the
+decode attention step (bq_attention_step: q/k RMSNorm, RoPE, KV-cache write,
+flash-decode over the cache) between QKV and O, as FusedDecoderLayer does
+(layer.py:89-90); otherwise the first ``attn_cols`` columns of ``qkv`` (the
+query block) stand in for it, which keeps the QKV -> O data dependency.
 
 Every projection is one bq_gemv launch (int4 tinygemm / plain, fp8 or int8
 weight-only, bf16), launched with programmatic dependent launch so each
@@ -113,6 +115,8 @@ class DecodeLayer:
     wd: QWeight
     ln1: torch.Tensor
     ln2: torch.Tensor
+    q_norm: torch.Tensor | None = None  # per-head RMSNorm weights (head_dim), as Qwen3 attention
+    k_norm: torch.Tensor | None = None
 
 
 def synthetic_stack(fmt: str, n_layers: int, device, seed: int = 0, hidden: int = 2048, qkv: int = 6144,
@@ -121,15 +125,16 @@ def synthetic_stack(fmt: str, n_layers: int, device, seed: int = 0, hidden: int 
     gate+up hidden->2*inter, down inter->hidden, plus the output head."""
     gen = torch.Generator(device=device).manual_seed(seed)
 
-    def norm_w():
-        return (1 + 0.1 * torch.randn(hidden, device=device, generator=gen)).to(torch.bfloat16)
+    def norm_w(n=hidden):
+        return (1 + 0.1 * torch.randn(n, device=device, generator=gen)).to(torch.bfloat16)
 
     layers = []
     for _ in range(n_layers):
         layers.append(DecodeLayer(synthetic_weight(fmt, qkv, hidden, device, gen),
                                   synthetic_weight(fmt, hidden, hidden, device, gen),
                                   synthetic_weight(fmt, 2 * inter, hidden, device, gen),
-                                  synthetic_weight(fmt, hidden, inter, device, gen), norm_w(), norm_w()))
+                                  synthetic_weight(fmt, hidden, inter, device, gen), norm_w(), norm_w(),
+                                  norm_w(128), norm_w(128)))
     return layers, synthetic_weight(fmt, head, hidden, device, gen), norm_w()
 
 
@@ -143,7 +148,8 @@ class DecodeStack:
     """
 
     def __init__(self, layers: list[DecodeLayer], head: QWeight, ln_f: torch.Tensor, rows: int,
-                 eps: float = 1e-6, attn_cols: int | None = None, chain: bool = False):
+                 eps: float = 1e-6, attn_cols: int | None = None, chain: bool = False, attention: bool = False,
+                 head_dim: int = 128, kv_heads: int | None = None, kv_len: int = 256):
         if not layers:
             raise ValueError("DecodeStack needs at least one layer")
         dev = layers[0].wqkv.w.device
@@ -169,6 +175,22 @@ class DecodeStack:
         self.logits = torch.zeros(rows, head.N, device=dev, dtype=torch.float32)
         self.graph = None
         self.chain = None
+        self.attention = attention
+        if attention:
+            if chain:
+                raise ValueError("the decode chain runs GEMVs only; attention=True needs chain=False")
+            hq = self.attn_cols // head_dim
+            hkv = kv_heads or (layers[0].wqkv.N // head_dim - hq) // 2
+            if (hq + 2 * hkv) * head_dim != layers[0].wqkv.N:
+                raise ValueError("QKV width does not split into q / k / v heads of head_dim")
+            self.hq, self.hkv, self.head_dim, self.kv_len = hq, hkv, head_dim, kv_len
+            cache = dict(device=dev, dtype=torch.bfloat16)
+            self.k_cache = [torch.zeros(rows, hkv, kv_len, head_dim, **cache) for _ in layers]
+            self.v_cache = [torch.zeros(rows, hkv, kv_len, head_dim, **cache) for _ in layers]
+            self.cos = torch.ones(rows, 1, head_dim, **cache)
+            self.sin = torch.zeros(rows, 1, head_dim, **cache)
+            self.pos = torch.full((1,), kv_len - 1, device=dev, dtype=torch.int64)  # attend over the whole cache
+            self.attn_out = torch.zeros(rows, hq * head_dim, **bf)
         if chain:
             descs = [_lib.gemv_desc(x, qw.w, qw.wfmt, qw.N, out=out, scale=qw.scale, group=qw.group, gamma=g,
                                     eps=eps, epilogue=epi, residual=res, flags=_lib.default_flags())
@@ -183,8 +205,17 @@ class DecodeStack:
         return b
 
     @property
+    def kv_bytes(self) -> int:
+        """KV-cache bytes the attention steps read per decode step."""
+        if not self.attention:
+            return 0
+        return len(self.layers) * 2 * self.rows * self.hkv * (int(self.pos.item()) + 1) * self.head_dim * 2
+
+    @property
     def launches(self) -> int:
-        return 1 if self.chain is not None else 4 * len(self.layers) + 1
+        if self.chain is not None:
+            return 1
+        return (5 if self.attention else 4) * len(self.layers) + 1
 
     def _ops(self):
         """(x, weight, out, gamma, epilogue, residual) of every launch, in order."""
@@ -203,12 +234,21 @@ class DecodeStack:
         return ops
 
     def run(self) -> torch.Tensor:
-        """Enqueue the step: one bq_gemv launch per projection, or the whole
+        """Enqueue the step: one bq_gemv launch per projection (and one
+        bq_attention_step per layer with ``attention=True``), or the whole
         step as one decode-chain launch (``chain=True``)."""
         if self.chain is not None:
             self.chain.launch()
             return self.logits
-        for x, qw, out, gamma, epi, res in self._ops():
+        ops = self._ops()
+        for k, (x, qw, out, gamma, epi, res) in enumerate(ops):
+            if self.attention and k % 4 == 1 and k < 4 * len(self.layers):
+                li = k // 4
+                l = self.layers[li]
+                _lib.attention_step(self.qkv[:, : l.wqkv.N], self.cos, self.sin, self.pos, self.k_cache[li],
+                                    self.v_cache[li], None, l.q_norm, l.k_norm, self.eps, out=self.attn_out,
+                                    flags=_lib.default_flags())
+                x = self.attn_out
             _lib.gemv(x, qw.w, qw.wfmt, qw.N, scale=qw.scale, group=qw.group, gamma=gamma, eps=self.eps,
                       epilogue=epi, residual=res, out=out, flags=_lib.default_flags())
         return self.logits

@@ -104,6 +104,22 @@ __global__ void __launch_bounds__(kAttnThreads) attention_step_kernel(const Attn
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = p.G;
 
+    // Before the dependent-launch wait: pull this CTA's slice of the caches into
+    // L2 (positions before the current one do not depend on the preceding
+    // kernel). The position read here is only a hint; it is read again below.
+    if (threadIdx.x == 0) {
+        const int64_t hint = *reinterpret_cast<const volatile int64_t*>(p.pos);
+        if (hint >= 0 && hint < p.S) {
+            const int len = int(hint) + 1, per0 = (len + p.splits - 1) / p.splits;
+            const int lo = sp * per0, hi = min(lo + per0, len);
+            if (hi > lo) {
+                const int64_t base = ((int64_t(b) * p.HKV + j) * p.S + lo) * D;
+                const uint32_t bytes = uint32_t(hi - lo) * D * 2;
+                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.kc + base), "r"(bytes) : "memory");
+                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.vc + base), "r"(bytes) : "memory");
+            }
+        }
+    }
     pdl_launch_dependents();
     pdl_wait();  // qkv comes from the preceding projection
 
@@ -173,37 +189,72 @@ __global__ void __launch_bounds__(kAttnThreads) attention_step_kernel(const Attn
         }
     }
     const int64_t kv_base = (int64_t(b) * p.HKV + j) * p.S * D + lane * DPL;
-    for (int t = s_lo + warp; t < s_hi; t += 4) {
-        float kr[DPL], vr[DPL];
-        if (t == pos) {
+    // Batches of PB positions per warp (warp w takes s_lo + w + 4 * (PB * it + i)):
+    // all k / v rows of a batch are loaded before any is used, then one
+    // online-softmax update per head covers the batch.
+    constexpr int PB = 4;
+    for (int t0 = s_lo + warp; t0 < s_hi; t0 += 4 * PB) {
+        float kr[PB][DPL], vr[PB][DPL], mk[PB];
+        bool ok[PB];
 #pragma unroll
-            for (int e = 0; e < DPL; ++e) {
-                kr[e] = s_k[lane * DPL + e];
-                vr[e] = s_v[lane * DPL + e];
+        for (int i = 0; i < PB; ++i) {
+            const int t = t0 + 4 * i;
+            ok[i] = t < s_hi;
+            const int tt = ok[i] ? t : t0;  // a row that exists; its result is discarded
+            if (tt == pos) {
+#pragma unroll
+                for (int e = 0; e < DPL; ++e) {
+                    kr[i][e] = s_k[lane * DPL + e];
+                    vr[i][e] = s_v[lane * DPL + e];
+                }
+            } else {
+                load_row<DPL>(p.kc + kv_base + int64_t(tt) * D, kr[i]);
+                load_row<DPL>(p.vc + kv_base + int64_t(tt) * D, vr[i]);
             }
-        } else {
-            load_row<DPL>(p.kc + kv_base + int64_t(t) * D, kr);
-            load_row<DPL>(p.vc + kv_base + int64_t(t) * D, vr);
-        }
-        float mk = 0.f;
-        if (p.mask) {
-            mk = p.mask_dtype == BQ_DT_BF16
-                     ? __bfloat162float(static_cast<const __nv_bfloat16*>(p.mask)[int64_t(b) * p.ldm + t])
-                     : static_cast<const float*>(p.mask)[int64_t(b) * p.ldm + t];
+            mk[i] = 0.f;
+            if (p.mask) {
+                mk[i] = p.mask_dtype == BQ_DT_BF16
+                            ? __bfloat162float(static_cast<const __nv_bfloat16*>(p.mask)[int64_t(b) * p.ldm + tt])
+                            : static_cast<const float*>(p.mask)[int64_t(b) * p.ldm + tt];
+            }
         }
 #pragma unroll
         for (int g = 0; g < kMaxG; ++g) {
             if (g >= G) break;
-            float d = 0.f;
+            float sc[PB];
 #pragma unroll
-            for (int e = 0; e < DPL; ++e) d = fmaf(qr[g][e], kr[e], d);
-            const float score = warp_sum(d) + mk;
-            const float m_new = fmaxf(m[g], score);
-            const float alpha = __expf(m[g] - m_new), pr = __expf(score - m_new);
-            l[g] = l[g] * alpha + pr;
+            for (int i = 0; i < PB; ++i) {
+                float d = 0.f;
 #pragma unroll
-            for (int e = 0; e < DPL; ++e) acc[g][e] = fmaf(acc[g][e], alpha, pr * vr[e]);
-            m[g] = m_new;
+                for (int e = 0; e < DPL; ++e) d = fmaf(qr[g][e], kr[i][e], d);
+                sc[i] = d;
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1)
+#pragma unroll
+                for (int i = 0; i < PB; ++i) sc[i] += __shfl_xor_sync(0xffffffffu, sc[i], o);
+            float bm = m[g];
+#pragma unroll
+            for (int i = 0; i < PB; ++i) {
+                sc[i] = ok[i] ? sc[i] + mk[i] : -1e30f;
+                bm = fmaxf(bm, sc[i]);
+            }
+            const float alpha = __expf(m[g] - bm);
+            float ls = l[g] * alpha;
+            float a2[DPL];
+#pragma unroll
+            for (int e = 0; e < DPL; ++e) a2[e] = acc[g][e] * alpha;
+#pragma unroll
+            for (int i = 0; i < PB; ++i) {
+                const float pr = ok[i] ? __expf(sc[i] - bm) : 0.f;
+                ls += pr;
+#pragma unroll
+                for (int e = 0; e < DPL; ++e) a2[e] = fmaf(pr, vr[i][e], a2[e]);
+            }
+            l[g] = ls;
+#pragma unroll
+            for (int e = 0; e < DPL; ++e) acc[g][e] = a2[e];
+            m[g] = bm;
         }
     }
     // ---- merge the 4 warps

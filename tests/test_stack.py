@@ -155,3 +155,34 @@ def test_chain_full_size_layer_matches_per_op(fmt):
     b.run()
     torch.cuda.synchronize()
     assert og.max_rel_err(b.logits.cpu(), a.logits.cpu().float()) < TOL
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("rows", [1, 2])
+def test_stack_with_attention_matches_oracle(rows):
+    """attention=True: the attention step sits between QKV and O; its output
+    matches the oracle on the QKV output and the caches it read, and O, gate+up,
+    down and the head still match stage by stage."""
+    from oracle import attention as oa
+
+    S = _stack()
+    dev = torch.device("cuda", 0)
+    layers, head, ln_f = _small("int4", dev)
+    st = S.DecodeStack(layers, head, ln_f, rows=rows, attention=True, kv_len=64)
+    assert (st.hq, st.hkv) == (2, 2) and st.launches == 11
+    g = torch.Generator().manual_seed(9)
+    st.x.copy_(torch.randn(rows, 256, generator=g).to(torch.bfloat16))
+    for c in st.k_cache + st.v_cache:
+        c.copy_((torch.randn(c.shape, generator=g) * 0.5).to(torch.bfloat16))
+    k_before = [c.cpu() for c in st.k_cache]
+    v_before = [c.cpu() for c in st.v_cache]
+    st.pos.fill_(40)
+    st.run()
+    torch.cuda.synchronize()
+    l = layers[1]
+    ref, _, _ = oa.attention_step(st.qkv.cpu(), st.cos.cpu(), st.sin.cpu(), 40, k_before[1].clone(),
+                                  v_before[1].clone(), torch.zeros(rows, 64), l.q_norm.cpu(), l.k_norm.cpu(), 1e-6)
+    assert og.max_rel_err(st.attn_out.cpu().float(), ref.float()) < TOL
+    _check("o", st.h, st.attn_out, l.wo, epilogue=2, residual=st.res[0])
+    _check("gate_up", st.act, st.h, l.wgu, gamma=l.ln2, epilogue=1)
+    _check("head", st.logits, st.res[1], head, gamma=ln_f)
