@@ -110,7 +110,7 @@ int plan_chain(const bq_gemv_desc* descs, int n, ChainPlan* cp) {
         const uint32_t smem_misc = align_up(smem_part + part_max, 16);
         for (int i = 0; i < n && ok; ++i) {
             Gemv3Plan& pl = cp->ops[i];
-            const int ugm = (pl.mt * pl.tpu >= 4) ? 2 : 4;
+            const int ugm = 1;  // kernel ug_max()
             const int kps = pl.mt == 1 ? 2 : 1;
             const int nkp = (pl.nkbw + kps - 1) / kps;
             int ug = std::min(ugm, pl.upc), rs = 0;

@@ -108,10 +108,12 @@ struct Fmt3<BQ_W_INT8> {
     static constexpr bool kInt4 = false, kF16 = true;
 };
 
-// Units per ring slot at most: keeps the accumulators at <= 32 registers.
+// Units per ring slot at most. One: every launch runs this code cold (each
+// warp walks it about once per call), so instruction fetch, not arithmetic,
+// is what unrolled copies of the slot body cost.
 template <int MT, int TPU>
 constexpr int ug_max() {
-    return (MT * TPU >= 4) ? 2 : 4;
+    return 1;
 }
 
 __device__ __forceinline__ float bf16lo(uint32_t u) { return __uint_as_float(u << 16); }

@@ -89,7 +89,7 @@ int plan_gemv3(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int slots) {
     }
     if (upc_need > 4) return set_error(BQ_ERR_SHAPE, "internal: %d units per CTA", upc_need);
     P.upc = upc_need;
-    const int ugm = (P.mt * P.tpu >= 4) ? 2 : 4;
+    const int ugm = 1;  // kernel ug_max()
     const int kps = P.mt == 1 ? 2 : 1;             // k-blocks per ring slot (kernel's KPS)
     const int nkp = (P.nkbw + kps - 1) / kps;      // ring slots per unit group and warp
     const uint32_t x_bytes = uint32_t(8 * (rows * P.xrow_pitch + 256));  // + one zero k-block per warp
