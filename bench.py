@@ -251,6 +251,7 @@ def run_ours(args, rank, local_rank, world):
 
 DECODE_FORMATS = ("int4", "fp8", "int8")
 DECODE_ROWS = (1, 2, 4, 8, 16)
+DECODE_ROWS_INT4 = (1, 2, 4, 8, 16, 32, 64)  # config 4 adds 32 and 64 concurrent streams per GPU
 DECODE_LAYERS = 28
 
 
@@ -265,9 +266,12 @@ def decode_step_bench(device, world: int, local_rank: int, replays: int = 10, wa
     cur = torch.cuda.current_stream(device)
     for fmt in DECODE_FORMATS:
         layers, head, ln_f = synthetic_stack(fmt, DECODE_LAYERS, device, seed=7)
-        for rows in DECODE_ROWS:
+        for rows in (DECODE_ROWS_INT4 if fmt == "int4" else DECODE_ROWS):
             entry = {"format": fmt, "rows": rows}
             for mode in ("per_op", "chain", "attn"):
+                if mode == "chain" and rows > 16:
+                    entry[mode] = {"unavailable": "the chain takes at most 16 rows"}
+                    continue
                 try:
                     st = DecodeStack(layers, head, ln_f, rows=rows, chain=(mode == "chain"),
                                      attention=(mode == "attn"))
@@ -298,6 +302,7 @@ def decode_step_bench(device, world: int, local_rank: int, replays: int = 10, wa
                 step_us = float(t.item()) * 1e3
                 wb = st.weight_bytes
                 entry[mode] = {"step_us": round(step_us, 1), "us_per_row": round(step_us / rows, 2),
+                               "tokens_per_s_all_gpus": round(world * rows / step_us * 1e6, 1),
                                "GBps": round((wb + st.kv_bytes) / step_us / 1e3, 1), "launches": st.launches,
                                "finite": bool(torch.isfinite(st.logits).all().item())}
                 entry["weight_bytes"] = wb

@@ -53,6 +53,7 @@ struct Gemv3Params {
     int32_t p_max;       // split mode: partial slots per unit
     int32_t xrow_pitch;  // bytes per staged activation row (per warp)
     int32_t x_bulk;      // bf16 x with 16-byte aligned rows: staged with 16-byte loads
+    int32_t res_bulk;    // residual rows 16-byte aligned: copied with 16-byte cp.async
     int32_t upc;         // most units any CTA covers
     int32_t group_shift; // log2(group) for int4
     uint32_t smem_ring, smem_x, smem_xsum, smem_gamma, smem_part, smem_misc;
@@ -71,7 +72,8 @@ struct Gemv3Params {
 };
 
 // Misc area: floats ss[8][16], up[8][16], rowscale[4*32], rowbias[4*32],
-// then 8 warps x 16 zero bytes, then the residual rows res[upc*32][M].
+// then 8 warps x 16 zero bytes, then the residual rows as stored in memory
+// (res_dtype): [M][upc*32] elements, at most 4 bytes each.
 constexpr int kMiscFixedBytes = (8 * 16 + 8 * 16 + 128 + 128) * 4 + 8 * 16;
 constexpr int misc3_bytes(int upc, int rows) { return kMiscFixedBytes + upc * 32 * rows * 4; }
 constexpr int kConsumerThreads = 256;
@@ -151,10 +153,11 @@ constexpr int kPhPdl = 4;      // programmatic-dependent-launch trigger and wait
 constexpr int kPhRun = 8;      // activations, staging, main loop, partials (ends in a block barrier)
 constexpr int kPhEpi = 16;     // cross-warp reduction, norm factor, epilogue, stores
 constexpr int kPhRing = 32;    // with kPhPrefill: also issue the first ring slots
+constexpr int kPhStatic = 64;  // per-row scale / bias and zero blocks into shared memory
 // The first ring slots go out before the dependent-launch wait: issuing them
 // costs ~1 us of load/store-path instructions per warp, which the previous
 // kernel's run hides (issued after the wait, they sit on the critical path).
-constexpr int kPhAll = kPhL2 | kPhPrefill | kPhRing | kPhPdl | kPhRun | kPhEpi;
+constexpr int kPhAll = kPhL2 | kPhPrefill | kPhRing | kPhStatic | kPhPdl | kPhRun | kPhEpi;
 
 struct RingState {
     int issued, ig, ij;  // ring slots issued so far; next (group, k-slot) to issue
@@ -352,7 +355,9 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
     float* s_up = misc + 128;      // [8][16]
     float* s_rscale = misc + 256;  // [128]
     float* s_rbias = misc + 384;   // [128]
-    float* s_res = misc + 512 + 32;  // [nu*32][M], after the zero blocks
+    uint8_t* s_res = reinterpret_cast<uint8_t*>(misc + 512 + 32);  // [M][upc*32] raw, after the zero blocks
+    const int res_sz = p.res_dtype == BQ_DT_F32 ? 4 : 2;
+    const int res_ld = p.upc * 32;
     const uint32_t zero_blk = sbase + p.smem_misc + 512 * 4 + warp * 16;
     // per-warp partial sums [upc][8 warps][TPU][MT][8 tg][nq tq][4]: only the lanes
     // whose columns 2tq, 2tq+1 can hold a real row (tq < nq = min(4, ceil(M/2)))
@@ -382,12 +387,8 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
         if (phases & kPhRing) fill_ring(rst);
     }
 
-    if (phases & kPhPdl) {
-        pdl_launch_dependents();
-        pdl_wait();
-    }
-
-    if (phases & kPhRun) {
+    // static per-call data (weights' row scales and bias, zero blocks): before the wait
+    if (phases & kPhStatic) {
     if (lane < 4) reinterpret_cast<uint32_t*>(smem + p.smem_misc + 512 * 4 + warp * 16)[lane] = 0u;
     if (lane < 16) reinterpret_cast<uint4*>(const_cast<uint8_t*>(xzero))[lane] = make_uint4(0u, 0u, 0u, 0u);
     for (int r = threadIdx.x; r < nu * 32; r += kConsumerThreads) {
@@ -408,41 +409,60 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
         s_rbias[r] = bi;
     }
 
-    if (p.epi == BQ_EPI_ADD_RESIDUAL) {
-        for (int r = threadIdx.x; r < nu * 32; r += kConsumerThreads) {
-            const int ul = r >> 5, rr = r & 31, tile = rr >> 4;
-            const int n = tile < TPU ? tile_row(u_first + ul, tile) + (rr & 15) : p.N;
-            for (int m = 0; m < M; ++m) s_res[r * M + m] = n < p.N ? load_act(p.residual, m * p.ldr + n, p.res_dtype) : 0.f;
-        }
     }
 
-    if (p.x_bulk) {
-        // this warp's k-blocks of every row, 16 bytes per lane per load
-        const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(p.x);
-        const int per_row = nkw * 16, segs = M * per_row;
-        for (int s0 = 0; s0 < segs; s0 += 128) {
-            uint4 v[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int s = s0 + q * 32 + lane;
-                if (s < segs) {
-                    const int m = s / per_row, r = s - m * per_row;
-                    v[q] = __ldcg(reinterpret_cast<const uint4*>(xb + m * p.ldx + (kw0 + (r >> 4)) * 128 + (r & 15) * 8));
-                }
-            }
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int s = s0 + q * 32 + lane;
-                if (s < segs) {
-                    const int m = s / per_row, r = s - m * per_row;
-                    *reinterpret_cast<uint4*>(xw_ptr + m * pitch + (r >> 4) * 256 + (r & 15) * 16) = v[q];
-                }
-            }
-        }
+    if (phases & kPhPdl) {
+        pdl_launch_dependents();
+        pdl_wait();
     }
+
+    if (phases & kPhRun) {
     if (rst.issued < 0) fill_ring(rst);
     int issued = rst.issued, ig = rst.ig, ij = rst.ij;
-    cp_async_wait_upto(issued);  // gamma landed (weight groups may still be pending)
+    // Inputs of this call, after the wait: x (this warp's k-blocks of every
+    // row) and the residual rows go out together as two cp.async groups
+    // (every thread commits both, possibly empty); only x is waited for here.
+    if (p.x_bulk) {
+        const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(p.x);
+        const int per_row = nkw * 16, segs = M * per_row;
+        for (int s = lane; s < segs; s += 32) {
+            const int m = s / per_row, r = s - m * per_row;
+            cp_async16(xw + m * pitch + (r >> 4) * 256 + (r & 15) * 16, xb + m * p.ldx + (kw0 + (r >> 4)) * 128 + (r & 15) * 8);
+        }
+    }
+    cp_async_commit();
+    const bool has_res = p.epi == BQ_EPI_ADD_RESIDUAL;
+    if (has_res && p.res_bulk) {
+        // 16-byte pieces of 16 / res_sz rows; rows past N are zero-filled
+        const int per_tile = res_sz, per_row = nu * TPU * per_tile;
+        const char* rb = static_cast<const char*>(p.residual);
+        for (int c = threadIdx.x; c < M * per_row; c += kConsumerThreads) {
+            const int m = c / per_row, r = c - m * per_row;
+            const int ul = r / (TPU * per_tile), t = r - ul * (TPU * per_tile), tile = t / per_tile, q = t - tile * per_tile;
+            const int n = tile_row(u_first + ul, tile) + q * (16 / res_sz);
+            const int valid = min(16 / res_sz, p.N - n);
+            const int lr = ul * 32 + tile * 16 + q * (16 / res_sz);
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(s_res) + uint32_t((m * res_ld + lr) * res_sz)),
+                         "l"(rb + (int64_t(m) * p.ldr + (valid > 0 ? n : 0)) * res_sz), "r"(valid > 0 ? valid * res_sz : 0)
+                         : "memory");
+        }
+    }
+    cp_async_commit();
+    if (has_res && !p.res_bulk) {
+        for (int c = threadIdx.x; c < M * nu * 32; c += kConsumerThreads) {
+            const int m = c / (nu * 32), lr = c - m * (nu * 32), tile = (lr & 31) >> 4;
+            const int n = tile < TPU ? tile_row(u_first + (lr >> 5), tile) + (lr & 15) : p.N;
+            const char* src = static_cast<const char*>(p.residual) + (int64_t(m) * p.ldr + n) * res_sz;
+            uint8_t* dst = s_res + (m * res_ld + lr) * res_sz;
+            if (res_sz == 4)
+                *reinterpret_cast<uint32_t*>(dst) = n < p.N ? *reinterpret_cast<const uint32_t*>(src) : 0u;
+            else
+                *reinterpret_cast<uint16_t*>(dst) = n < p.N ? *reinterpret_cast<const uint16_t*>(src) : uint16_t(0);
+        }
+    }
+    // groups after gamma: the first `f0` ring slots, x, residual, then refills
+    const int f0 = issued;
+    cp_async_wait_upto(1);  // gamma, first ring slots and x landed; the residual may be pending
     __syncwarp();
 
     // ---- staging: row groups of kp lanes, 16-byte units (8 values = one 8-k group)
@@ -661,8 +681,9 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
 #pragma unroll 1
         for (int jp = 0; jp < nkp; ++jp) {
             if (!pair_valid(g, jp)) continue;
-            // this slot's group is complete once at most issued - 1 - consumed newer ones are pending
-            cp_async_wait_upto(issued - 1 - consumed);
+            // this slot's group is complete once at most the groups issued after it are pending
+            // (x and residual count for the first f0 slots)
+            cp_async_wait_upto(issued - 1 - consumed + (consumed < f0 ? 2 : 0));
             __syncwarp();
             {
                 const uint8_t* src0 = smem + p.smem_ring + (warp * RS + slot) * p.slot_bytes;
@@ -835,6 +856,7 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
             }
         }
     }
+    if (has_res) cp_async_wait_upto(0);  // this thread's residual pieces
     __syncthreads();
     }  // kPhRun
 
@@ -940,7 +962,13 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
                     const int m = m0 + (d & 1);
                     if (n < p.N && m < M) {
                         float o = v[tile][d];
-                        if (p.epi == BQ_EPI_ADD_RESIDUAL) o += s_res[(ul * 32 + rr) * M + m];
+                        if (p.epi == BQ_EPI_ADD_RESIDUAL) {
+                            const uint8_t* q = s_res + (m * res_ld + ul * 32 + rr) * res_sz;
+                            o += res_sz == 4 ? *reinterpret_cast<const float*>(q)
+                                             : (p.res_dtype == BQ_DT_BF16
+                                                    ? __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(q))
+                                                    : __half2float(*reinterpret_cast<const __half*>(q)));
+                        }
                         store_act(p.out, m * p.ldo + n, p.out_dtype, o);
                     }
                 }
@@ -1018,7 +1046,7 @@ __global__ void __launch_bounds__(kThreads3, 2)
         } else {
             const int i = (s - 1) >> 2, k = (s - 1) & 3;
             op = (k == 0 || k == 2) ? i + 1 : i;
-            ph = k == 0 ? kPhL2 : k == 1 ? kPhRun : k == 2 ? (kPhPrefill | kPhRing) : kPhEpi;
+            ph = k == 0 ? kPhL2 : k == 1 ? (kPhStatic | kPhRun) : k == 2 ? (kPhPrefill | kPhRing) : kPhEpi;
             if (op >= n_ops) continue;
             if (k == 0) load_op(op);
         }

@@ -194,6 +194,10 @@ void fill_gemv3_params(const bq_gemv_desc* d, const Gemv3Plan& pl, int row0, voi
     p.bias = d->bias;
     p.residual = d->residual ? static_cast<const char*>(d->residual) + int64_t(row0) * d->ldr * rsz : nullptr;
     p.ldr = d->ldr;
+    p.res_bulk = (p.residual && (d->res_dtype == BQ_DT_BF16 || d->res_dtype == BQ_DT_F16 || d->res_dtype == BQ_DT_F32) &&
+                  (reinterpret_cast<uintptr_t>(p.residual) & 15) == 0 && (d->ldr * rsz) % 16 == 0)
+                     ? 1
+                     : 0;
     p.out = static_cast<char*>(d->out) + int64_t(row0) * d->ldo * os;
     p.ldo = d->ldo;
     if (!pl.owned) {
