@@ -57,9 +57,9 @@ def measured_peak():
     return 6650.0, "fallback"
 
 
-# DRAM bytes (read + write) of one gemv2_kernel launch on this workload, from
-# the ncu capture summarised in profiles/gemv2_int4_plain_config1.md.
-NCU_TRAFFIC_BYTES = 6_747_392
+# DRAM bytes (read + write) of one gemv3_kernel launch on this workload (mean of
+# two launches), from the ncu capture summarised in profiles/gemv3_int4_plain_config1.md.
+NCU_TRAFFIC_BYTES = 6_766_976
 
 
 class ClockSampler:
