@@ -59,6 +59,38 @@ class AttnDesc(ctypes.Structure):
     ]
 
 
+HEAD_NK = 0
+HEAD_KN = 1
+SAMPLE_TOPK_VALUE = 2
+
+
+class HeadDesc(ctypes.Structure):
+    """bq_head_desc (include/breeze_b200.h)."""
+
+    _fields_ = [
+        ("M", ctypes.c_int32), ("N", ctypes.c_int32), ("K", ctypes.c_int32), ("layout", ctypes.c_int32),
+        ("x_dtype", ctypes.c_int32), ("flags", ctypes.c_uint32), ("eps", ctypes.c_float), ("reserved", ctypes.c_int32),
+        ("x", ctypes.c_void_p), ("ldx", ctypes.c_int64), ("gamma", ctypes.c_void_p), ("w", ctypes.c_void_p),
+        ("ldw", ctypes.c_int64), ("out", ctypes.c_void_p), ("ldo", ctypes.c_int64),
+    ]
+
+
+class SampleDesc(ctypes.Structure):
+    """bq_sample_desc (include/breeze_b200.h)."""
+
+    _fields_ = [
+        ("rows", ctypes.c_int32), ("V", ctypes.c_int32), ("cfg", ctypes.c_int32), ("max_k", ctypes.c_int32),
+        ("mask_lo", ctypes.c_int32), ("mask_hi", ctypes.c_int32), ("clamp_hi", ctypes.c_int32),
+        ("flags", ctypes.c_uint32), ("rep_penalty", ctypes.c_float), ("history_cap", ctypes.c_int32),
+        ("logits", ctypes.c_void_p), ("ldl", ctypes.c_int64), ("guidance", ctypes.c_void_p),
+        ("temperature", ctypes.c_void_p), ("top_k", ctypes.c_void_p), ("top_p", ctypes.c_void_p),
+        ("do_sample", ctypes.c_void_p), ("history", ctypes.c_void_p), ("history_len", ctypes.c_void_p),
+        ("suppress", ctypes.c_void_p), ("uniform", ctypes.c_void_p), ("rng", ctypes.c_void_p),
+        ("cfg_out", ctypes.c_void_p), ("ldc", ctypes.c_int64), ("tokens", ctypes.c_void_p), ("ldt", ctypes.c_int64),
+        ("tokens2", ctypes.c_void_p), ("ldt2", ctypes.c_int64),
+    ]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -78,6 +110,10 @@ _SIGS = {
                                               ctypes.c_size_t, ctypes.c_void_p]),
     "bq_attention_workspace_bytes": (ctypes.c_int32, [ctypes.POINTER(AttnDesc), ctypes.POINTER(ctypes.c_size_t)]),
     "bq_attention_step": (ctypes.c_int32, [ctypes.POINTER(AttnDesc), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "bq_head_workspace_bytes": (ctypes.c_int32, [ctypes.POINTER(HeadDesc), ctypes.POINTER(ctypes.c_size_t)]),
+    "bq_head_gemv": (ctypes.c_int32, [ctypes.POINTER(HeadDesc), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "bq_sample_workspace_bytes": (ctypes.c_int32, [ctypes.POINTER(SampleDesc), ctypes.POINTER(ctypes.c_size_t)]),
+    "bq_sample": (ctypes.c_int32, [ctypes.POINTER(SampleDesc), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     "bq_int4_tinygemm_pack": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
                                                ctypes.c_int32, ctypes.c_void_p]),
     "bq_int4_tinygemm_unpack": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
@@ -199,6 +235,9 @@ WORKSPACE = Workspace()
 # bq_gemv's arrival counters (also at the start) must stay zero at rest, so
 # the two never share a buffer.
 ATTN_WORKSPACE = Workspace()
+# bq_head_gemv (K-major layout) and bq_sample keep arrival counters the same way.
+HEAD_WORKSPACE = Workspace()
+SAMPLE_WORKSPACE = Workspace()
 
 
 def make_desc(x: torch.Tensor, w: torch.Tensor, wfmt: int, n: int, *, scale=None, group: int = 128, gamma=None,
@@ -367,6 +406,90 @@ def attention_step(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, cach
     ws = ATTN_WORKSPACE.get(dev, need.value)
     check(lib.bq_attention_step(ctypes.byref(ad), ws.data_ptr(), ws.numel(), _stream(dev)), "bq_attention_step")
     return out
+
+
+def head_gemv(x: torch.Tensor, w: torch.Tensor, layout: int, *, gamma: torch.Tensor | None = None, eps: float = 1e-6,
+              out: torch.Tensor | None = None, flags: int = 0) -> torch.Tensor:
+    """fp32 output head through bq_head_gemv: out (M, N) fp32 = y @ W, with y = x
+    or the reference's BreezeRMSNorm of x when gamma is given. layout HEAD_NK:
+    w is an nn.Linear weight (N, K); HEAD_KN: w is one codebook slice (K, N)."""
+    dev = _require_cuda(x, w, gamma, out)
+    if w.dtype != torch.float32 or w.stride(1) != 1:
+        raise ValueError("head weights must be fp32 with contiguous rows")
+    x = _rowmajor(x, "x")
+    m, k = x.shape
+    n = w.shape[0] if layout == HEAD_NK else w.shape[1]
+    if (w.shape[1] if layout == HEAD_NK else w.shape[0]) != k:
+        raise ValueError(f"weight shape {tuple(w.shape)} does not match K={k}")
+    if gamma is not None and (gamma.dtype != torch.bfloat16 or not gamma.is_contiguous()):
+        raise ValueError("gamma must be a contiguous bf16 vector")
+    if out is None:
+        out = torch.empty(m, n, device=dev, dtype=torch.float32)
+    out = _rowmajor(out, "out")
+    d = HeadDesc()
+    d.M, d.N, d.K, d.layout, d.x_dtype, d.flags, d.eps = m, n, k, layout, _DT[x.dtype], flags, eps
+    d.x, d.ldx, d.gamma = x.data_ptr(), x.stride(0), _ptr(gamma)
+    d.w, d.ldw, d.out, d.ldo = w.data_ptr(), w.stride(0), out.data_ptr(), out.stride(0)
+    lib = load()
+    need = ctypes.c_size_t(0)
+    check(lib.bq_head_workspace_bytes(ctypes.byref(d), ctypes.byref(need)), "bq_head_workspace_bytes")
+    ws = HEAD_WORKSPACE.get(dev, need.value) if need.value else None
+    check(lib.bq_head_gemv(ctypes.byref(d), _ptr(ws), 0 if ws is None else ws.numel(), _stream(dev)), "bq_head_gemv")
+    return out
+
+
+def sample(logits: torch.Tensor, rows: int, *, temperature: torch.Tensor, top_k: torch.Tensor, top_p: torch.Tensor,
+           do_sample: torch.Tensor, tokens: torch.Tensor, guidance: torch.Tensor | None = None, max_k: int | None = None,
+           mask: tuple[int, int] = (0, 0), clamp_hi: int | None = None, topk_by_value: bool = False,
+           rep_penalty: float = 1.0, history: torch.Tensor | None = None, history_len: torch.Tensor | None = None,
+           suppress: torch.Tensor | None = None, uniform: torch.Tensor | None = None, rng: torch.Tensor | None = None,
+           cfg_out: torch.Tensor | None = None, tokens2: torch.Tensor | None = None, flags: int = 0) -> torch.Tensor:
+    """CFG mix + sampling through bq_sample (see the header). logits (rows or
+    2 rows when guidance is given, V) fp32; per-row parameter buffers on the
+    device; tokens (and tokens2) int64 with row stride given by stride(0)."""
+    dev = _require_cuda(logits, temperature, top_k, top_p, do_sample, tokens, guidance, history, history_len,
+                        suppress, uniform, rng, cfg_out, tokens2)
+    if logits.dtype != torch.float32 or logits.stride(1) != 1:
+        raise ValueError("logits must be fp32 with contiguous rows")
+    v = logits.shape[1]
+    cfg = guidance is not None
+    if logits.shape[0] < (2 * rows if cfg else rows):
+        raise ValueError("logits has too few rows")
+    checks = ((temperature, torch.float32), (top_k, torch.int64), (top_p, torch.float32), (do_sample, torch.int64),
+              (guidance, torch.float32), (uniform, torch.float32), (rng, torch.int64), (history, torch.int64),
+              (history_len, torch.int32), (tokens, torch.int64), (tokens2, torch.int64))
+    for t, dt in checks:
+        if t is not None and t.dtype != dt:
+            raise ValueError(f"sampling buffer of dtype {t.dtype}, expected {dt}")
+    for t in (temperature, top_k, top_p, do_sample, guidance, uniform, rng, history_len, suppress):
+        if t is not None and not t.is_contiguous():
+            raise ValueError("per-row sampling buffers must be contiguous")
+    d = SampleDesc()
+    d.rows, d.V, d.cfg = rows, v, int(cfg)
+    d.max_k = v if max_k is None else max_k
+    d.mask_lo, d.mask_hi = mask
+    d.clamp_hi = v - 1 if clamp_hi is None else clamp_hi
+    d.flags = flags | (SAMPLE_TOPK_VALUE if topk_by_value else 0)
+    d.rep_penalty = rep_penalty
+    d.logits, d.ldl = logits.data_ptr(), logits.stride(0)
+    d.guidance, d.temperature, d.top_k, d.top_p = _ptr(guidance), temperature.data_ptr(), top_k.data_ptr(), top_p.data_ptr()
+    d.do_sample = do_sample.data_ptr()
+    if history is not None:
+        if history.stride(1) != 1:
+            raise ValueError("history rows must be contiguous")
+        d.history, d.history_cap, d.history_len = history.data_ptr(), history.stride(0), _ptr(history_len)
+    d.suppress, d.uniform, d.rng = _ptr(suppress), _ptr(uniform), _ptr(rng)
+    if cfg_out is not None:
+        d.cfg_out, d.ldc = cfg_out.data_ptr(), cfg_out.stride(0)
+    d.tokens, d.ldt = tokens.data_ptr(), tokens.stride(0)
+    if tokens2 is not None:
+        d.tokens2, d.ldt2 = tokens2.data_ptr(), tokens2.stride(0)
+    lib = load()
+    need = ctypes.c_size_t(0)
+    check(lib.bq_sample_workspace_bytes(ctypes.byref(d), ctypes.byref(need)), "bq_sample_workspace_bytes")
+    ws = SAMPLE_WORKSPACE.get(dev, need.value)
+    check(lib.bq_sample(ctypes.byref(d), ws.data_ptr(), ws.numel(), _stream(dev)), "bq_sample")
+    return tokens
 
 
 def dequant(w: torch.Tensor, wfmt: int, n: int, k: int, *, scale=None, group: int = 128) -> torch.Tensor:

@@ -189,6 +189,91 @@ typedef struct bq_attn_desc {
 int32_t bq_attention_workspace_bytes(const bq_attn_desc* desc, size_t* bytes);
 int32_t bq_attention_step(const bq_attn_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- fp32 output heads -------------------------------------------------- */
+/* out[M, N] (fp32) = y @ W, W fp32, where y is x or, when gamma is given, the
+ * reference's BreezeRMSNorm of x (models/breeze.py:115-120: xh = bf16(x *
+ * rsqrt(mean(x^2) + eps)), y = bf16(gamma * xh)) read as fp32.
+ * Replaces the fp32 heads of the decode graphs: BreezeCodebooksHead.forward
+ * (models/breeze.py:598-613; W = weight[codebook], layout K-major) after the
+ * depth model's final norm (models/cudagraph/depth_decoder_graph.py:161,
+ * 617-623, 641-648), and the backbone lm_head.float() (nn.Linear weight,
+ * layout N-major; models/cudagraph/backbone_graph.py:70, 272-273). */
+#define BQ_HEAD_NK 0 /* W[n * ldw + k]: nn.Linear weight [N, K]               */
+#define BQ_HEAD_KN 1 /* W[k * ldw + n]: one codebook slice [K, N] (hidden, vocab) */
+
+typedef struct bq_head_desc {
+    int32_t M, N, K;     /* rows (M <= 16), outputs, inputs */
+    int32_t layout;      /* BQ_HEAD_NK or BQ_HEAD_KN */
+    int32_t x_dtype;     /* BQ_DT_* */
+    uint32_t flags;      /* BQ_FLAG_PDL */
+    float eps;           /* RMSNorm epsilon (gamma != NULL) */
+    int32_t reserved;
+    const void* x;       /* [M, ldx] */
+    int64_t ldx;
+    const void* gamma;   /* bf16 [K] or NULL */
+    const float* w;      /* fp32, see layout */
+    int64_t ldw;
+    float* out;          /* fp32 [M, ldo] */
+    int64_t ldo;
+} bq_head_desc;
+
+/* The workspace (K-major layout only; 256-byte aligned) starts with arrival
+ * counters that the kernel leaves at zero: zero-fill it once, and give it to
+ * no other kernel. */
+int32_t bq_head_workspace_bytes(const bq_head_desc* desc, size_t* bytes);
+int32_t bq_head_gemv(const bq_head_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- CFG mix and token sampling ----------------------------------------- */
+/* Per sample row r: cfg = uncond + g * (cond - uncond) (paired rows; else cond),
+ * logits [mask_lo, mask_hi) = -inf (mask_invalid_codec_token_logits), the
+ * HF repetition penalty over the row's token history, the suppress mask;
+ * greedy = argmax(cfg); then temperature, top-k, top-p (HF order, on raw
+ * logits), softmax and one draw by inverse CDF over the kept tokens in
+ * descending-probability order with u in [0, 1); token = do_sample ? draw :
+ * greedy, clamped to [0, clamp_hi]. u comes from `uniform` or from
+ * Philox4x32-10 (key = rng[0], counter = {rng[1], r}); the launch advances
+ * rng[1] by one, so a replayed graph draws fresh numbers.
+ * Replaces DepthDecoderGraph._cfg_sample (models/cudagraph/depth_decoder_graph.py:
+ * 487-558) and sample_logits (models/cudagraph/sampling.py:36-87) with the CFG
+ * mix of BackboneGraph._decode_step (models/cudagraph/backbone_graph.py:275-285). */
+#define BQ_SAMPLE_TOPK_VALUE 2u /* top-k keeps every logit >= the k-th largest (sample_logits);
+                                   default: the first k ranks (the depth graph's topk mask)   */
+#define BQ_SAMPLE_MAX_V 8192
+
+typedef struct bq_sample_desc {
+    int32_t rows;              /* samples; with cfg the logits hold 2 * rows rows: cond, then uncond */
+    int32_t V;                 /* logits per row, <= BQ_SAMPLE_MAX_V */
+    int32_t cfg;               /* 0 or 1 */
+    int32_t max_k;             /* top_k <= 0 means max_k; top_k is clamped to [1, max_k] */
+    int32_t mask_lo, mask_hi;  /* logits [mask_lo, mask_hi) become -inf (empty when equal) */
+    int32_t clamp_hi;          /* tokens are clamped to [0, clamp_hi] */
+    uint32_t flags;            /* BQ_FLAG_PDL | BQ_SAMPLE_TOPK_VALUE */
+    float rep_penalty;         /* HF repetition penalty (1 = none) */
+    int32_t history_cap;       /* tokens per history row */
+    const float* logits;       /* fp32 [rows or 2 rows, ldl] */
+    int64_t ldl;
+    const float* guidance;     /* fp32 [rows] (cfg only) */
+    const float* temperature;  /* fp32 [rows] */
+    const int64_t* top_k;      /* int64 [rows] */
+    const float* top_p;        /* fp32 [rows] */
+    const int64_t* do_sample;  /* int64 [rows], 0 = greedy */
+    const int64_t* history;    /* int64 [rows, history_cap] or NULL */
+    const int32_t* history_len;/* int32 [rows] valid entries per history row */
+    const uint8_t* suppress;   /* bool [V] or NULL */
+    const float* uniform;      /* fp32 [rows] or NULL (Philox) */
+    uint64_t* rng;             /* {seed, call counter}, required when uniform is NULL */
+    float* cfg_out;            /* fp32 [rows, ldc] mixed and masked logits, or NULL */
+    int64_t ldc;
+    int64_t* tokens;           /* tokens[r * ldt]; with cfg also tokens[(r + rows) * ldt] */
+    int64_t ldt;
+    int64_t* tokens2;          /* optional second destination, same rule */
+    int64_t ldt2;
+} bq_sample_desc;
+
+/* 256 bytes (an arrival counter the kernel leaves at zero); zero-fill once. */
+int32_t bq_sample_workspace_bytes(const bq_sample_desc* desc, size_t* bytes);
+int32_t bq_sample(const bq_sample_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- layouts and dequantization ---------------------------------------- */
 /* (N, K/2) uint8 odd-k-low -> tinygemm int32 [N/8, K/(16*ikt), 32, ikt/2].
  * Replaces torch._convert_weight_to_int4pack (models/int4_linear.py:59). */
