@@ -114,6 +114,9 @@ _SIGS = {
     "bq_head_gemv": (ctypes.c_int32, [ctypes.POINTER(HeadDesc), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     "bq_sample_workspace_bytes": (ctypes.c_int32, [ctypes.POINTER(SampleDesc), ctypes.POINTER(ctypes.c_size_t)]),
     "bq_sample": (ctypes.c_int32, [ctypes.POINTER(SampleDesc), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "bq_embed_rows": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
+                                       ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int64,
+                                       ctypes.c_uint32, ctypes.c_void_p]),
     "bq_int4_tinygemm_pack": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
                                                ctypes.c_int32, ctypes.c_void_p]),
     "bq_int4_tinygemm_unpack": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
@@ -490,6 +493,20 @@ def sample(logits: torch.Tensor, rows: int, *, temperature: torch.Tensor, top_k:
     ws = SAMPLE_WORKSPACE.get(dev, need.value)
     check(lib.bq_sample(ctypes.byref(d), ws.data_ptr(), ws.numel(), _stream(dev)), "bq_sample")
     return tokens
+
+
+def embed_rows(table: torch.Tensor, ids: torch.Tensor, offset: int, out: torch.Tensor, flags: int = 0) -> torch.Tensor:
+    """out[r] = table[clamp(ids[r] + offset, 0, rows - 1)] through bq_embed_rows
+    (bf16 rows; ids int64, any row stride)."""
+    dev = _require_cuda(table, ids, out)
+    if table.dtype != torch.bfloat16 or out.dtype != torch.bfloat16 or ids.dtype != torch.int64:
+        raise ValueError("embedding rows must be bf16 and ids int64")
+    if table.stride(1) != 1 or out.stride(1) != 1:
+        raise ValueError("embedding rows must be contiguous")
+    n = out.shape[0]
+    check(load().bq_embed_rows(table.data_ptr(), table.stride(0), table.shape[0], ids.data_ptr(), ids.stride(0), offset,
+                               n, table.shape[1], out.data_ptr(), out.stride(0), flags, _stream(dev)), "bq_embed_rows")
+    return out
 
 
 def dequant(w: torch.Tensor, wfmt: int, n: int, k: int, *, scale=None, group: int = 128) -> torch.Tensor:

@@ -24,6 +24,11 @@ namespace {
 
 constexpr int kAttnThreads = 128;
 constexpr int kMaxG = 8;  // query heads per kv head
+// Fixed counter region at the start of the workspace (one counter per (row,
+// kv head)): a shape-dependent size would let one call's partials land where
+// a later call with more (row, kv head) pairs keeps its counters.
+constexpr int kAttnMaxPairs = 4096;
+constexpr size_t kAttnCounterBytes = size_t(kAttnMaxPairs) * 4;
 
 struct AttnParams {
     int32_t B, HQ, HKV, S, G, splits, mask_dtype, has_norm;
@@ -336,6 +341,8 @@ int validate_attn(const bq_attn_desc* d) {
     if (d->B < 1 || d->HQ < 1 || d->HKV < 1 || d->S < 1)
         return set_error(BQ_ERR_SHAPE, "B, HQ, HKV, S must be positive");
     if (d->D != 64 && d->D != 128) return set_error(BQ_ERR_SHAPE, "head dim %d not supported (64 or 128)", d->D);
+    if (int64_t(d->B) * d->HKV > kAttnMaxPairs)
+        return set_error(BQ_ERR_SHAPE, "B * HKV = %lld exceeds %d", (long long)d->B * d->HKV, kAttnMaxPairs);
     if (d->HQ % d->HKV || d->HQ / d->HKV > kMaxG)
         return set_error(BQ_ERR_SHAPE, "HQ=%d must be a multiple of HKV=%d, at most %d query heads per kv head", d->HQ,
                          d->HKV, kMaxG);
@@ -369,7 +376,7 @@ int32_t bq_attention_workspace_bytes(const bq_attn_desc* d, size_t* bytes) {
     if (!dev) return BQ_ERR_CUDA;
     const int sp = attn_splits(d, dev->sm_count);
     const int G = d->HQ / d->HKV;
-    const size_t counters = (size_t(d->B) * d->HKV * 4 + 255) / 256 * 256;
+    const size_t counters = kAttnCounterBytes;
     *bytes = sp == 1 ? 0 : counters + size_t(d->B) * d->HKV * sp * G * (d->D + 2) * 4;
     return BQ_OK;
 }
@@ -407,7 +414,7 @@ int32_t bq_attention_step(const bq_attn_desc* d, void* workspace, size_t workspa
     p.out = static_cast<__nv_bfloat16*>(d->out);
     p.ldo = d->ldo;
     if (p.splits > 1) {
-        const size_t counters = (size_t(d->B) * d->HKV * 4 + 255) / 256 * 256;
+        const size_t counters = kAttnCounterBytes;
         const size_t need = counters + size_t(d->B) * d->HKV * p.splits * p.G * (d->D + 2) * 4;
         if (!workspace || workspace_bytes < need)
             return set_error(BQ_ERR_WORKSPACE, "attention workspace of %zu bytes given, %zu needed", workspace_bytes, need);

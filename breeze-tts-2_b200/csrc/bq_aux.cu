@@ -7,6 +7,8 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <cstring>
+
 #include "bq_device.cuh"
 #include "bq_host.h"
 
@@ -148,6 +150,26 @@ static int check_launch(const char* what) {
 }
 
 
+// One CTA per output row: out[r] = table[clamp(ids[r * ld_ids] + offset, 0, rows - 1)].
+__global__ void embed_rows_kernel(const uint8_t* __restrict__ table, int64_t ld_bytes, int64_t table_rows,
+                                  const int64_t* __restrict__ ids, int64_t ld_ids, int64_t offset, int width_bytes,
+                                  uint8_t* __restrict__ out, int64_t ldo_bytes, int vec) {
+    pdl_launch_dependents();
+    pdl_wait();  // the ids come from the previous step's sampler
+    const int r = blockIdx.x;
+    int64_t row = ids[int64_t(r) * ld_ids] + offset;
+    row = row < 0 ? 0 : (row >= table_rows ? table_rows - 1 : row);
+    const uint8_t* src = table + row * ld_bytes;
+    uint8_t* dst = out + int64_t(r) * ldo_bytes;
+    if (vec) {
+        for (int i = threadIdx.x; i < width_bytes / 16; i += blockDim.x)
+            reinterpret_cast<uint4*>(dst)[i] = __ldg(reinterpret_cast<const uint4*>(src) + i);
+    } else {
+        for (int i = threadIdx.x; i < width_bytes / 2; i += blockDim.x)
+            reinterpret_cast<uint16_t*>(dst)[i] = reinterpret_cast<const uint16_t*>(src)[i];
+    }
+}
+
 }  // namespace bq
 
 using namespace bq;
@@ -212,6 +234,37 @@ int32_t bq_silu_mul(const void* g, int64_t ldg, const void* u, int64_t ldu, void
         static_cast<const __nv_bfloat16*>(g), ldg, static_cast<const __nv_bfloat16*>(u), ldu,
         static_cast<__nv_bfloat16*>(out), ldo, M, N);
     return check_launch("silu_mul");
+}
+
+int32_t bq_embed_rows(const void* table, int64_t ld_table, int64_t table_rows, const int64_t* ids, int64_t ld_ids,
+                      int64_t offset, int32_t n, int32_t width, void* out, int64_t ldo, uint32_t flags, void* stream) {
+    if (!table || !ids || !out) return set_error(BQ_ERR_INVALID_ARG, "table, ids and out must be non-NULL");
+    if (n < 1 || width < 1 || table_rows < 1 || ld_table < width || ldo < width)
+        return set_error(BQ_ERR_SHAPE, "bad embedding lookup shape (n=%d, width=%d)", n, width);
+    const int vec = ((reinterpret_cast<uintptr_t>(table) | reinterpret_cast<uintptr_t>(out)) % 16 == 0 &&
+                     (ld_table * 2) % 16 == 0 && (ldo * 2) % 16 == 0 && (int64_t(width) * 2) % 16 == 0)
+                        ? 1
+                        : 0;
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(n);
+    cfg.blockDim = dim3(128);
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    if (flags & BQ_FLAG_PDL) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    const uint8_t* tb = static_cast<const uint8_t*>(table);
+    int64_t ldb = ld_table * 2, tr = table_rows, ldi = ld_ids, off = offset, ldob = ldo * 2;
+    int wb = width * 2;
+    uint8_t* ob = static_cast<uint8_t*>(out);
+    void* args[] = {&tb, &ldb, &tr, &ids, &ldi, &off, &wb, &ob, &ldob, const_cast<int*>(&vec)};
+    cudaError_t e = cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(&embed_rows_kernel), args);
+    if (e != cudaSuccess) return set_error(BQ_ERR_CUDA, "embed launch failed: %s", cudaGetErrorString(e));
+    return BQ_OK;
 }
 
 }  // extern "C"

@@ -25,6 +25,11 @@ namespace {
 constexpr int kHeadThreads = 256;
 constexpr int kHeadMaxM = 16;
 constexpr int kKnCols = 128;  // K-major: columns per CTA
+// Fixed counter region: the arrival counters of every call sit at the same
+// bytes, which no call's partial sums ever touch (a shape-dependent region
+// would let one call's partials land where a later, larger call counts).
+constexpr int kKnMaxTiles = 1024;
+constexpr size_t kKnCounterBytes = size_t(kKnMaxTiles) * 4;
 
 struct HeadParams {
     int32_t M, N, K, x_dtype, has_norm, splits, tiles, vec;
@@ -218,6 +223,8 @@ int validate_head(const bq_head_desc* d) {
     if (!d->x || !d->w || !d->out) return set_error(BQ_ERR_INVALID_ARG, "x, w and out must be non-NULL");
     if (d->ldx < d->K || d->ldo < d->N) return set_error(BQ_ERR_SHAPE, "ldx < K or ldo < N");
     if (d->layout == BQ_HEAD_NK ? d->ldw < d->K : d->ldw < d->N) return set_error(BQ_ERR_SHAPE, "ldw too small");
+    if (d->layout == BQ_HEAD_KN && (d->N + kKnCols - 1) / kKnCols > kKnMaxTiles)
+        return set_error(BQ_ERR_SHAPE, "head: N=%d exceeds %d columns", d->N, kKnMaxTiles * kKnCols);
     if (size_t(d->M) * d->K * 4 > 96 * 1024)
         return set_error(BQ_ERR_SHAPE, "head: M * K = %d inputs do not fit in shared memory", d->M * d->K);
     return BQ_OK;
@@ -230,7 +237,7 @@ void kn_grid(const bq_head_desc* d, int sm_count, int* tiles, int* splits) {
     *splits = std::max(1, std::min(s, 64));
 }
 
-size_t kn_counter_bytes(int tiles) { return (size_t(tiles) * 4 + 255) / 256 * 256; }
+
 
 }  // namespace
 }  // namespace bq
@@ -249,7 +256,7 @@ int32_t bq_head_workspace_bytes(const bq_head_desc* d, size_t* bytes) {
         if (!dev) return BQ_ERR_CUDA;
         int tiles, splits;
         kn_grid(d, dev->sm_count, &tiles, &splits);
-        if (splits > 1) *bytes = kn_counter_bytes(tiles) + size_t(splits) * d->M * d->N * 4;
+        if (splits > 1) *bytes = kKnCounterBytes + size_t(splits) * d->M * d->N * 4;
     }
     return BQ_OK;
 }
@@ -285,7 +292,7 @@ int32_t bq_head_gemv(const bq_head_desc* d, void* workspace, size_t workspace_by
     } else {
         kn_grid(d, dev->sm_count, &p.tiles, &p.splits);
         if (p.splits > 1) {
-            const size_t cb = kn_counter_bytes(p.tiles);
+            const size_t cb = kKnCounterBytes;
             const size_t need = cb + size_t(p.splits) * d->M * d->N * 4;
             if (!workspace || workspace_bytes < need)
                 return set_error(BQ_ERR_WORKSPACE, "head workspace of %zu bytes given, %zu needed", workspace_bytes, need);

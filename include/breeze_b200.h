@@ -289,6 +289,15 @@ int32_t bq_int4_tinygemm_unpack(const void* in_i32, void* packed_u8, int32_t N, 
  * group, w, scale}. For parity checks and debugging. */
 int32_t bq_dequant(const bq_gemv_desc* desc, float* out, void* stream);
 
+/* ---- embedding lookup ---------------------------------------------------- */
+/* out[r, :] = table[clamp(ids[r * ld_ids] + offset, 0, table_rows - 1), :] for
+ * r < n; bf16 rows of `width` elements. The depth loop's token embedding
+ * (embed_tokens(tok + codebook offset), clamped:
+ * models/cudagraph/depth_decoder_graph.py:563-567, 602-609). ids are read
+ * after the dependent-launch wait (they come from the previous sampler). */
+int32_t bq_embed_rows(const void* table, int64_t ld_table, int64_t table_rows, const int64_t* ids, int64_t ld_ids,
+                      int64_t offset, int32_t n, int32_t width, void* out, int64_t ldo, uint32_t flags, void* stream);
+
 /* ---- glue kernels (models/fused/kernels.py:541-575) ---------------------- */
 /* out[M, K] = x * rsqrt(mean(x^2) + eps) * gamma (fp32 math), bf16 in/out. */
 int32_t bq_rmsnorm(const void* x, int64_t ldx, const void* gamma, void* out, int64_t ldo,
