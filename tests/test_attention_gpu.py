@@ -54,6 +54,9 @@ CASES = [
     (2, 4, 2, 64, 48, 0, True, "float", False),
     (3, 6, 3, 64, 600, 599, False, "bool", False),
     (2, 32, 8, 128, 4096, 3000, True, "float", True),
+    # 256 (row, kv head) pairs after the smaller cases: the workspace's counter
+    # region must not overlap what earlier calls wrote as partials
+    (16, 16, 16, 128, 512, 300, False, None, True),
 ]
 
 
