@@ -238,9 +238,12 @@ def run_ours(args, rank, local_rank, world):
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
     decode = None if args.no_decode_step else decode_step_bench(device, world, local_rank)
+    depth = None if args.no_decode_step else depth_frame_bench(device, world, local_rank)
     if rank == 0:
         if decode is not None:
             line["decode_step"] = decode
+        if depth is not None:
+            line["depth_frame"] = depth
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -317,6 +320,56 @@ def decode_step_bench(device, world: int, local_rank: int, replays: int = 10, wa
                     "(16 q / 16 kv heads of 128, kv_len 256; 141 launches)",
             "launches_per_step": 4 * DECODE_LAYERS + 1, "replays_timed": replays,
             "l2_policy": "weights 1-1.9 GB per step >> L2", "results": results}
+
+
+DEPTH_LAYERS = 12
+
+
+def depth_frame_bench(device, world: int, local_rank: int, replays: int = 10, warmup: int = 3):
+    """Depth-decoder frame leg (breeze_b200.fused.depth.DepthDecoderLoop): one
+    CUDA graph of a whole frame (2-position prefill + 14 single steps over 12
+    layers, fp32 codebook head and CFG sampling per step) at the depth shapes
+    (hidden 1024, MLP 8192, 8 q / 8 kv heads of 128, audio embedding 2048,
+    vocab 2051, 16 codebooks), int4 MLP with bf16 attention projections as the
+    reference's FusedDecoderLayer(attn_bits=16) over Int4Linear runs it. Device
+    time per replay, max over ranks."""
+    from breeze_b200.fused.depth import DepthDecoderLoop, synthetic_depth
+
+    cur = torch.cuda.current_stream(device)
+    out = []
+    layers, norm_w, head, embed, in_proj = synthetic_depth("int4", DEPTH_LAYERS, device, seed=9, attn_fmt="bf16",
+                                                           proj_fmt="bf16")
+    for batch in (1, 2):
+        loop = DepthDecoderLoop(layers, norm_w, head, embed, in_proj, batch, codebook_size=2048, kv_heads=8, seed=batch)
+        loop.capture()
+        for _ in range(warmup):
+            loop.replay()
+        torch.cuda.synchronize(device)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier(device_ids=[local_rank])
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(cur)
+        for _ in range(replays):
+            loop.replay()
+        e1.record(cur)
+        torch.cuda.synchronize(device)
+        t = torch.tensor([e0.elapsed_time(e1) / replays], device=device, dtype=torch.float64)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        us = float(t.item()) * 1e3
+        out.append({"batch": batch, "frame_us": round(us, 1), "us_per_codebook_step": round(us / loop.n_dec, 1),
+                    "launches": loop.launches, "weight_GBps": round(loop.weight_bytes_per_frame / us / 1e3, 1),
+                    "tokens_valid": bool(((loop.output_tokens >= 0) & (loop.output_tokens < 2048)).all().item())})
+        del loop
+    del layers, head, embed
+    torch.cuda.empty_cache()
+    return {"what": f"depth-decoder frame: {DEPTH_LAYERS} layers, 15 codebooks (prefill at positions 0-1 + 14 steps), "
+                    "int4 MLP / bf16 QKV+O / bf16 projector, fp32 codebook head, CFG sampling in the graph",
+            "replays_timed": replays, "results": out}
 
 
 def _cpu_inputs():

@@ -62,6 +62,7 @@ class AttnDesc(ctypes.Structure):
 HEAD_NK = 0
 HEAD_KN = 1
 SAMPLE_TOPK_VALUE = 2
+SAMPLE_APPEND_HISTORY = 4
 
 
 class HeadDesc(ctypes.Structure):
@@ -87,7 +88,8 @@ class SampleDesc(ctypes.Structure):
         ("do_sample", ctypes.c_void_p), ("history", ctypes.c_void_p), ("history_len", ctypes.c_void_p),
         ("suppress", ctypes.c_void_p), ("uniform", ctypes.c_void_p), ("rng", ctypes.c_void_p),
         ("cfg_out", ctypes.c_void_p), ("ldc", ctypes.c_int64), ("tokens", ctypes.c_void_p), ("ldt", ctypes.c_int64),
-        ("tokens2", ctypes.c_void_p), ("ldt2", ctypes.c_int64),
+        ("tokens2", ctypes.c_void_p), ("ldt2", ctypes.c_int64), ("eos_id", ctypes.c_int64),
+        ("eos_flag", ctypes.c_void_p),
     ]
 
 
@@ -446,12 +448,13 @@ def sample(logits: torch.Tensor, rows: int, *, temperature: torch.Tensor, top_k:
            mask: tuple[int, int] = (0, 0), clamp_hi: int | None = None, topk_by_value: bool = False,
            rep_penalty: float = 1.0, history: torch.Tensor | None = None, history_len: torch.Tensor | None = None,
            suppress: torch.Tensor | None = None, uniform: torch.Tensor | None = None, rng: torch.Tensor | None = None,
-           cfg_out: torch.Tensor | None = None, tokens2: torch.Tensor | None = None, flags: int = 0) -> torch.Tensor:
+           cfg_out: torch.Tensor | None = None, tokens2: torch.Tensor | None = None, append_history: bool = False,
+           eos_id: int = -1, eos_flag: torch.Tensor | None = None, flags: int = 0) -> torch.Tensor:
     """CFG mix + sampling through bq_sample (see the header). logits (rows or
     2 rows when guidance is given, V) fp32; per-row parameter buffers on the
     device; tokens (and tokens2) int64 with row stride given by stride(0)."""
     dev = _require_cuda(logits, temperature, top_k, top_p, do_sample, tokens, guidance, history, history_len,
-                        suppress, uniform, rng, cfg_out, tokens2)
+                        suppress, uniform, rng, cfg_out, tokens2, eos_flag)
     if logits.dtype != torch.float32 or logits.stride(1) != 1:
         raise ValueError("logits must be fp32 with contiguous rows")
     v = logits.shape[1]
@@ -472,7 +475,10 @@ def sample(logits: torch.Tensor, rows: int, *, temperature: torch.Tensor, top_k:
     d.max_k = v if max_k is None else max_k
     d.mask_lo, d.mask_hi = mask
     d.clamp_hi = v - 1 if clamp_hi is None else clamp_hi
-    d.flags = flags | (SAMPLE_TOPK_VALUE if topk_by_value else 0)
+    d.flags = flags | (SAMPLE_TOPK_VALUE if topk_by_value else 0) | (SAMPLE_APPEND_HISTORY if append_history else 0)
+    if eos_flag is not None and eos_flag.dtype != torch.int32:
+        raise ValueError("eos_flag must be int32")
+    d.eos_id, d.eos_flag = eos_id, _ptr(eos_flag)
     d.rep_penalty = rep_penalty
     d.logits, d.ldl = logits.data_ptr(), logits.stride(0)
     d.guidance, d.temperature, d.top_k, d.top_p = _ptr(guidance), temperature.data_ptr(), top_k.data_ptr(), top_p.data_ptr()

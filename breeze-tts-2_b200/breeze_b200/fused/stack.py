@@ -147,11 +147,27 @@ class DecodeStack:
     launches.
     """
 
-    def __init__(self, layers: list[DecodeLayer], head: QWeight, ln_f: torch.Tensor, rows: int,
+    def __init__(self, layers: list[DecodeLayer], head: QWeight | None, ln_f: torch.Tensor, rows: int,
                  eps: float = 1e-6, attn_cols: int | None = None, chain: bool = False, attention: bool = False,
-                 head_dim: int = 128, kv_heads: int | None = None, kv_len: int = 256):
+                 head_dim: int = 128, kv_heads: int | None = None, kv_len: int = 256,
+                 lm_head: torch.Tensor | None = None, sampling: dict | None = None):
+        """``lm_head``: an fp32 nn.Linear weight (V, hidden) used instead of the
+        quantized ``head``, as the backbone graph casts lm_head to fp32
+        (backbone_graph.py:70, 272-273). ``sampling`` (needs ``lm_head``):
+        the token is drawn in the graph (bq_sample) instead of on the host
+        after a copy (fast_streaming.py:929-939): keys temperature, top_k,
+        top_p, do_sample, guidance_scale (CFG when rows >= 2: cond rows, then
+        uncond rows), repetition_penalty, history_cap, suppress (lo, hi),
+        eos_id, seed. Each step first appends the current token to the
+        history, then draws; ``eos_flag`` becomes 1 when EOS is drawn."""
         if not layers:
             raise ValueError("DecodeStack needs at least one layer")
+        if head is None and lm_head is None:
+            raise ValueError("DecodeStack needs a head or an fp32 lm_head")
+        if sampling is not None and lm_head is None:
+            raise ValueError("in-graph sampling needs the fp32 lm_head")
+        if lm_head is not None and chain:
+            raise ValueError("the decode chain runs GEMVs only; lm_head needs chain=False")
         dev = layers[0].wqkv.w.device
         hidden = layers[0].wqkv.K
         for i, l in enumerate(layers):
@@ -159,8 +175,10 @@ class DecodeStack:
                 raise ValueError(f"layer {i}: projections do not match hidden size {hidden}")
             if l.wgu.N != 2 * l.wd.K or l.wgu.N % 2:
                 raise ValueError(f"layer {i}: gate+up N={l.wgu.N} does not match down K={l.wd.K}")
-        if head.K != hidden:
+        if head is not None and head.K != hidden:
             raise ValueError("head K does not match the hidden size")
+        if lm_head is not None and (lm_head.dtype != torch.float32 or lm_head.dim() != 2 or lm_head.shape[1] != hidden):
+            raise ValueError("lm_head must be fp32 (V, hidden)")
         self.layers, self.head, self.ln_f = layers, head, ln_f
         self.rows, self.eps, self.hidden = rows, eps, hidden
         self.attn_cols = attn_cols or hidden
@@ -172,7 +190,31 @@ class DecodeStack:
         self.h = torch.zeros(rows, hidden, **bf)
         self.act = torch.zeros(rows, max(l.wd.K for l in layers), **bf)
         self.res = [torch.zeros(rows, hidden, **bf), torch.zeros(rows, hidden, **bf)]
-        self.logits = torch.zeros(rows, head.N, device=dev, dtype=torch.float32)
+        self.lm_head = lm_head
+        self.logits = torch.zeros(rows, lm_head.shape[0] if lm_head is not None else head.N, device=dev,
+                                  dtype=torch.float32)
+        self.sampling = None
+        if sampling is not None:
+            sp = dict(temperature=0.9, top_k=50, top_p=0.95, do_sample=True, guidance_scale=3.0,
+                      repetition_penalty=1.1, history_cap=2048, suppress=(0, 0), eos_id=-1, seed=0)
+            unknown = set(sampling) - set(sp)
+            if unknown:
+                raise ValueError(f"unknown sampling keys {sorted(unknown)}")
+            sp.update(sampling)
+            half = rows // 2 if rows >= 2 else rows
+            f = lambda v, dt: torch.full((half,), v, device=dev, dtype=dt)  # noqa: E731
+            self.sampling = sp
+            self.half, self.cfg = half, rows >= 2
+            self.temperature_buf = f(sp["temperature"], torch.float32)
+            self.top_k_buf = f(sp["top_k"], torch.int64)
+            self.top_p_buf = f(sp["top_p"], torch.float32)
+            self.do_sample_buf = f(1 if sp["do_sample"] else 0, torch.int64)
+            self.guidance_scale = f(sp["guidance_scale"], torch.float32)
+            self.history = torch.zeros(half, sp["history_cap"], device=dev, dtype=torch.int64)
+            self.history_len = torch.zeros(half, device=dev, dtype=torch.int32)
+            self.token = torch.zeros(rows, device=dev, dtype=torch.int64)
+            self.eos_flag = torch.zeros(1, device=dev, dtype=torch.int32)
+            self.rng = torch.tensor([sp["seed"], 0], device=dev, dtype=torch.int64)
         self.graph = None
         self.chain = None
         self.attention = attention
@@ -199,7 +241,7 @@ class DecodeStack:
 
     @property
     def weight_bytes(self) -> int:
-        b = self.head.nbytes + self.ln_f.numel() * 2
+        b = (self.head.nbytes if self.lm_head is None else self.lm_head.numel() * 4) + self.ln_f.numel() * 2
         for l in self.layers:
             b += l.wqkv.nbytes + l.wo.nbytes + l.wgu.nbytes + l.wd.nbytes + 2 * l.ln1.numel() * 2
         return b
@@ -215,7 +257,7 @@ class DecodeStack:
     def launches(self) -> int:
         if self.chain is not None:
             return 1
-        return (5 if self.attention else 4) * len(self.layers) + 1
+        return (5 if self.attention else 4) * len(self.layers) + 1 + (1 if self.sampling is not None else 0)
 
     def _ops(self):
         """(x, weight, out, gamma, epilogue, residual) of every launch, in order."""
@@ -230,7 +272,10 @@ class DecodeStack:
             y = self.res[i % 2]
             ops.append((act, l.wd, y, None, _lib.EPI_ADD_RESIDUAL, self.h))
             x = y
-        ops.append((x, self.head, self.logits, self.ln_f, _lib.EPI_NONE, None))
+        if self.lm_head is None:
+            ops.append((x, self.head, self.logits, self.ln_f, _lib.EPI_NONE, None))
+        else:
+            self._final = x
         return ops
 
     def run(self) -> torch.Tensor:
@@ -251,6 +296,17 @@ class DecodeStack:
                 x = self.attn_out
             _lib.gemv(x, qw.w, qw.wfmt, qw.N, scale=qw.scale, group=qw.group, gamma=gamma, eps=self.eps,
                       epilogue=epi, residual=res, out=out, flags=_lib.default_flags())
+        if self.lm_head is not None:
+            _lib.head_gemv(self._final, self.lm_head, _lib.HEAD_NK, gamma=self.ln_f, eps=self.eps, out=self.logits,
+                           flags=_lib.default_flags())
+        if self.sampling is not None:
+            sp = self.sampling
+            _lib.sample(self.logits, self.half, temperature=self.temperature_buf, top_k=self.top_k_buf,
+                        top_p=self.top_p_buf, do_sample=self.do_sample_buf, tokens=self.token,
+                        guidance=self.guidance_scale if self.cfg else None, max_k=self.logits.shape[1],
+                        mask=sp["suppress"], topk_by_value=True, rep_penalty=sp["repetition_penalty"],
+                        history=self.history, history_len=self.history_len, append_history=True, rng=self.rng,
+                        eos_id=sp["eos_id"], eos_flag=self.eos_flag, flags=_lib.default_flags())
         return self.logits
 
     def capture(self) -> None:

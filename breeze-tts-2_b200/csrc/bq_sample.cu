@@ -30,7 +30,7 @@ namespace {
 constexpr int kSampleThreads = 512;
 
 struct SampleParams {
-    int32_t rows, V, cfg, max_k, mask_lo, mask_hi, clamp_hi, topk_value, history_cap, flags_off;
+    int32_t rows, V, cfg, max_k, mask_lo, mask_hi, clamp_hi, topk_value, history_cap, flags_off, append;
     float rep_penalty;
     const float* logits;
     int64_t ldl;
@@ -39,8 +39,8 @@ struct SampleParams {
     const int64_t* top_k;
     const float* top_p;
     const int64_t* do_sample;
-    const int64_t* history;
-    const int32_t* history_len;
+    int64_t* history;
+    int32_t* history_len;
     const uint8_t* suppress;
     const float* uniform;
     unsigned long long* rng;
@@ -50,6 +50,8 @@ struct SampleParams {
     int64_t ldt;
     int64_t* tokens2;
     int64_t ldt2;
+    long long eos_id;
+    int32_t* eos_flag;
     unsigned int* arrive;
 };
 
@@ -147,6 +149,15 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
     pdl_launch_dependents();
     pdl_wait();  // logits (and the parameter buffers) come from earlier kernels
 
+    if (p.history && p.append && t == 0) {
+        // the row's current token (the previous step's draw) joins its history
+        const int n = p.history_len[r];
+        if (n < p.history_cap) {
+            p.history[int64_t(r) * p.history_cap + n] = p.tokens[int64_t(r) * p.ldt];
+            p.history_len[r] = n + 1;
+        }
+    }
+    __syncthreads();
     const bool pen = p.history != nullptr && p.rep_penalty != 1.f;
     if (pen) {
         for (int v = t; v < p.V; v += kSampleThreads) hflag[v] = 0;
@@ -268,6 +279,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
             p.tokens2[int64_t(r) * p.ldt2] = tok;
             if (p.cfg) p.tokens2[int64_t(r + p.rows) * p.ldt2] = tok;
         }
+        if (p.eos_flag && tok == p.eos_id) *p.eos_flag = 1;
         if (!p.uniform) {
             // the last CTA advances the call counter (every CTA has read it by now)
             __threadfence();
@@ -360,6 +372,9 @@ int32_t bq_sample(const bq_sample_desc* d, void* workspace, size_t workspace_byt
     p.ldt = d->ldt;
     p.tokens2 = d->tokens2;
     p.ldt2 = d->ldt2;
+    p.append = (d->flags & BQ_SAMPLE_APPEND_HISTORY) ? 1 : 0;
+    p.eos_id = d->eos_id;
+    p.eos_flag = d->eos_flag;
     p.arrive = static_cast<unsigned int*>(workspace);
     const int items = sample_items(d->V);
     const void* fn;

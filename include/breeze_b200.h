@@ -238,6 +238,10 @@ int32_t bq_head_gemv(const bq_head_desc* desc, void* workspace, size_t workspace
  * mix of BackboneGraph._decode_step (models/cudagraph/backbone_graph.py:275-285). */
 #define BQ_SAMPLE_TOPK_VALUE 2u /* top-k keeps every logit >= the k-th largest (sample_logits);
                                    default: the first k ranks (the depth graph's topk mask)   */
+#define BQ_SAMPLE_APPEND_HISTORY 4u /* before sampling, append the row's current token
+                                       (tokens[r * ldt]) to its history, as the backbone
+                                       loop does with the previous step's token
+                                       (models/fast_streaming.py:929-939)          */
 #define BQ_SAMPLE_MAX_V 8192
 
 typedef struct bq_sample_desc {
@@ -257,8 +261,8 @@ typedef struct bq_sample_desc {
     const int64_t* top_k;      /* int64 [rows] */
     const float* top_p;        /* fp32 [rows] */
     const int64_t* do_sample;  /* int64 [rows], 0 = greedy */
-    const int64_t* history;    /* int64 [rows, history_cap] or NULL */
-    const int32_t* history_len;/* int32 [rows] valid entries per history row */
+    int64_t* history;          /* int64 [rows, history_cap] or NULL */
+    int32_t* history_len;      /* int32 [rows] valid entries per history row */
     const uint8_t* suppress;   /* bool [V] or NULL */
     const float* uniform;      /* fp32 [rows] or NULL (Philox) */
     uint64_t* rng;             /* {seed, call counter}, required when uniform is NULL */
@@ -268,6 +272,8 @@ typedef struct bq_sample_desc {
     int64_t ldt;
     int64_t* tokens2;          /* optional second destination, same rule */
     int64_t ldt2;
+    int64_t eos_id;            /* token that sets *eos_flag (the backbone EOS class), or -1 */
+    int32_t* eos_flag;         /* set to 1 when a row draws eos_id; never cleared here; or NULL */
 } bq_sample_desc;
 
 /* 256 bytes (an arrival counter the kernel leaves at zero); zero-fill once. */

@@ -240,3 +240,32 @@ def test_sample_rejects_bad_args_cpu():
     h = L.HeadDesc()
     h.M, h.N, h.K, h.layout = 17, 10, 10, L.HEAD_NK
     assert lib.bq_head_workspace_bytes(ctypes.byref(h), ctypes.byref(ctypes.c_size_t())) != 0
+
+
+# The reference's own sampling tests (tests/test_logits_process.py), through bq_sample.
+@pytest.mark.gpu
+def test_reference_case_penalty_on_generated_history():
+    from breeze_b200 import _lib as L
+
+    dev = torch.device("cuda", 0)
+    tokens = torch.zeros(1, dtype=torch.int64, device=dev)
+    L.sample(torch.tensor([[1.0, 0.9, 0.1]], device=dev), 1, tokens=tokens, rep_penalty=2.0,
+             history=torch.tensor([[0]], device=dev), history_len=torch.tensor([1], dtype=torch.int32, device=dev),
+             uniform=torch.zeros(1, device=dev), **_params(1, dev, 1.0, 0, 1.0, 0))
+    assert int(tokens[0]) == 1
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("width", [2052, 2051])
+def test_reference_case_codec_mask(width):
+    from breeze_b200 import _lib as L
+
+    dev = torch.device("cuda", 0)
+    cfg_out = torch.zeros(1, width, device=dev)
+    L.sample(torch.zeros(1, width, device=dev), 1, tokens=torch.zeros(1, dtype=torch.int64, device=dev),
+             mask=(2048, 2051), cfg_out=cfg_out, uniform=torch.zeros(1, device=dev), **_params(1, dev, 1.0, 0, 1.0, 0))
+    torch.cuda.synchronize()
+    s = cfg_out.cpu()[0]
+    assert torch.isfinite(s[2047]) and torch.isneginf(s[2048:2051]).all()
+    if width > 2051:
+        assert torch.isfinite(s[2051])  # the backbone EOS class stays

@@ -186,3 +186,46 @@ def test_stack_with_attention_matches_oracle(rows):
     _check("o", st.h, st.attn_out, l.wo, epilogue=2, residual=st.res[0])
     _check("gate_up", st.act, st.h, l.wgu, gamma=l.ln2, epilogue=1)
     _check("head", st.logits, st.res[1], head, gamma=ln_f)
+
+
+@pytest.mark.gpu
+def test_stack_fp32_lm_head_and_in_graph_sampling():
+    """lm_head (fp32, norm fused) replaces the quantized head; the token is
+    drawn in the graph with CFG, repetition penalty over the appended history,
+    the suppressed range, and the EOS flag."""
+    from oracle import sampling as osm
+
+    S = _stack()
+    dev = torch.device("cuda", 0)
+    layers, _, ln_f = _small("int4", dev)
+    g = torch.Generator().manual_seed(21)
+    lm = torch.randn(300, 256, generator=g) * 0.05
+    st = S.DecodeStack(layers, None, ln_f, rows=2, lm_head=lm.to(dev),
+                       sampling=dict(do_sample=False, repetition_penalty=1.3, suppress=(296, 299), guidance_scale=2.0,
+                                     history_cap=8))
+    assert st.launches == 4 * 2 + 2
+    st.x.copy_(torch.randn(2, 256, generator=g).to(torch.bfloat16))
+    st.token.fill_(7)
+    st.capture()  # one eager warm-up step, then the graph
+    torch.cuda.synchronize()
+    assert int(st.history_len[0]) == 1 and int(st.history[0, 0]) == 7
+    ref = osm.head(st.res[1].cpu(), lm, False, ln_f.cpu(), 1e-6)
+    assert og.max_rel_err(st.logits.cpu(), ref) < 2e-3
+    mixed = osm.mixed_logits(st.logits.cpu(), 1, torch.tensor([2.0]), mask=(296, 299), rep_penalty=1.3,
+                             history=st.history.cpu(), history_len=st.history_len.cpu())
+    tok = int(torch.argmax(mixed[0]))
+    assert int(st.token[0]) == tok and int(st.token[1]) == tok
+    assert int(st.eos_flag[0]) == 0
+    prev = tok
+    st.replay()
+    torch.cuda.synchronize()
+    assert int(st.history_len[0]) == 2 and int(st.history[0, 1]) == prev
+    # EOS: a stack whose eos_id is the token it will draw raises the flag
+    st2 = S.DecodeStack(layers, None, ln_f, rows=2, lm_head=lm.to(dev),
+                        sampling=dict(do_sample=False, repetition_penalty=1.3, suppress=(296, 299),
+                                      guidance_scale=2.0, history_cap=8, eos_id=tok))
+    st2.x.copy_(st.x)
+    st2.token.fill_(7)
+    st2.run()
+    torch.cuda.synchronize()
+    assert int(st2.token[0]) == tok and int(st2.eos_flag[0]) == 1
