@@ -192,6 +192,10 @@ __device__ __forceinline__ uint32_t i4hi_to_f16x2(uint32_t w) {
 // Low lanes (bits 0-3 / 16-19): 1024 + q. High lanes (bits 4-7 / 20-23):
 // 1024 + 16 q. The GEMV pre-scales the activations that meet high lanes by
 // 1/16 and subtracts the offsets once per group from precomputed sums.
+// bf16 pair 128 + q from nibbles 0 and 4 of w (bits 0-3, 16-19): exact, one LOP3.
+__device__ __forceinline__ uint32_t i4_bf16(uint32_t w) {
+    return lop3<(0xF0 & 0xCC) | 0xAA>(w, 0x000F000Fu, 0x43004300u);
+}
 __device__ __forceinline__ uint32_t i4lo_raw(uint32_t w) {
     return lop3<(0xF0 & 0xCC) | 0xAA>(w, 0x000F000Fu, 0x64006400u);
 }

@@ -87,16 +87,19 @@ struct Fmt3<BQ_W_BF16> {
     static constexpr int kBoxes = 4;
     static constexpr bool kInt4 = false, kF16 = false;
 };
+// kF16: activations staged as f16 with a per-(warp, row) power-of-two scale
+// (fp8 / int8 weights convert exactly to f16); otherwise bf16 activations
+// (bf16 weights, and int4, whose codes dequantize to bf16 128 + q exactly).
 template <>
 struct Fmt3<BQ_W_INT4_TINYGEMM> {
     static constexpr int kBoxes = 1;
-    static constexpr bool kInt4 = true, kF16 = true;
+    static constexpr bool kInt4 = true, kF16 = false;
     static constexpr int kOfs = 8;
 };
 template <>
 struct Fmt3<BQ_W_INT4_PLAIN> {
     static constexpr int kBoxes = 1;
-    static constexpr bool kInt4 = true, kF16 = true;
+    static constexpr bool kInt4 = true, kF16 = false;
     static constexpr int kOfs = 0;
 };
 template <>
@@ -466,13 +469,59 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
     __syncwarp();
 
     // ---- staging: row groups of kp lanes, 16-byte units (8 values = one 8-k group)
-    {
-        int lg = 0;
-        while ((1 << lg) < M) ++lg;   // rows rounded up to a power of two
-        const int kp_log = 5 - lg, kp = 1 << kp_log;
-        const int lm = lane >> kp_log, lk = lane & (kp - 1);
+    int lg = 0;
+    while ((1 << lg) < M) ++lg;   // rows rounded up to a power of two
+    const int kp_log = 5 - lg, kp = 1 << kp_log;
+    const int lm = lane >> kp_log, lk = lane & (kp - 1);
+    const bool rowok = lm < M;
+    float ss_lane = 0.f;  // bf16 activations: this lane's share of sum(x^2), reduced after the main loop
+    if constexpr (!F::kF16) {
+        // One pass, no cross-lane dependency: x (times gamma) rounded to bf16 in
+        // place. int4 plain pairs {s0,s4},{s1,s5},.. to match its nibble order;
+        // tinygemm and bf16 weights take consecutive pairs, so with bf16 x and
+        // no norm the staged row is x itself and the pass is skipped.
+        const bool identity = FMT != BQ_W_INT4_PLAIN && !norm && p.x_bulk;
         const int nunits = 16 * nkw;
-        const bool rowok = lm < M;
+        const uint8_t* grow = smem + p.smem_gamma + warp * p.nkbw * 256;
+        uint8_t* xrow = xw_ptr + lm * pitch;
+        if (rowok && !identity) {
+#pragma unroll 2
+            for (int t = lk; t < nunits; t += kp) {
+                const int jj = t >> 4, off = jj * 256 + (t & 15) * 16;
+                float v[8];
+                if (p.x_bulk) {
+                    const uint4 r = *reinterpret_cast<const uint4*>(xrow + off);
+                    v[0] = bf16lo(r.x); v[1] = bf16hi(r.x); v[2] = bf16lo(r.y); v[3] = bf16hi(r.y);
+                    v[4] = bf16lo(r.z); v[5] = bf16hi(r.z); v[6] = bf16lo(r.w); v[7] = bf16hi(r.w);
+                } else {
+                    const int64_t base = int64_t(lm) * p.ldx + int64_t(kw0 + jj) * 128 + (t & 15) * 8;
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) v[e] = load_act(p.x, base + e, p.x_dtype);
+                }
+                if (norm) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) ss_lane = fmaf(v[e], v[e], ss_lane);
+                    const uint4 gv = *reinterpret_cast<const uint4*>(grow + off);
+                    v[0] *= bf16lo(gv.x); v[1] *= bf16hi(gv.x); v[2] *= bf16lo(gv.y); v[3] *= bf16hi(gv.y);
+                    v[4] *= bf16lo(gv.z); v[5] *= bf16hi(gv.z); v[6] *= bf16lo(gv.w); v[7] *= bf16hi(gv.w);
+                }
+                uint4 o;
+                if constexpr (FMT == BQ_W_INT4_PLAIN) {
+                    o.x = pack_bf162(v[0], v[4]);
+                    o.y = pack_bf162(v[1], v[5]);
+                    o.z = pack_bf162(v[2], v[6]);
+                    o.w = pack_bf162(v[3], v[7]);
+                } else {
+                    o.x = pack_bf162(v[0], v[1]);
+                    o.y = pack_bf162(v[2], v[3]);
+                    o.z = pack_bf162(v[4], v[5]);
+                    o.w = pack_bf162(v[6], v[7]);
+                }
+                *reinterpret_cast<uint4*>(xrow + off) = o;
+            }
+        }
+    } else {
+        const int nunits = 16 * nkw;
         const uint8_t* grow = smem + p.smem_gamma + warp * p.nkbw * 256;
         uint8_t* xrow = xw_ptr + lm * pitch;
         auto load8 = [&](int t, float (&v)[8]) {
@@ -526,7 +575,7 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
             amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
         }
         int e = 0;
-        if (F::kF16 && amax > 0.f && amax < INFINITY) {
+        if (amax > 0.f && amax < INFINITY) {
             int ex;
             frexpf(amax, &ex);
             e = min(max(ex - 15, -100), 100);
@@ -536,7 +585,7 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
             s_ss[warp * 16 + lm] = ss;
             s_up[warp * 16 + lm] = __int_as_float((127 + e) << 23);
         }
-        // pass 2: rewrite the row in place as f16 (bf16 for bf16 weights)
+        // pass 2: rewrite the row in place as f16 scaled by 2^-e
         if (rowok) {
 #pragma unroll 2
             for (int t = lk; t < nunits; t += kp) {
@@ -544,36 +593,10 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
                 float v[8];
                 load8(t, v);
                 uint4 o;
-                if constexpr (F::kInt4) {
-                    // activations that meet high-nibble operand lanes carry 1/16:
-                    // tinygemm k % 16 >= 8 (odd units), plain layout odd k
-                    float sc[8];
-#pragma unroll
-                    for (int q = 0; q < 8; ++q)
-                        sc[q] = ((FMT == BQ_W_INT4_TINYGEMM) ? (t & 1) : (q & 1)) ? down * 0.0625f : down;
-                    if constexpr (FMT == BQ_W_INT4_PLAIN) {
-                        // pair order {s0,s4},{s1,s5},{s2,s6},{s3,s7}
-                        o.x = pack_half2(v[0] * sc[0], v[4] * sc[4]);
-                        o.y = pack_half2(v[1] * sc[1], v[5] * sc[5]);
-                        o.z = pack_half2(v[2] * sc[2], v[6] * sc[6]);
-                        o.w = pack_half2(v[3] * sc[3], v[7] * sc[7]);
-                    } else {
-                        o.x = pack_half2(v[0] * sc[0], v[1] * sc[1]);
-                        o.y = pack_half2(v[2] * sc[2], v[3] * sc[3]);
-                        o.z = pack_half2(v[4] * sc[4], v[5] * sc[5]);
-                        o.w = pack_half2(v[6] * sc[6], v[7] * sc[7]);
-                    }
-                } else if constexpr (F::kF16) {
-                    o.x = pack_half2(v[0] * down, v[1] * down);
-                    o.y = pack_half2(v[2] * down, v[3] * down);
-                    o.z = pack_half2(v[4] * down, v[5] * down);
-                    o.w = pack_half2(v[6] * down, v[7] * down);
-                } else {
-                    o.x = pack_bf162(v[0], v[1]);
-                    o.y = pack_bf162(v[2], v[3]);
-                    o.z = pack_bf162(v[4], v[5]);
-                    o.w = pack_bf162(v[6], v[7]);
-                }
+                o.x = pack_half2(v[0] * down, v[1] * down);
+                o.y = pack_half2(v[2] * down, v[3] * down);
+                o.z = pack_half2(v[4] * down, v[5] * down);
+                o.w = pack_half2(v[6] * down, v[7] * down);
                 *reinterpret_cast<uint4*>(xrow + off) = o;
             }
         }
@@ -647,17 +670,15 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
                     const int i = sg * (8 / GPK) + ii;
 #pragma unroll
                     for (int mt = 0; mt < MT; ++mt)
-                        mma_f16(c2[ii & 1][mt], 0x3C003C00u, 0u, 0u, 0x3C003C00u, bf[mt][2 * i], bf[mt][2 * i + 1]);
+                        mma_bf16(c2[ii & 1][mt], 0x3F803F80u, 0u, 0x3F803F80u, 0u, bf[mt][2 * i], bf[mt][2 * i + 1]);
                 }
                 if (tg == 0) {
 #pragma unroll
                     for (int mt = 0; mt < MT; ++mt) {
-                        const float lo0 = c2[0][mt][0] + c2[1][mt][0], lo1 = c2[0][mt][1] + c2[1][mt][1];
-                        const float hi0 = c2[0][mt][2] + c2[1][mt][2], hi1 = c2[0][mt][3] + c2[1][mt][3];
-                        const float x0 = lo0 + 16.f * hi0, x1 = lo1 + 16.f * hi1;
-                        xsum4[((j * GPK + sg) * MT + mt) * 4 + tq] =
-                            make_float4(1024.f * (lo0 + hi0) + float(F::kOfs) * x0, x0,
-                                        1024.f * (lo1 + hi1) + float(F::kOfs) * x1, x1);
+                        // rows 0-7 of the indicator hold sum_k x over the 16-k chunks of this group
+                        const float x0 = c2[0][mt][0] + c2[1][mt][0], x1 = c2[0][mt][1] + c2[1][mt][1];
+                        constexpr float kMagic = 128.f + float(F::kOfs);  // dequantized code = 128 + q
+                        xsum4[((j * GPK + sg) * MT + mt) * 4 + tq] = make_float4(kMagic * x0, x0, kMagic * x1, x1);
                     }
                 }
             }
@@ -740,11 +761,11 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
                                     const int ki = sg * (8 / GPK) + ii;
                                     const uint32_t x0 = (ki & 1) ? (w0[ki >> 1] >> 8) : w0[ki >> 1];
                                     const uint32_t x1 = (ki & 1) ? (w1[ki >> 1] >> 8) : w1[ki >> 1];
-                                    const uint32_t a0 = i4lo_raw(x0), a2 = i4hi_raw(x0);
-                                    const uint32_t a1 = i4lo_raw(x1), a3 = i4hi_raw(x1);
+                                    const uint32_t a0 = i4_bf16(x0), a2 = i4_bf16(x0 >> 4);
+                                    const uint32_t a1 = i4_bf16(x1), a3 = i4_bf16(x1 >> 4);
 #pragma unroll
                                     for (int mt = 0; mt < MT; ++mt)
-                                        mma_f16(c2[ii % NCH][mt], a0, a1, a2, a3, bfr[kk][mt][2 * ki], bfr[kk][mt][2 * ki + 1]);
+                                        mma_bf16(c2[ii % NCH][mt], a0, a1, a2, a3, bfr[kk][mt][2 * ki], bfr[kk][mt][2 * ki + 1]);
                                 }
 #pragma unroll
                                 for (int h = 1; h < NCH; ++h)
@@ -841,8 +862,8 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
             const int m0 = 8 * mt + 2 * tq;
-            const float u0 = m0 < M ? s_up[warp * 16 + m0] : 0.f;
-            const float u1 = m0 + 1 < M ? s_up[warp * 16 + m0 + 1] : 0.f;
+            const float u0 = m0 < M ? (F::kF16 ? s_up[warp * 16 + m0] : 1.f) : 0.f;
+            const float u1 = m0 + 1 < M ? (F::kF16 ? s_up[warp * 16 + m0 + 1] : 1.f) : 0.f;
 #pragma unroll
             for (int i = 0; i < UGM; ++i) {
                 const int ul = g * UG + i;
@@ -854,6 +875,12 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
                                                                    acc[i][tile][mt][2] * u0, acc[i][tile][mt][3] * u1);
                 }
             }
+        }
+    }
+    if constexpr (!F::kF16) {
+        if (norm) {
+            for (int o = kp >> 1; o; o >>= 1) ss_lane += __shfl_xor_sync(0xffffffffu, ss_lane, o);
+            if (lk == 0 && lm < M) s_ss[warp * 16 + lm] = ss_lane;
         }
     }
     if (has_res) cp_async_wait_upto(0);  // this thread's residual pieces
