@@ -1,5 +1,5 @@
-// CFG mix and token sampling for sm_100a (bq_sample): one CTA of 512 threads
-// per sample row. The row's logits are mixed (cond/uncond), masked and
+// CFG mix and token sampling for sm_100a (bq_sample): one CTA (512 or 1024
+// threads, by vocabulary size) per sample row. The row's logits are mixed (cond/uncond), masked and
 // penalised in registers, sorted once (CUB block radix sort, descending), and
 // top-k, top-p, the softmax and the inverse-CDF draw all work on the sorted
 // order with block scans. Follows DepthDecoderGraph._cfg_sample
@@ -27,7 +27,6 @@ namespace bq {
 
 namespace {
 
-constexpr int kSampleThreads = 512;
 
 struct SampleParams {
     int32_t rows, V, cfg, max_k, mask_lo, mask_hi, clamp_hi, topk_value, history_cap, flags_off, append;
@@ -67,8 +66,8 @@ __device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint2 k) {
     return c;
 }
 
-// Block-wide helpers over kSampleThreads threads (scratch: 16 entries).
-template <bool MAX>
+// Block-wide helpers over THREADS threads (scratch: THREADS / 32 entries).
+template <int THREADS, bool MAX>
 __device__ __forceinline__ int block_reduce_int(int v, int* scratch) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
@@ -78,7 +77,7 @@ __device__ __forceinline__ int block_reduce_int(int v, int* scratch) {
     }
     if (lane == 0) scratch[warp] = v;
     __syncthreads();
-    v = lane < kSampleThreads / 32 ? scratch[lane] : (MAX ? INT_MIN : INT_MAX);
+    v = lane < THREADS / 32 ? scratch[lane] : (MAX ? INT_MIN : INT_MAX);
 #pragma unroll
     for (int o = 16; o; o >>= 1) {
         const int w = __shfl_xor_sync(0xffffffffu, v, o);
@@ -88,6 +87,7 @@ __device__ __forceinline__ int block_reduce_int(int v, int* scratch) {
     return v;
 }
 // (value, index) argmax: largest value, smallest index among equal values.
+template <int THREADS>
 __device__ __forceinline__ int block_argmax(float v, int i, float* sv, int* si) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
@@ -104,8 +104,8 @@ __device__ __forceinline__ int block_argmax(float v, int i, float* sv, int* si) 
         si[warp] = i;
     }
     __syncthreads();
-    v = lane < kSampleThreads / 32 ? sv[lane] : -INFINITY;
-    i = lane < kSampleThreads / 32 ? si[lane] : INT_MAX;
+    v = lane < THREADS / 32 ? sv[lane] : -INFINITY;
+    i = lane < THREADS / 32 ? si[lane] : INT_MAX;
 #pragma unroll
     for (int o = 16; o; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, v, o);
@@ -119,19 +119,19 @@ __device__ __forceinline__ int block_argmax(float v, int i, float* sv, int* si) 
     return i;
 }
 
-template <int ITEMS>
+template <int THREADS, int ITEMS>
 struct SampleTypes {
-    using Sort = cub::BlockRadixSort<float, kSampleThreads, ITEMS, int>;
-    using Scan = cub::BlockScan<float, kSampleThreads>;
+    using Sort = cub::BlockRadixSort<float, THREADS, ITEMS, int>;
+    using Scan = cub::BlockScan<float, THREADS>;
     union Temp {
         typename Sort::TempStorage sort;
         typename Scan::TempStorage scan;
     };
 };
 
-template <int ITEMS>
-__global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleParams p) {
-    using T = SampleTypes<ITEMS>;
+template <int THREADS, int ITEMS>
+__global__ void __launch_bounds__(THREADS) sample_kernel(const SampleParams p) {
+    using T = SampleTypes<THREADS, ITEMS>;
     extern __shared__ __align__(16) unsigned char smem[];
     auto& temp = *reinterpret_cast<typename T::Temp*>(smem);
     uint8_t* hflag = smem + p.flags_off;  // [V] repetition-penalty flags
@@ -160,10 +160,10 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
     __syncthreads();
     const bool pen = p.history != nullptr && p.rep_penalty != 1.f;
     if (pen) {
-        for (int v = t; v < p.V; v += kSampleThreads) hflag[v] = 0;
+        for (int v = t; v < p.V; v += THREADS) hflag[v] = 0;
         __syncthreads();
         const int n = min(p.history_len[r], p.history_cap);
-        for (int i = t; i < n; i += kSampleThreads) {
+        for (int i = t; i < n; i += THREADS) {
             const int64_t h = p.history[int64_t(r) * p.history_cap + i];
             if (h >= 0 && h < p.V) hflag[h] = 1;
         }
@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
             idx[j] = INT_MAX;
         }
     }
-    const int greedy = block_argmax(gv, gi, s_f, s_i);
+    const int greedy = block_argmax<THREADS>(gv, gi, s_f, s_i);
 
     // ---- sort descending; thread t then holds ranks [t * ITEMS, +ITEMS)
     typename T::Sort(temp.sort).SortDescending(key, idx);
@@ -259,8 +259,8 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
             last = rank;
         }
     }
-    first = block_reduce_int<false>(first, s_i);
-    last = block_reduce_int<true>(last, s_i);
+    first = block_reduce_int<THREADS, false>(first, s_i);
+    last = block_reduce_int<THREADS, true>(last, s_i);
     const int sel = first != INT_MAX ? first : last;  // u * z2 rounding up to z2 takes the last kept rank
     if (sel != INT_MIN && t == sel / ITEMS) {
 #pragma unroll
@@ -292,12 +292,10 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
     }
 }
 
-template <int ITEMS>
+template <int THREADS, int ITEMS>
 size_t sample_temp_bytes() {
-    return (sizeof(typename SampleTypes<ITEMS>::Temp) + 15) / 16 * 16;
+    return (sizeof(typename SampleTypes<THREADS, ITEMS>::Temp) + 15) / 16 * 16;
 }
-
-int sample_items(int V) { return V <= 2048 ? 4 : (V <= 4096 ? 8 : 16); }
 
 int validate_sample(const bq_sample_desc* d) {
     if (!d) return set_error(BQ_ERR_INVALID_ARG, "desc is NULL");
@@ -376,18 +374,22 @@ int32_t bq_sample(const bq_sample_desc* d, void* workspace, size_t workspace_byt
     p.eos_id = d->eos_id;
     p.eos_flag = d->eos_flag;
     p.arrive = static_cast<unsigned int*>(workspace);
-    const int items = sample_items(d->V);
+    // V <= 2048: 512 threads x 4 keys; <= 4096: 1024 x 4; <= 8192: 1024 x 8
     const void* fn;
     size_t temp;
-    if (items == 4) {
-        fn = reinterpret_cast<const void*>(&sample_kernel<4>);
-        temp = sample_temp_bytes<4>();
-    } else if (items == 8) {
-        fn = reinterpret_cast<const void*>(&sample_kernel<8>);
-        temp = sample_temp_bytes<8>();
+    int threads;
+    if (d->V <= 2048) {
+        fn = reinterpret_cast<const void*>(&sample_kernel<512, 4>);
+        temp = sample_temp_bytes<512, 4>();
+        threads = 512;
+    } else if (d->V <= 4096) {
+        fn = reinterpret_cast<const void*>(&sample_kernel<1024, 4>);
+        temp = sample_temp_bytes<1024, 4>();
+        threads = 1024;
     } else {
-        fn = reinterpret_cast<const void*>(&sample_kernel<16>);
-        temp = sample_temp_bytes<16>();
+        fn = reinterpret_cast<const void*>(&sample_kernel<1024, 8>);
+        temp = sample_temp_bytes<1024, 8>();
+        threads = 1024;
     }
     p.flags_off = int(temp);
     const uint32_t smem = uint32_t(temp + (size_t(d->V) + 15) / 16 * 16);
@@ -396,7 +398,7 @@ int32_t bq_sample(const bq_sample_desc* d, void* workspace, size_t workspace_byt
     cudaLaunchConfig_t cfg;
     std::memset(&cfg, 0, sizeof(cfg));
     cfg.gridDim = dim3(d->rows);
-    cfg.blockDim = dim3(kSampleThreads);
+    cfg.blockDim = dim3(threads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = static_cast<cudaStream_t>(stream);
     cudaLaunchAttribute attr[1];
