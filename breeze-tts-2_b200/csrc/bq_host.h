@@ -39,18 +39,6 @@ int ensure_smem_attr(const void* fn, uint32_t bytes);
 // [K/g, N, 2] scale/zero tensor.
 int encode_weight_maps(const bq_gemv_desc* d, CUtensorMap* tm_w, CUtensorMap* tm_sz);
 
-struct Gemv2Plan {
-    int rows, mt, upc, tpu, gpk;
-    int grid, owned, n_units, ring_slots, slot_bytes, nkbw, p_max, xrow_pitch;
-    int64_t total_chunks, ws_bytes;
-    uint32_t smem_bars, smem_ring, smem_x, smem_xsum, smem_gamma, smem_part, smem_misc, smem_total;
-};
-
-// v2 GEMV (CTA-owned units): rows per launch, plan, launch.
-int gemv2_rows_per_launch(const bq_gemv_desc* d);
-int plan_gemv2(const bq_gemv_desc* d, int rows, Gemv2Plan* pl);
-int launch_gemv2(const bq_gemv_desc* d, const Gemv2Plan& pl, int row0, void* workspace, cudaStream_t stream);
-
 struct Gemv3Plan {
     int rows, mt, upc, tpu, gpk, ug;
     int grid, owned, n_units, ring_slots, slot_bytes, nkbw, p_max, xrow_pitch;
