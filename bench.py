@@ -441,12 +441,19 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode-step", action="store_true", help="skip the 28-layer decode-step leg")
+    ap.add_argument("--depth-only", action="store_true",
+                    help="run only the depth-decoder frame leg (one GPU; for profiling) and print its JSON")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     rank, local_rank, world = dist_env()
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.depth_only:
+        device = torch.device("cuda", local_rank)
+        torch.cuda.set_device(device)
+        print(json.dumps({"depth_frame": depth_frame_bench(device, 1, local_rank)}), flush=True)
         return
     run_ours(args, rank, local_rank, world)
 
