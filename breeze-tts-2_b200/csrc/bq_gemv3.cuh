@@ -56,6 +56,7 @@ struct Gemv3Params {
     int32_t res_bulk;    // residual rows 16-byte aligned: copied with 16-byte cp.async
     int32_t upc;         // most units any CTA covers
     int32_t group_shift; // log2(group) for int4
+    int32_t ksplit;      // > 1: CTA = (unit group, K slice) rectangles; slices summed by the last arriver
     uint32_t smem_ring, smem_x, smem_xsum, smem_gamma, smem_part, smem_misc;
     const void* x;
     const void* w;
@@ -166,7 +167,9 @@ struct RingState {
     int issued, ig, ij;  // ring slots issued so far; next (group, k-slot) to issue
 };
 
-template <int FMT, int MT, int TPU, int GPK>
+// RECT: K split across CTAs (rectangles of units x a K slice; see the host
+// planner). A template parameter, so kernels without it carry none of its code.
+template <int FMT, int MT, int TPU, int GPK, bool RECT = false>
 __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, const int cta, const int phases,
                                          RingState& rst) {
     using F = Fmt3<FMT>;
@@ -184,7 +187,16 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
 
     // ---- this CTA's chunk range (32-bit: the host keeps grid * chunks < 2^32)
     uint32_t cb, ce;
-    if (p.owned) {
+    constexpr bool rect = RECT;
+    int kb_lo = 0, kb_hi = KB;  // this CTA's k-blocks (a K slice in rectangle mode)
+    if (rect) {
+        const int ngrp = p.grid / p.ksplit, ugi = cta / p.ksplit, ks = cta - ugi * p.ksplit;
+        const int u0 = int(int64_t(ugi) * p.n_units / ngrp), u1 = int(int64_t(ugi + 1) * p.n_units / ngrp);
+        kb_lo = ks * KB / p.ksplit;
+        kb_hi = (ks + 1) * KB / p.ksplit;
+        cb = uint32_t(u0) * uint32_t(KB) + uint32_t(kb_lo);
+        ce = uint32_t(u1 - 1) * uint32_t(KB) + uint32_t(kb_hi);
+    } else if (p.owned) {
         cb = (uint32_t(cta) * uint32_t(p.n_units) / uint32_t(p.grid)) * uint32_t(KB);
         ce = ((uint32_t(cta) + 1) * uint32_t(p.n_units) / uint32_t(p.grid)) * uint32_t(KB);
     } else {
@@ -198,6 +210,7 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
     const int lo0 = int(cb - uint32_t(u_first) * KB), hi_last = int((ce - 1) - uint32_t(u_last) * KB);
     const int ngroups = (nu + UG - 1) / UG;
     auto valid = [&](int ul, int kb) {
+        if (rect) return ul < nu && kb >= lo0 && kb <= hi_last;
         return ul < nu && (ul > 0 || kb >= lo0) && (ul < nu - 1 || kb <= hi_last);
     };
     auto any_valid = [&](int g, int kb) {
@@ -208,7 +221,8 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
     };
     // this warp's k-blocks: [kw0, kw0 + nkw), a contiguous eighth of K; a ring
     // slot carries KPS consecutive ones (index jp)
-    const int kw0 = (warp * KB) >> 3, nkw = (((warp + 1) * KB) >> 3) - kw0;
+    const int kw0 = kb_lo + ((warp * (kb_hi - kb_lo)) >> 3);
+    const int nkw = kb_lo + (((warp + 1) * (kb_hi - kb_lo)) >> 3) - kw0;
     const int nkp = (nkw + KPS - 1) / KPS;
     auto pair_valid = [&](int g, int jp) {
         bool v = false;
@@ -312,21 +326,36 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
             r0[0] = 16 * TPU * u_first;
             r1[0] = min(p.N, 16 * TPU * (u_first + nu));
         }
-        if (threadIdx.x == 0) {
+        if (!rect) {
+            if (threadIdx.x == 0) {
+                for (int q = 0; q < nr; ++q) {
+                    int64_t off = int64_t(r0[q]) * row_bytes;
+                    const int64_t end = int64_t(r1[q]) * row_bytes;
+                    for (; off < end; off += 65536)
+                        bulk_prefetch_l2(wg + off, uint32_t(end - off < 65536 ? end - off : 65536));
+                }
+            }
+        } else {
+            // the K slice of each 8-row tinygemm tile (contiguous k-blocks of 512 B), or of each row
+            const int tinygemm = FMT == BQ_W_INT4_TINYGEMM;
+            const int64_t kbytes = tinygemm ? 512 : row_bytes / KB;
+            const int64_t len = int64_t(kb_hi - kb_lo) * kbytes;
             for (int q = 0; q < nr; ++q) {
-                int64_t off = int64_t(r0[q]) * row_bytes;
-                const int64_t end = int64_t(r1[q]) * row_bytes;
-                for (; off < end; off += 65536)
-                    bulk_prefetch_l2(wg + off, uint32_t(end - off < 65536 ? end - off : 65536));
+                const int n0 = tinygemm ? r0[q] / 8 : r0[q], n1 = tinygemm ? (r1[q] + 7) / 8 : r1[q];
+                for (int n = n0 + int(threadIdx.x); n < n1; n += kConsumerThreads) {
+                    const int64_t off = tinygemm ? (int64_t(n) * KB + kb_lo) * 512 : int64_t(n) * row_bytes + kb_lo * kbytes;
+                    for (int64_t o = 0; o < len; o += 65536)
+                        bulk_prefetch_l2(wg + off + o, uint32_t(len - o < 65536 ? len - o : 65536));
+                }
             }
         }
         if constexpr (F::kInt4) {
             // scale/zero rows [r0, r1) of every group row: 128-byte lines
-            const int ngrp = p.K / p.group;
+            const int g_lo = (kb_lo * kKB) / p.group, ngrp = (kb_hi * kKB + p.group - 1) / p.group - g_lo;
             for (int q = 0; q < nr; ++q) {
                 const int lines = ((r1[q] - r0[q]) * 4 + 127) / 128 + 1;
                 for (int t = threadIdx.x; t < ngrp * lines; t += kConsumerThreads) {
-                    const int gr = t / lines, l = t - gr * lines;
+                    const int gr = g_lo + t / lines, l = t - (t / lines) * lines;
                     const int64_t a = (int64_t(gr) * p.N + r0[q]) * 4 + l * 128;
                     if (a < (int64_t(gr) * p.N + r1[q]) * 4) prefetch_l2(szg + a);
                 }
@@ -905,15 +934,21 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
             v[tile][3] = ((q[0].w + q[1].w) + (q[2].w + q[3].w)) + ((q[4].w + q[5].w) + (q[6].w + q[7].w));
         }
         const int m0 = 8 * mt + 2 * tq;
-        const bool full = (ul > 0 || lo0 == 0) && (ul < nu - 1 || hi_last == KB - 1);
+        const bool full = !rect && (ul > 0 || lo0 == 0) && (ul < nu - 1 || hi_last == KB - 1);
         if (!full) {
             // split mode: pieces = CTAs covering the unit, fixed summation order
-            const uint32_t c_first = uint32_t(unit) * KB, c_last = c_first + KB - 1;
-            const uint32_t T = uint32_t(p.total_chunks);
-            const int cta_f = int(((c_first + 1) * uint32_t(p.grid) - 1) / T);
-            const int cta_l = int(((c_last + 1) * uint32_t(p.grid) - 1) / T);
-            const int npieces = cta_l - cta_f + 1;
-            const int me = cta - cta_f;
+            int npieces, me;
+            if (rect) {
+                npieces = p.ksplit;  // one piece per K slice, in slice order
+                me = cta - (cta / p.ksplit) * p.ksplit;
+            } else {
+                const uint32_t c_first = uint32_t(unit) * KB, c_last = c_first + KB - 1;
+                const uint32_t T = uint32_t(p.total_chunks);
+                const int cta_f = int(((c_first + 1) * uint32_t(p.grid) - 1) / T);
+                const int cta_l = int(((c_last + 1) * uint32_t(p.grid) - 1) / T);
+                npieces = cta_l - cta_f + 1;
+                me = cta - cta_f;
+            }
             float* base = p.partials + (int64_t(unit) * p.p_max) * (TPU * 2 * 128);
             float* mine = base + int64_t(me) * (TPU * 2 * 128);
 #pragma unroll
@@ -1003,11 +1038,11 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
     }
 }
 
-template <int FMT, int MT, int TPU, int GPK>
+template <int FMT, int MT, int TPU, int GPK, bool RECT = false>
 __global__ void __launch_bounds__(kThreads3, 2) gemv3_kernel(const Gemv3Params p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     RingState rst;
-    gemv_cta<FMT, MT, TPU, GPK>(p, smem, int(blockIdx.x), kPhAll, rst);
+    gemv_cta<FMT, MT, TPU, GPK, RECT>(p, smem, int(blockIdx.x), kPhAll, rst);
 }
 
 // ---------------------------------------------------------------- decode chain

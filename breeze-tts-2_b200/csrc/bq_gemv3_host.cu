@@ -26,7 +26,9 @@ int gemv3_gpk(const bq_gemv_desc* d) { return gpk_of(d); }
 int gemv3_rows_per_launch(const bq_gemv_desc* d) {
     const DeviceInfo* dev = device_info();
     const int optin = dev ? dev->smem_optin : 232448;
-    const int KB = d->K / kKB;
+    // Without a norm the planner may split K across CTAs (up to 8 slices), so
+    // only a slice of the activations is staged per CTA.
+    const int KB = d->gamma ? d->K / kKB : (d->K / kKB + 7) / 8;
     const int nkbw = (KB + 7) / 8;
     const int64_t pitch = nkbw * 256 + 16;
     // smallest ring that still double-buffers: two slots of one two-tile unit per warp
@@ -38,19 +40,23 @@ int gemv3_rows_per_launch(const bq_gemv_desc* d) {
     return std::max(1, std::min(16, r));
 }
 
-int plan_gemv3(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int slots) {
+namespace {
+// One plan for a K split into `ks` slices (ks = 1: every CTA covers all of K).
+int plan_gemv3_ks(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int SMs, int ks) {
     const DeviceInfo* dev = device_info();
     if (!dev) return BQ_ERR_CUDA;
     const int fmt = d->wfmt;
-    const int SMs = slots > 0 ? slots : dev->sm_count;  // CTA slots the work is spread over
     const int KB = d->K / kKB;
+    if (ks > KB) return BQ_ERR_SHAPE;
     Gemv3Plan P;
     std::memset(&P, 0, sizeof(P));
     P.rows = rows;
     P.mt = rows > 8 ? 2 : 1;
-    P.nkbw = (KB + 7) / 8;
+    P.ksplit = ks;
+    P.nkbw = ((KB + ks - 1) / ks + 7) / 8;
     P.xrow_pitch = P.nkbw * 256 + 16;
     P.gpk = gpk_of(d);
+    const int SMu = std::max(1, SMs / ks);  // CTAs per K slice
 
     int64_t U;
     if (d->epilogue == BQ_EPI_SILU_MUL) {
@@ -59,10 +65,10 @@ int plan_gemv3(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int slots) {
     } else {
         const int64_t u32 = (d->N + 31) / 32, u16 = (d->N + 15) / 16;
         auto rows_per_cta = [&](int64_t u, int r) {
-            const int64_t g = std::min<int64_t>(SMs, u);
+            const int64_t g = std::min<int64_t>(SMu, u);
             return ((u + g - 1) / g) * r;
         };
-        P.tpu = rows_per_cta(u16, 16) < rows_per_cta(u32, 32) ? 1 : 2;
+        P.tpu = (ks > 1 || rows_per_cta(u16, 16) < rows_per_cta(u32, 32)) ? 1 : 2;  // rectangles: one-tile units
         U = P.tpu == 1 ? u16 : u32;
     }
     if (2 * U > kMaxUnits) return set_error(BQ_ERR_SHAPE, "N=%d too large for one launch", d->N);
@@ -72,7 +78,16 @@ int plan_gemv3(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int slots) {
     if ((T + 1) * int64_t(std::max(SMs, int((U + 3) / 4))) >= (int64_t(1) << 32))
         return set_error(BQ_ERR_SHAPE, "GEMV too large for one launch (N=%d, K=%d)", d->N, d->K);
     int upc_need;
-    if (U >= SMs / 2) {
+    if (ks > 1) {
+        // rectangles: a group of units x one K slice per CTA; the slices of a
+        // unit are summed by the last CTA to finish it (split-mode epilogue)
+        P.owned = 0;
+        int64_t ngrp = std::min<int64_t>(SMu, U);
+        if ((U + ngrp - 1) / ngrp > 4) ngrp = (U + 3) / 4;
+        P.grid = int(ngrp * ks);
+        upc_need = int((U + ngrp - 1) / ngrp);
+        P.p_max = ks;
+    } else if (U >= SMs / 2) {
         P.owned = 1;
         int64_t G = std::min<int64_t>(SMs, U);
         if ((U + G - 1) / G > 4) G = (U + 3) / 4;
@@ -148,6 +163,28 @@ int plan_gemv3(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int slots) {
     *pl = P;
     return BQ_OK;
 }
+}  // namespace
+
+int plan_gemv3(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int slots) {
+    const DeviceInfo* dev = device_info();
+    if (!dev) return BQ_ERR_CUDA;
+    // Without a norm (the row's sum of squares would need all of K), split K
+    // across CTAs when a CTA's activations for every k would not leave room
+    // for a co-resident dependent CTA: the smallest split that fits.
+    if (slots == 0 && !d->gamma && d->epilogue != BQ_EPI_SILU_MUL) {
+        for (int ks = 1; ks <= 8; ks *= 2) {
+            Gemv3Plan t;
+            if (plan_gemv3_ks(d, rows, &t, dev->sm_count, ks) == BQ_OK && t.smem_total <= kTargetSmem) {
+                *pl = t;
+                return BQ_OK;
+            }
+        }
+        // nothing leaves room for a dependent CTA: the finest split that fits at all
+        for (int ks = 8; ks >= 2; ks /= 2)
+            if (plan_gemv3_ks(d, rows, pl, dev->sm_count, ks) == BQ_OK) return BQ_OK;
+    }
+    return plan_gemv3_ks(d, rows, pl, slots > 0 ? slots : dev->sm_count, 1);
+}
 
 void fill_gemv3_params(const bq_gemv_desc* d, const Gemv3Plan& pl, int row0, void* workspace, Gemv3Params* out) {
     Gemv3Params& p = *out;
@@ -176,6 +213,7 @@ void fill_gemv3_params(const bq_gemv_desc* d, const Gemv3Plan& pl, int row0, voi
     p.p_max = pl.p_max;
     p.xrow_pitch = pl.xrow_pitch;
     p.upc = pl.upc;
+    p.ksplit = pl.ksplit > 1 ? pl.ksplit : 1;
     p.smem_ring = pl.smem_ring;
     p.smem_x = pl.smem_x;
     p.smem_xsum = pl.smem_xsum;
@@ -210,11 +248,11 @@ int launch_gemv3(const bq_gemv_desc* d, const Gemv3Plan& pl, int row0, void* wor
     const int fmt = d->wfmt;
     const void* fn = nullptr;
     if (int4fmt(fmt))
-        fn = gemv3_kernel_int4(fmt, pl.mt, pl.tpu, pl.gpk);
+        fn = gemv3_kernel_int4(fmt, pl.mt, pl.tpu, pl.gpk, pl.ksplit > 1);
     else if (fmt == BQ_W_BF16)
-        fn = gemv3_kernel_bf16(pl.mt, pl.tpu);
+        fn = gemv3_kernel_bf16(pl.mt, pl.tpu, pl.ksplit > 1);
     else
-        fn = gemv3_kernel_f8(fmt, pl.mt, pl.tpu);
+        fn = gemv3_kernel_f8(fmt, pl.mt, pl.tpu, pl.ksplit > 1);
     if (!fn) return set_error(BQ_ERR_FORMAT, "no GEMV kernel for format %d (group %d)", fmt, d->group);
 
     Gemv3Params p;

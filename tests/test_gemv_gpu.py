@@ -353,3 +353,22 @@ def test_workspace_shared_across_shapes():
         x = torch.randn(1, k, generator=torch.Generator().manual_seed(n)).to(torch.bfloat16)
         got = run_gemv(case, x, n, fmt="int4_tinygemm")
         assert gemv.max_rel_err(got.float(), x.float() @ case["deq"].T) < TOL, (n, k)
+
+
+# ---------------------------------------------------------------- K split across CTAs
+@pytest.mark.parametrize("fmt", FORMATS)
+@pytest.mark.parametrize("m,n,k,epi", [(16, 2048, 8192, 2), (32, 1024, 8192, 0), (8, 512, 16384, 2),
+                                       (12, 2048, 4096, 2), (16, 6144, 2048, 0)])
+def test_gemv_k_split_large_m(fmt, m, n, k, epi):
+    """Without a norm, activations that do not fit one CTA beside a dependent
+    CTA split K across CTAs (rectangles of units x K slices, summed by the last
+    arriver in slice order): parity with the oracle and bit-identical reruns."""
+    case = make_weight(fmt, n, k, seed=m + n + k)
+    g = torch.Generator().manual_seed(m * 3 + k)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    res = torch.randn(m, n, generator=g).to(torch.bfloat16) if epi == 2 else None
+    got = run_gemv(case, x, n, epilogue=epi, residual=res, fmt=fmt)
+    again = run_gemv(case, x, n, epilogue=epi, residual=res, fmt=fmt)
+    ref = gemv.fused_reference(x, case["deq"], None, 1e-6, epi, res)
+    assert gemv.max_rel_err(got.float(), ref) < TOL
+    assert torch.equal(got, again)
