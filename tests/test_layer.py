@@ -5,8 +5,9 @@ type; q/k norms included). CPU: construction keeps the reference's attributes
 and refuses nothing it accepts. GPU: after a 5-token prefill through the
 wrapped layer, one decode step through FusedDecoderLayer (bf16, fp8 and int4
 MLPs) matches the wrapped layer's own eager forward on a copy of the same
-static cache within max rel err 2e-2 (bf16 end to end), writes the same k / v
-at the cache position, and keeps the cache's own length counter; the int4
+static cache within max rel err 2e-2 (bf16 end to end), writes k / v at the
+cache position within 2 % (the projections round differently: fused RMSNorm in
+fp32 here, bf16 norm then matmul in the wrapped layer), and keeps the cache's own length counter; the int4
 gate and up modules end up as views of one tensor (no duplicate weight
 memory); install_fused_depth wraps every layer and runs its warm-up step.
 """
@@ -111,7 +112,8 @@ def test_fused_layer_decode_step_matches_wrapped_layer(mlp):
     assert og.max_rel_err(got.float().cpu(), ref.float().cpu()) < 2e-2
     kd = (cache.layers[0].keys[:, :, t0].float() - ref_cache.layers[0].keys[:, :, t0].float()).abs()
     assert float(kd.max()) <= 0.02 * float(ref_cache.layers[0].keys[:, :, t0].float().abs().max())
-    assert torch.equal(cache.layers[0].values[:, :, t0], ref_cache.layers[0].values[:, :, t0])
+    vd = (cache.layers[0].values[:, :, t0].float() - ref_cache.layers[0].values[:, :, t0].float()).abs()
+    assert float(vd.max()) <= 0.02 * float(ref_cache.layers[0].values[:, :, t0].float().abs().max())
     if n0 is not None:
         assert int(cache.layers[0].cumulative_length) == n0 + 1
 
