@@ -374,7 +374,7 @@ int32_t bq_sample(const bq_sample_desc* d, void* workspace, size_t workspace_byt
     p.eos_id = d->eos_id;
     p.eos_flag = d->eos_flag;
     p.arrive = static_cast<unsigned int*>(workspace);
-    // V <= 2048: 512 threads x 4 keys; <= 4096: 1024 x 4; <= 8192: 1024 x 8
+    // V <= 2048: 512 threads x 4 keys; <= 4096: 512 x 8 (1024 x 4 measured slower); <= 8192: 1024 x 8
     const void* fn;
     size_t temp;
     int threads;
@@ -383,9 +383,9 @@ int32_t bq_sample(const bq_sample_desc* d, void* workspace, size_t workspace_byt
         temp = sample_temp_bytes<512, 4>();
         threads = 512;
     } else if (d->V <= 4096) {
-        fn = reinterpret_cast<const void*>(&sample_kernel<1024, 4>);
-        temp = sample_temp_bytes<1024, 4>();
-        threads = 1024;
+        fn = reinterpret_cast<const void*>(&sample_kernel<512, 8>);
+        temp = sample_temp_bytes<512, 8>();
+        threads = 512;
     } else {
         fn = reinterpret_cast<const void*>(&sample_kernel<1024, 8>);
         temp = sample_temp_bytes<1024, 8>();
