@@ -54,6 +54,14 @@ struct SampleParams {
     unsigned int* arrive;
 };
 
+constexpr int kFastK = 128;  // top-k up to this size skips the full sort
+
+// Order-preserving unsigned image of a float (larger float -> larger key).
+__device__ __forceinline__ uint32_t ordered_bits(float f) {
+    const uint32_t b = __float_as_uint(f);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
 __device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint2 k) {
 #pragma unroll
     for (int i = 0; i < 10; ++i) {
@@ -139,6 +147,10 @@ __global__ void __launch_bounds__(THREADS) sample_kernel(const SampleParams p) {
     __shared__ int s_i[32];
     __shared__ int s_tok;
     __shared__ unsigned int s_last;
+    __shared__ unsigned int s_hist[256];
+    __shared__ int s_sel[4];
+    __shared__ float s_ck[kFastK], s_sk[kFastK];
+    __shared__ int s_ci[kFastK], s_si[kFastK];
     const int r = blockIdx.x, t = threadIdx.x;
 
     unsigned long long calls = 0, seed = 0;
@@ -205,12 +217,172 @@ __global__ void __launch_bounds__(THREADS) sample_kernel(const SampleParams p) {
     }
     const int greedy = block_argmax<THREADS>(gv, gi, s_f, s_i);
 
-    // ---- sort descending; thread t then holds ranks [t * ITEMS, +ITEMS)
-    typename T::Sort(temp.sort).SortDescending(key, idx);
-    __syncthreads();
     int k = int(p.top_k[r]);
     if (k <= 0) k = p.max_k;
     k = max(1, min(k, min(p.max_k, p.V)));
+    float u;
+    if (p.uniform) {
+        u = p.uniform[r];
+    } else {
+        const uint4 c = philox4x32_10(make_uint4(uint32_t(calls), uint32_t(calls >> 32), uint32_t(r), 0u),
+                                      make_uint2(uint32_t(seed), uint32_t(seed >> 32)));
+        u = float(c.x >> 8) * (1.0f / 16777216.0f);
+    }
+    const float tp = p.top_p[r];
+    int sel = INT_MIN;  // rank of the drawn token among the kept ones (INT_MIN: nothing kept)
+    bool done = false;
+
+    // ---- fast path (k <= kFastK): radix-select the k-th largest scaled logit
+    // (4 passes of 8 bits over order-preserving keys), keep the candidates
+    // (ties at the threshold by ascending index for rank-based top-k), rank
+    // them by counting and finish top-p, softmax and the draw in one warp.
+    if (k <= kFastK) {
+        uint32_t uk[ITEMS];
+#pragma unroll
+        for (int j = 0; j < ITEMS; ++j) uk[j] = ordered_bits(key[j]);
+        uint32_t prefix = 0, pmask = 0;
+        int rem = k;
+#pragma unroll 1
+        for (int pass = 0; pass < 4; ++pass) {
+            const int shift = 24 - 8 * pass;
+            for (int i = t; i < 256; i += THREADS) s_hist[i] = 0;
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < ITEMS; ++j)
+                if ((uk[j] & pmask) == prefix) atomicAdd(&s_hist[(uk[j] >> shift) & 255u], 1u);
+            __syncthreads();
+            if (t < 32) {
+                // lane l owns bins 255 - 8l - q (q = 0..7), largest digits first
+                int c[8], sum = 0;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    c[q] = int(s_hist[255 - 8 * t - q]);
+                    sum += c[q];
+                }
+                int incl = sum;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (t >= o) incl += v;
+                }
+                const int excl = incl - sum;
+                if (excl < rem && rem <= incl) {
+                    int acc = excl;
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        if (acc + c[q] >= rem) {
+                            s_sel[0] = 255 - 8 * t - q;
+                            s_sel[1] = acc;
+                            break;
+                        }
+                        acc += c[q];
+                    }
+                }
+            }
+            __syncthreads();
+            prefix |= uint32_t(s_sel[0]) << shift;
+            pmask |= 0xFFu << shift;
+            rem -= s_sel[1];
+            __syncthreads();
+        }
+        // candidates: above the threshold, plus ties at it (the first `rem` by index for rank-based top-k)
+        float tf[ITEMS], tr[ITEMS], tot;
+#pragma unroll
+        for (int j = 0; j < ITEMS; ++j) tf[j] = uk[j] == prefix ? 1.f : 0.f;
+        typename T::Scan(temp.scan).ExclusiveSum(tf, tr, tot);
+        __syncthreads();
+        float take[ITEMS], pos[ITEMS], nc_f;
+#pragma unroll
+        for (int j = 0; j < ITEMS; ++j) {
+            const bool tk = key[j] > -INFINITY &&
+                            (uk[j] > prefix || (uk[j] == prefix && (p.topk_value || tr[j] < float(rem))));
+            take[j] = tk ? 1.f : 0.f;
+        }
+        typename T::Scan(temp.scan).ExclusiveSum(take, pos, nc_f);
+        __syncthreads();
+        const int nc = int(nc_f);
+        if (nc <= kFastK) {
+#pragma unroll
+            for (int j = 0; j < ITEMS; ++j) {
+                if (take[j] > 0.f) {
+                    s_ck[int(pos[j])] = key[j];
+                    s_ci[int(pos[j])] = idx[j];
+                }
+            }
+            __syncthreads();
+            for (int c = t; c < nc; c += THREADS) {
+                const float kc = s_ck[c];
+                const int ic = s_ci[c];
+                int rk = 0;
+                for (int i = 0; i < nc; ++i) rk += (s_ck[i] > kc || (s_ck[i] == kc && s_ci[i] < ic)) ? 1 : 0;
+                s_sk[rk] = kc;
+                s_si[rk] = ic;
+            }
+            __syncthreads();
+            if (t < 32) {
+                // lane l holds ranks 4l .. 4l + 3
+                const float mx = nc > 0 ? s_sk[0] : 0.f;
+                float e[4], sum = 0.f;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int rk = 4 * t + q;
+                    e[q] = rk < nc ? expf(s_sk[rk] - mx) : 0.f;
+                    sum += e[q];
+                }
+                float incl = sum;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const float v = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (t >= o) incl += v;
+                }
+                const float z = __shfl_sync(0xffffffffu, incl, 31);
+                float ex = incl - sum;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int rk = 4 * t + q;
+                    if (rk >= 1 && ex / z > tp) e[q] = 0.f;  // mass before this rank exceeds top_p
+                    ex += rk < nc ? expf(s_sk[rk] - mx) : 0.f;
+                }
+                sum = e[0] + e[1] + e[2] + e[3];
+                incl = sum;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const float v = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (t >= o) incl += v;
+                }
+                const float z2 = __shfl_sync(0xffffffffu, incl, 31);
+                const float target = u * z2;
+                float cum = incl - sum;
+                int first = INT_MAX, last = INT_MIN;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    cum += e[q];
+                    if (e[q] > 0.f) {
+                        if (first == INT_MAX && cum > target) first = 4 * t + q;
+                        last = 4 * t + q;
+                    }
+                }
+#pragma unroll
+                for (int o = 16; o; o >>= 1) {
+                    first = min(first, __shfl_xor_sync(0xffffffffu, first, o));
+                    last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
+                }
+                if (t == 0) {
+                    const int sl = first != INT_MAX ? first : last;
+                    s_sel[2] = sl;
+                    if (sl != INT_MIN) s_tok = s_si[sl];
+                }
+            }
+            __syncthreads();
+            sel = s_sel[2];
+            done = true;
+        }
+    }
+
+    if (!done) {
+    // ---- sort descending; thread t then holds ranks [t * ITEMS, +ITEMS)
+    typename T::Sort(temp.sort).SortDescending(key, idx);
+    __syncthreads();
     if (t == 0) s_f[0] = key[0];
     if (t == (k - 1) / ITEMS) {
 #pragma unroll
@@ -230,7 +402,6 @@ __global__ void __launch_bounds__(THREADS) sample_kernel(const SampleParams p) {
     float excl[ITEMS], z;
     typename T::Scan(temp.scan).ExclusiveSum(e, excl, z);
     __syncthreads();
-    const float tp = p.top_p[r];
 #pragma unroll
     for (int j = 0; j < ITEMS; ++j) {
         const int rank = t * ITEMS + j;
@@ -241,14 +412,6 @@ __global__ void __launch_bounds__(THREADS) sample_kernel(const SampleParams p) {
     __syncthreads();
 
     // ---- one draw: the first kept rank whose cumulative mass exceeds u * z2
-    float u;
-    if (p.uniform) {
-        u = p.uniform[r];
-    } else {
-        const uint4 c = philox4x32_10(make_uint4(uint32_t(calls), uint32_t(calls >> 32), uint32_t(r), 0u),
-                                      make_uint2(uint32_t(seed), uint32_t(seed >> 32)));
-        u = float(c.x >> 8) * (1.0f / 16777216.0f);
-    }
     const float target = u * z2;
     int first = INT_MAX, last = INT_MIN;
 #pragma unroll
@@ -261,11 +424,12 @@ __global__ void __launch_bounds__(THREADS) sample_kernel(const SampleParams p) {
     }
     first = block_reduce_int<THREADS, false>(first, s_i);
     last = block_reduce_int<THREADS, true>(last, s_i);
-    const int sel = first != INT_MAX ? first : last;  // u * z2 rounding up to z2 takes the last kept rank
+    sel = first != INT_MAX ? first : last;  // u * z2 rounding up to z2 takes the last kept rank
     if (sel != INT_MIN && t == sel / ITEMS) {
 #pragma unroll
         for (int j = 0; j < ITEMS; ++j)
             if (j == sel % ITEMS) s_tok = idx[j];
+    }
     }
     __syncthreads();
     if (t == 0) {
