@@ -372,6 +372,54 @@ def depth_frame_bench(device, world: int, local_rank: int, replays: int = 10, wa
             "replays_timed": replays, "results": out}
 
 
+def shape_bench(device, spec: str, steps: int, warmup: int):
+    """One GEMV shape as a CUDA graph over rotated weight copies (> 4x L2), PDL
+    between calls; device time per call. For per-shape numbers and targeted
+    profiles."""
+    from breeze_b200 import _lib
+    from breeze_b200.fused.stack import synthetic_weight
+
+    fmt, n, k, m, epi = spec.split(":")
+    n, k, m, epi = int(n), int(k), int(m), int(epi)
+    g = torch.Generator(device=device).manual_seed(0)
+    w0 = synthetic_weight(fmt, n, k, device, g)
+    l2 = torch.cuda.get_device_properties(device).L2_cache_size
+    r = max(8, (4 * l2) // w0.nbytes + 1)
+    copies = [w0] + [synthetic_weight(fmt, n, k, device, g) for _ in range(r - 1)]
+    x = torch.randn(m, k, device=device, generator=g).to(torch.bfloat16)
+    gamma = (1 + 0.1 * torch.randn(k, device=device, generator=g)).to(torch.bfloat16) if epi != 2 else None
+    res = torch.randn(m, n, device=device, generator=g).to(torch.bfloat16) if epi == 2 else None
+    out = torch.empty(m, n // 2 if epi == 1 else n, device=device, dtype=torch.bfloat16)
+
+    def step():
+        for q in copies:
+            _lib.gemv(x, q.w, q.wfmt, q.N, scale=q.scale, group=q.group, gamma=gamma, epilogue=epi, residual=res,
+                      out=out, flags=_lib.default_flags())
+
+    step()
+    torch.cuda.synchronize(device)
+    s = torch.cuda.Stream(device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(s):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            step()
+    torch.cuda.current_stream(device).wait_stream(s)
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize(device)
+    us = e0.elapsed_time(e1) * 1e3 / (steps * r)
+    algo = w0.nbytes + m * k * 2 + out.numel() * 2 + (0 if gamma is None else k * 2) + (0 if res is None else res.numel() * 2)
+    return {"shape": spec, "us_per_call": round(us, 2), "GBps": round(algo / us / 1e3, 1), "calls_per_replay": r,
+            "algorithmic_bytes_per_call": algo}
+
+
 def _cpu_inputs():
     g = torch.Generator().manual_seed(1234)
     codes = torch.randint(0, 16, (N, K), generator=g, dtype=torch.int32).to(torch.uint8)
@@ -441,6 +489,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode-step", action="store_true", help="skip the 28-layer decode-step leg")
+    ap.add_argument("--shape", default=None, metavar="FMT:N:K:M:EPI",
+                    help="time one GEMV shape (fmt int4|fp8|int8|bf16, epilogue 0 none / 1 SiLU*up / 2 residual; "
+                         "RMSNorm unless EPI is 2) over rotated weight copies > 4x L2 and print its JSON")
     ap.add_argument("--depth-only", action="store_true",
                     help="run only the depth-decoder frame leg (one GPU; for profiling) and print its JSON")
     args = ap.parse_args()
@@ -449,6 +500,11 @@ def main():
     rank, local_rank, world = dist_env()
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.shape:
+        device = torch.device("cuda", local_rank)
+        torch.cuda.set_device(device)
+        print(json.dumps(shape_bench(device, args.shape, args.steps, args.warmup)), flush=True)
         return
     if args.depth_only:
         device = torch.device("cuda", local_rank)

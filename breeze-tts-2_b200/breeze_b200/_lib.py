@@ -274,11 +274,38 @@ def _rowmajor(t: torch.Tensor, name: str) -> torch.Tensor:
     return t
 
 
+# Descriptors of calls that name their output buffer, keyed by every pointer,
+# shape, stride and dtype the descriptor holds: a repeated call (a decode loop
+# over static buffers) skips validation, descriptor construction and the
+# workspace query and goes straight to bq_gemv.
+_GEMV_CACHE: dict = {}
+_GEMV_CACHE_MAX = 4096
+
+
+def _gemv_key(x, w, wfmt, n, scale, group, gamma, eps, epilogue, residual, bias, out, flags):
+    return (x.data_ptr(), x.shape, x.stride(), x.dtype, x.device, w.data_ptr(), wfmt, n,
+            None if scale is None else scale.data_ptr(), group,
+            None if gamma is None else (gamma.data_ptr(), gamma.dtype), eps, epilogue,
+            None if residual is None else (residual.data_ptr(), residual.shape, residual.stride(), residual.dtype),
+            None if bias is None else (bias.data_ptr(), bias.dtype),
+            out.data_ptr(), out.shape, out.stride(), out.dtype, flags)
+
+
 def gemv(x: torch.Tensor, w: torch.Tensor, wfmt: int, n: int, *, scale=None, group: int = 128, gamma=None,
          eps: float = 1e-6, epilogue: int = EPI_NONE, residual=None, bias=None, out: torch.Tensor | None = None,
          out_dtype: torch.dtype | None = None, flags: int = 0) -> torch.Tensor:
     """out = epilogue(rmsnorm(x) @ dequant(w)^T) on the current stream."""
+    key = None
+    if out is not None and x.is_cuda:
+        key = _gemv_key(x, w, wfmt, n, scale, group, gamma, eps, epilogue, residual, bias, out, flags)
+        hit = _GEMV_CACHE.get(key)
+        if hit is not None:
+            d, ws = hit
+            check(_lib.bq_gemv(ctypes.byref(d), ws.data_ptr(), ws.numel(), torch.cuda.current_stream(x.device).cuda_stream),
+                  "bq_gemv")
+            return out
     dev = _require_cuda(x, w, scale, gamma, residual, bias, out)
+    own = (_ptr(gamma), _ptr(bias))  # the caller's own tensors, before any dtype conversion
     x = _rowmajor(x, "x")
     if x.dtype not in _DT:
         raise ValueError(f"unsupported activation dtype {x.dtype}")
@@ -302,6 +329,11 @@ def gemv(x: torch.Tensor, w: torch.Tensor, wfmt: int, n: int, *, scale=None, gro
     check(lib.bq_gemv_workspace_bytes(ctypes.byref(d), ctypes.byref(need)), "bq_gemv_workspace_bytes")
     ws = WORKSPACE.get(dev, need.value)
     check(lib.bq_gemv(ctypes.byref(d), ws.data_ptr(), ws.numel(), _stream(dev)), "bq_gemv")
+    # cache only descriptors that point at the caller's own tensors (no converted copies)
+    if key is not None and (d.gamma, d.bias) == own:
+        if len(_GEMV_CACHE) >= _GEMV_CACHE_MAX:
+            _GEMV_CACHE.clear()
+        _GEMV_CACHE[key] = (d, ws)
     return out
 
 
