@@ -2,7 +2,10 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <array>
 #include <cstring>
+#include <map>
+#include <mutex>
 
 #include "bq_gemv3.cuh"
 #include "bq_gemv3_kinst.h"
@@ -165,7 +168,38 @@ int plan_gemv3_ks(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int SMs, int k
 }
 }  // namespace
 
+namespace {
+// Plans depend only on the shape, format, epilogue, norm and device: cached,
+// so a decode loop's repeated calls skip the layout search.
+std::mutex g_plan_mu;
+std::map<std::array<int, 9>, Gemv3Plan> g_plans;
+int plan_gemv3_uncached(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int slots);
+}  // namespace
+
 int plan_gemv3(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int slots) {
+    const DeviceInfo* dev = device_info();
+    if (!dev) return BQ_ERR_CUDA;
+    const std::array<int, 9> key{dev->device, rows, d->N, d->K, d->wfmt, d->group, d->epilogue,
+                                 d->gamma != nullptr ? 1 : 0, slots};
+    {
+        std::lock_guard<std::mutex> lk(g_plan_mu);
+        auto it = g_plans.find(key);
+        if (it != g_plans.end()) {
+            *pl = it->second;
+            return BQ_OK;
+        }
+    }
+    const int rc = plan_gemv3_uncached(d, rows, pl, slots);
+    if (rc == BQ_OK) {
+        std::lock_guard<std::mutex> lk(g_plan_mu);
+        if (g_plans.size() > 65536) g_plans.clear();
+        g_plans.emplace(key, *pl);
+    }
+    return rc;
+}
+
+namespace {
+int plan_gemv3_uncached(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int slots) {
     const DeviceInfo* dev = device_info();
     if (!dev) return BQ_ERR_CUDA;
     // Without a norm (the row's sum of squares would need all of K), split K
@@ -185,6 +219,7 @@ int plan_gemv3(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int slots) {
     }
     return plan_gemv3_ks(d, rows, pl, slots > 0 ? slots : dev->sm_count, 1);
 }
+}  // namespace
 
 void fill_gemv3_params(const bq_gemv_desc* d, const Gemv3Plan& pl, int row0, void* workspace, Gemv3Params* out) {
     Gemv3Params& p = *out;
