@@ -159,8 +159,9 @@ __global__ void __launch_bounds__(kAttnThreads) attention_step_kernel(const Attn
 #pragma unroll
         for (int e = 0; e < DPL; ++e) s_q[g][lane * DPL + e] = v[e] * p.scale;
     }
-    // the new k (normed, roped, rounded to the cache dtype) and v
-    if (warp == 0) {
+    // the new k (normed, roped, rounded to the cache dtype) and v, on a warp
+    // that has no query head when G < 4, so it runs beside the q heads
+    if (warp == (G < 4 ? G : 3)) {
         float v[DPL];
         const __nv_bfloat16* k = row + (p.HQ + j) * D + lane * DPL;
 #pragma unroll

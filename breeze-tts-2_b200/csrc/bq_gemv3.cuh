@@ -35,6 +35,11 @@
 
 namespace bq {
 
+template <int V>
+struct KConst {
+    static constexpr int value = V;
+};
+
 struct Gemv3Params {
     int32_t M, N, K, KB;
     int32_t epi, group, x_dtype, out_dtype, res_dtype;
@@ -169,7 +174,9 @@ struct RingState {
 
 // RECT: K split across CTAs (rectangles of units x a K slice; see the host
 // planner). A template parameter, so kernels without it carry none of its code.
-template <int FMT, int MT, int TPU, int GPK, bool RECT = false>
+// EVEN: the host guarantees every warp an even number of k-blocks, so every ring
+// slot of a one-row kernel is full and the half-slot body is not compiled.
+template <int FMT, int MT, int TPU, int GPK, bool RECT = false, bool EVEN = false>
 __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, const int cta, const int phases,
                                          RingState& rst) {
     using F = Fmt3<FMT>;
@@ -735,21 +742,25 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
             // (x and residual count for the first f0 slots)
             cp_async_wait_upto(issued - 1 - consumed + (consumed < f0 ? 2 : 0));
             __syncwarp();
-            {
+            // KH = k-blocks of this slot inside the warp's range: KPS, or 1 for the last slot of a
+            // warp with an odd count (e.g. K = 1024); a compile-time count keeps the full-slot body
+            // free of per-k-block branches
+            auto slot_body = [&](auto kh_c) {
+                constexpr int KH = decltype(kh_c)::value;
                 const uint8_t* src0 = smem + p.smem_ring + (warp * RS + slot) * p.slot_bytes;
                 uint32_t bfr[KPS][MT][16];
                 // int4: per-group (A, X) of columns m0, m0+1 from indicator MMAs
                 float sA[KPS][GPK][MT][2], sX[KPS][GPK][MT][2];
 #pragma unroll
                 for (int kk = 0; kk < KPS; ++kk) {
-                    // a k-block past this warp's range reads real activations against zero-filled weights
-                    const int jj = jp * KPS + kk < nkw ? jp * KPS + kk : nkw - 1;
-                    load_bfrag(jj, bfr[kk]);
+                    if (kk >= KH) continue;
+                    load_bfrag(jp * KPS + kk, bfr[kk]);
                 }
                 if constexpr (F::kInt4) {
 #pragma unroll
                     for (int kk = 0; kk < KPS; ++kk) {
-                        const int jj = jp * KPS + kk < nkw ? jp * KPS + kk : nkw - 1;
+                        if (kk >= KH) continue;
+                        const int jj = jp * KPS + kk;
 #pragma unroll
                         for (int sg = 0; sg < GPK; ++sg)
 #pragma unroll
@@ -769,6 +780,7 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
                     for (int tile = 0; tile < TPU; ++tile)
 #pragma unroll
                     for (int kk = 0; kk < KPS; ++kk) {
+                        if (kk >= KH) continue;
                         const uint8_t* src = src0 + ((kk * UG + i) * TPU + tile) * tile_bytes;
                         if constexpr (F::kInt4) {
                             const uint4 r0 = *reinterpret_cast<const uint4*>(src + lane * 16);
@@ -871,6 +883,14 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
                         }
                     }
                 }
+            };
+            if constexpr (KPS == 1 || EVEN) {
+                slot_body(KConst<KPS>{});
+            } else {
+                if (jp * KPS + KPS <= nkw)
+                    slot_body(KConst<KPS>{});
+                else
+                    slot_body(KConst<1>{});
             }
             __syncwarp();  // every lane is done reading the slot: refill it
             ++consumed;
@@ -1038,11 +1058,11 @@ __device__ __forceinline__ void gemv_cta(const Gemv3Params& p, uint8_t* smem, co
     }
 }
 
-template <int FMT, int MT, int TPU, int GPK, bool RECT = false>
+template <int FMT, int MT, int TPU, int GPK, bool RECT = false, bool EVEN = false>
 __global__ void __launch_bounds__(kThreads3, 2) gemv3_kernel(const Gemv3Params p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     RingState rst;
-    gemv_cta<FMT, MT, TPU, GPK, RECT>(p, smem, int(blockIdx.x), kPhAll, rst);
+    gemv_cta<FMT, MT, TPU, GPK, RECT, EVEN>(p, smem, int(blockIdx.x), kPhAll, rst);
 }
 
 // ---------------------------------------------------------------- decode chain

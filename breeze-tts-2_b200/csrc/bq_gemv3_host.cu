@@ -57,6 +57,15 @@ int plan_gemv3_ks(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int SMs, int k
     P.mt = rows > 8 ? 2 : 1;
     P.ksplit = ks;
     P.nkbw = ((KB + ks - 1) / ks + 7) / 8;
+    // k-block ranges exactly as the kernel derives them: slice [s*KB/ks, (s+1)*KB/ks), a warp
+    // an eighth of it; all even lets the one-row kernels (two k-blocks per ring slot) drop
+    // the half-slot path
+    P.even_k = 1;
+    for (int s = 0; s < ks; ++s) {
+        const int n = (s + 1) * KB / ks - s * KB / ks;
+        for (int w = 0; w < 8; ++w)
+            if (((((w + 1) * n) >> 3) - ((w * n) >> 3)) & 1) P.even_k = 0;
+    }
     P.xrow_pitch = P.nkbw * 256 + 16;
     P.gpk = gpk_of(d);
     const int SMu = std::max(1, SMs / ks);  // CTAs per K slice
@@ -283,11 +292,11 @@ int launch_gemv3(const bq_gemv_desc* d, const Gemv3Plan& pl, int row0, void* wor
     const int fmt = d->wfmt;
     const void* fn = nullptr;
     if (int4fmt(fmt))
-        fn = gemv3_kernel_int4(fmt, pl.mt, pl.tpu, pl.gpk, pl.ksplit > 1);
+        fn = gemv3_kernel_int4(fmt, pl.mt, pl.tpu, pl.gpk, pl.ksplit > 1, pl.even_k != 0);
     else if (fmt == BQ_W_BF16)
-        fn = gemv3_kernel_bf16(pl.mt, pl.tpu, pl.ksplit > 1);
+        fn = gemv3_kernel_bf16(pl.mt, pl.tpu, pl.ksplit > 1, pl.even_k != 0);
     else
-        fn = gemv3_kernel_f8(fmt, pl.mt, pl.tpu, pl.ksplit > 1);
+        fn = gemv3_kernel_f8(fmt, pl.mt, pl.tpu, pl.ksplit > 1, pl.even_k != 0);
     if (!fn) return set_error(BQ_ERR_FORMAT, "no GEMV kernel for format %d (group %d)", fmt, d->group);
 
     Gemv3Params p;

@@ -41,6 +41,7 @@ int encode_weight_maps(const bq_gemv_desc* d, CUtensorMap* tm_w, CUtensorMap* tm
 
 struct Gemv3Plan {
     int rows, mt, upc, tpu, gpk, ug, ksplit;
+    int even_k;  // 1: every warp of every K slice owns an even number of k-blocks
     int grid, owned, n_units, ring_slots, slot_bytes, nkbw, p_max, xrow_pitch;
     int64_t total_chunks, ws_bytes;
     uint32_t smem_ring, smem_x, smem_xsum, smem_gamma, smem_part, smem_misc, smem_total;

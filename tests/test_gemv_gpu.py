@@ -355,6 +355,31 @@ def test_workspace_shared_across_shapes():
         assert gemv.max_rel_err(got.float(), x.float() @ case["deq"].T) < TOL, (n, k)
 
 
+# ---------------------------------------------------------------- one-row kernels, k-blocks per warp
+@pytest.mark.parametrize("fmt", FORMATS)
+@pytest.mark.parametrize("m", [1, 5])
+@pytest.mark.parametrize("k", [1024, 1280, 2048, 3072, 4096])
+@pytest.mark.parametrize("epi", [0, 2])
+def test_gemv_one_row_kernel_k_blocks_per_warp(fmt, m, k, epi):
+    """One-row kernels (M <= 8) carry two k-blocks per ring slot. Each warp
+    owns an eighth of K (of a K slice when K is split): K = 2048 and 4096 give
+    every warp an even count (the variant without the half-slot path), 1024
+    and 3072 an odd one (last slot half full), 1280 a mix. With a norm
+    (epi 0) K is never split; without one (epi 2) it may be. Parity with the
+    oracle and bit-identical reruns either way."""
+    n = 256
+    case = make_weight(fmt, n, k, seed=k + m + epi)
+    g = torch.Generator().manual_seed(k * 5 + m)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    gamma = (1 + 0.1 * torch.randn(k, generator=g)).to(torch.bfloat16) if epi == 0 else None
+    res = torch.randn(m, n, generator=g).to(torch.bfloat16) if epi == 2 else None
+    got = run_gemv(case, x, n, gamma=gamma, epilogue=epi, residual=res, fmt=fmt)
+    again = run_gemv(case, x, n, gamma=gamma, epilogue=epi, residual=res, fmt=fmt)
+    ref = gemv.fused_reference(x, case["deq"], gamma, 1e-6, epi, res)
+    assert gemv.max_rel_err(got.float(), ref) < TOL, (fmt, m, k, epi)
+    assert torch.equal(got, again)
+
+
 # ---------------------------------------------------------------- K split across CTAs
 @pytest.mark.parametrize("fmt", FORMATS)
 @pytest.mark.parametrize("m,n,k,epi", [(16, 2048, 8192, 2), (32, 1024, 8192, 0), (8, 512, 16384, 2),
