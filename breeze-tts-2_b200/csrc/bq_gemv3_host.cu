@@ -178,6 +178,47 @@ int plan_gemv3_ks(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int SMs, int k
 }  // namespace
 
 namespace {
+// The main loop's critical path under a plan: the most (unit, k-block) chunks
+// one warp streams, in tiles, times the CTAs that share an SM. CTA ranges and
+// warp k-ranges are derived as the kernel derives them; a warp whose eighth
+// of K misses the CTA's range idles.
+int64_t warp_load_max(const Gemv3Plan& P, int KB, int SMs) {
+    const int ks = P.ksplit > 1 ? P.ksplit : 1;
+    int64_t worst = 0;
+    for (int cta = 0; cta < P.grid; ++cta) {
+        int kb_lo = 0, kb_hi = KB;
+        int64_t cb, ce;
+        if (ks > 1) {
+            const int ngrp = P.grid / ks, ugi = cta / ks, s = cta - ugi * ks;
+            const int64_t u0 = int64_t(ugi) * P.n_units / ngrp, u1 = int64_t(ugi + 1) * P.n_units / ngrp;
+            kb_lo = s * KB / ks;
+            kb_hi = (s + 1) * KB / ks;
+            cb = u0 * KB + kb_lo;
+            ce = (u1 - 1) * KB + kb_hi;
+        } else if (P.owned) {
+            cb = int64_t(cta) * P.n_units / P.grid * KB;
+            ce = int64_t(cta + 1) * P.n_units / P.grid * KB;
+        } else {
+            cb = int64_t(cta) * P.total_chunks / P.grid;
+            ce = int64_t(cta + 1) * P.total_chunks / P.grid;
+        }
+        if (ce <= cb) continue;
+        const int64_t uf = cb / KB, ul = (ce - 1) / KB;
+        const int lo0 = int(cb - uf * KB), hi_last = int(ce - 1 - ul * KB);
+        for (int w = 0; w < 8; ++w) {
+            const int a = kb_lo + ((w * (kb_hi - kb_lo)) >> 3), b = kb_lo + (((w + 1) * (kb_hi - kb_lo)) >> 3);
+            int64_t n = 0;
+            for (int64_t u = uf; u <= ul; ++u) {
+                const int lo = (ks > 1 || u == uf) ? std::max(a, lo0) : a;
+                const int hi = (ks > 1 || u == ul) ? std::min(b - 1, hi_last) : b - 1;
+                if (hi >= lo) n += hi - lo + 1;
+            }
+            worst = std::max(worst, n);
+        }
+    }
+    return worst * P.tpu * ((P.grid + SMs - 1) / SMs);
+}
+
 // Plans depend only on the shape, format, epilogue, norm and device: cached,
 // so a decode loop's repeated calls skip the layout search.
 std::mutex g_plan_mu;
@@ -211,17 +252,25 @@ namespace {
 int plan_gemv3_uncached(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int slots) {
     const DeviceInfo* dev = device_info();
     if (!dev) return BQ_ERR_CUDA;
-    // Without a norm (the row's sum of squares would need all of K), split K
-    // across CTAs when a CTA's activations for every k would not leave room
-    // for a co-resident dependent CTA: the smallest split that fits.
+    // Without a norm (the row's sum of squares would need all of K), K may be
+    // split across CTAs. Among the splits that leave room for a co-resident
+    // dependent CTA, the one with the shortest per-warp critical path; a finer
+    // split (more partial sums to reduce) must shorten it by a fifth.
     if (slots == 0 && !d->gamma && d->epilogue != BQ_EPI_SILU_MUL) {
+        const int KB = d->K / kKB;
+        bool found = false;
+        int64_t best = 0;
         for (int ks = 1; ks <= 8; ks *= 2) {
             Gemv3Plan t;
-            if (plan_gemv3_ks(d, rows, &t, dev->sm_count, ks) == BQ_OK && t.smem_total <= kTargetSmem) {
+            if (plan_gemv3_ks(d, rows, &t, dev->sm_count, ks) != BQ_OK || t.smem_total > kTargetSmem) continue;
+            const int64_t cost = warp_load_max(t, KB, dev->sm_count);
+            if (!found || 5 * cost <= 4 * best) {
                 *pl = t;
-                return BQ_OK;
+                best = cost;
+                found = true;
             }
         }
+        if (found) return BQ_OK;
         // nothing leaves room for a dependent CTA: the finest split that fits at all
         for (int ks = 8; ks >= 2; ks /= 2)
             if (plan_gemv3_ks(d, rows, pl, dev->sm_count, ks) == BQ_OK) return BQ_OK;
