@@ -59,6 +59,16 @@ class AttnDesc(ctypes.Structure):
     ]
 
 
+class AttnODesc(ctypes.Structure):
+    """bq_attn_o_desc (include/breeze_b200.h)."""
+
+    _fields_ = [
+        ("attn", AttnDesc), ("N", ctypes.c_int32), ("reserved", ctypes.c_int32), ("wo", ctypes.c_void_p),
+        ("ldw", ctypes.c_int64), ("residual", ctypes.c_void_p), ("ldr", ctypes.c_int64), ("out", ctypes.c_void_p),
+        ("ldo", ctypes.c_int64),
+    ]
+
+
 HEAD_NK = 0
 HEAD_KN = 1
 SAMPLE_TOPK_VALUE = 2
@@ -112,6 +122,9 @@ _SIGS = {
                                               ctypes.c_size_t, ctypes.c_void_p]),
     "bq_attention_workspace_bytes": (ctypes.c_int32, [ctypes.POINTER(AttnDesc), ctypes.POINTER(ctypes.c_size_t)]),
     "bq_attention_step": (ctypes.c_int32, [ctypes.POINTER(AttnDesc), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "bq_attention_o_workspace_bytes": (ctypes.c_int32, [ctypes.POINTER(AttnODesc), ctypes.POINTER(ctypes.c_size_t)]),
+    "bq_attention_o_step": (ctypes.c_int32, [ctypes.POINTER(AttnODesc), ctypes.c_void_p, ctypes.c_size_t,
+                                              ctypes.c_void_p]),
     "bq_head_workspace_bytes": (ctypes.c_int32, [ctypes.POINTER(HeadDesc), ctypes.POINTER(ctypes.c_size_t)]),
     "bq_head_gemv": (ctypes.c_int32, [ctypes.POINTER(HeadDesc), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     "bq_sample_workspace_bytes": (ctypes.c_int32, [ctypes.POINTER(SampleDesc), ctypes.POINTER(ctypes.c_size_t)]),
@@ -393,11 +406,9 @@ def additive_mask(mask: torch.Tensor, b: int, s: int) -> torch.Tensor:
     return m2
 
 
-def attention_step(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, cache_position: torch.Tensor,
-                   keys: torch.Tensor, values: torch.Tensor, mask: torch.Tensor | None, q_norm_w=None, k_norm_w=None,
-                   eps: float = 1e-6, out: torch.Tensor | None = None, flags: int = 0) -> torch.Tensor:
-    """One decode-attention step through bq_attention_step (see the header)."""
-    dev = _require_cuda(qkv, cos, sin, cache_position, keys, values, mask, q_norm_w, k_norm_w, out)
+def _attn_desc(qkv, cos, sin, cache_position, keys, values, mask, q_norm_w, k_norm_w, eps, flags):
+    """bq_attn_desc of one attention step (out / ldo left unset), and the
+    temporaries it points into (keep them alive until the launch)."""
     b = qkv.shape[0]
     _, hkv, s, d = keys.shape
     hq = (qkv.shape[1] - 2 * hkv * d) // d
@@ -413,9 +424,6 @@ def attention_step(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, cach
         raise ValueError("cos / sin rows must be contiguous with equal strides")
     if cache_position.dtype != torch.int64:
         raise ValueError("cache_position must be int64")
-    if out is None:
-        out = torch.empty(b, hq * d, device=dev, dtype=torch.bfloat16)
-    out = _rowmajor(out, "out")
     ad = AttnDesc()
     ad.B, ad.HQ, ad.HKV, ad.D, ad.S = b, hq, hkv, d, s
     ad.eps, ad.flags = eps, flags
@@ -424,7 +432,7 @@ def attention_step(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, cach
     ad.ldcs = cos2.stride(0) if cos2.shape[0] == b else 0
     ad.pos = cache_position.data_ptr()
     ad.k_cache, ad.v_cache = keys.data_ptr(), values.data_ptr()
-    m2 = None
+    keep = [qkv, cos2, sin2]
     if mask is not None:
         m2 = additive_mask(mask, b, s)
         if m2.dtype not in (torch.bfloat16, torch.float32):
@@ -433,15 +441,62 @@ def attention_step(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, cach
             m2 = m2.contiguous()
         ad.mask, ad.ldm = m2.data_ptr(), m2.stride(0)
         ad.mask_dtype = _DT[m2.dtype]
+        keep.append(m2)
     if q_norm_w is not None:
-        ad.q_norm = q_norm_w.to(torch.bfloat16).data_ptr()
-        ad.k_norm = k_norm_w.to(torch.bfloat16).data_ptr()
+        qn, kn = q_norm_w.to(torch.bfloat16), k_norm_w.to(torch.bfloat16)
+        ad.q_norm, ad.k_norm = qn.data_ptr(), kn.data_ptr()
+        keep += [qn, kn]
+    return ad, keep
+
+
+def attention_step(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, cache_position: torch.Tensor,
+                   keys: torch.Tensor, values: torch.Tensor, mask: torch.Tensor | None, q_norm_w=None, k_norm_w=None,
+                   eps: float = 1e-6, out: torch.Tensor | None = None, flags: int = 0) -> torch.Tensor:
+    """One decode-attention step through bq_attention_step (see the header)."""
+    dev = _require_cuda(qkv, cos, sin, cache_position, keys, values, mask, q_norm_w, k_norm_w, out)
+    ad, keep = _attn_desc(qkv, cos, sin, cache_position, keys, values, mask, q_norm_w, k_norm_w, eps, flags)
+    if out is None:
+        out = torch.empty(ad.B, ad.HQ * ad.D, device=dev, dtype=torch.bfloat16)
+    out = _rowmajor(out, "out")
     ad.out, ad.ldo = out.data_ptr(), out.stride(0)
     lib = load()
     need = ctypes.c_size_t(0)
     check(lib.bq_attention_workspace_bytes(ctypes.byref(ad), ctypes.byref(need)), "bq_attention_workspace_bytes")
     ws = ATTN_WORKSPACE.get(dev, need.value)
     check(lib.bq_attention_step(ctypes.byref(ad), ws.data_ptr(), ws.numel(), _stream(dev)), "bq_attention_step")
+    del keep
+    return out
+
+
+def attention_o_step(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, cache_position: torch.Tensor,
+                     keys: torch.Tensor, values: torch.Tensor, q_norm_w, k_norm_w, eps: float, wo: torch.Tensor,
+                     residual: torch.Tensor, out: torch.Tensor | None = None, flags: int = 0) -> torch.Tensor:
+    """The attention step fused with the output projection and residual add,
+    through bq_attention_o_step: out = residual + attention_step(...) @ wo^T
+    (wo bf16 [N, HQ D]); caches written as by attention_step. Short caches
+    only (see the header)."""
+    dev = _require_cuda(qkv, cos, sin, cache_position, keys, values, q_norm_w, k_norm_w, wo, residual, out)
+    ad, keep = _attn_desc(qkv, cos, sin, cache_position, keys, values, None, q_norm_w, k_norm_w, eps, flags)
+    if wo.dtype != torch.bfloat16 or residual.dtype != torch.bfloat16:
+        raise ValueError("wo and residual must be bf16")
+    wo = _rowmajor(wo, "wo")
+    residual = _rowmajor(residual, "residual")
+    n = wo.shape[0]
+    if out is None:
+        out = torch.empty(ad.B, n, device=dev, dtype=torch.bfloat16)
+    out = _rowmajor(out, "out")
+    od = AttnODesc()
+    od.attn = ad
+    od.N = n
+    od.wo, od.ldw = wo.data_ptr(), wo.stride(0)
+    od.residual, od.ldr = residual.data_ptr(), residual.stride(0)
+    od.out, od.ldo = out.data_ptr(), out.stride(0)
+    lib = load()
+    need = ctypes.c_size_t(0)
+    check(lib.bq_attention_o_workspace_bytes(ctypes.byref(od), ctypes.byref(need)), "bq_attention_o_workspace_bytes")
+    ws = ATTN_WORKSPACE.get(dev, need.value)
+    check(lib.bq_attention_o_step(ctypes.byref(od), ws.data_ptr(), ws.numel(), _stream(dev)), "bq_attention_o_step")
+    del keep
     return out
 
 

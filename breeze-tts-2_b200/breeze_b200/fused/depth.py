@@ -49,14 +49,17 @@ class DepthDecoderLoop:
     as in the reference. Inputs: ``backbone_hidden_buf`` (B, backbone width)
     bf16 and ``first_cb_token_buf`` (B,) int64. Output: ``output_tokens``
     (B, num_decode_codebooks) int64; ``step_logits`` keeps every step's fp32
-    logits (B, vocab)."""
+    logits (B, vocab). With ``fuse_attention_o`` (default) the single-position
+    steps run attention, O projection and residual add as one launch
+    (bq_attention_o_step) when the O weight is bf16; the two-position prefill
+    keeps the separate launches."""
 
     def __init__(self, layers: list[DecodeLayer], norm_w: torch.Tensor, codebooks_head: torch.Tensor,
                  embed: torch.Tensor, in_proj: QWeight, batch_size: int, *, codebook_size: int,
                  num_decode_codebooks: int | None = None, bb_proj: QWeight | None = None, head_dim: int = 128,
                  kv_heads: int | None = None, rope_theta: float = 10000.0, max_k: int = 1024, eps: float = 1e-6,
                  temperature: float = 0.9, top_k: int = 50, top_p: float = 0.95, do_sample: bool = True,
-                 guidance_scale: float = 3.0, seed: int = 0):
+                 guidance_scale: float = 3.0, seed: int = 0, fuse_attention_o: bool = True):
         if not layers:
             raise ValueError("the depth loop needs at least one layer")
         dev = layers[0].wqkv.w.device
@@ -116,6 +119,7 @@ class DepthDecoderLoop:
         self.do_sample_buf = f(1 if do_sample else 0, torch.int64)
         self.guidance_scale = f(guidance_scale, torch.float32)
         self.rng = torch.tensor([seed, 0], device=dev, dtype=torch.int64)
+        self.fuse_attention_o = fuse_attention_o
         self.graph = None
 
     # ---- setters (device buffers: no recapture), as the reference's set_* (:240-290)
@@ -140,7 +144,8 @@ class DepthDecoderLoop:
     def launches(self) -> int:
         n_l = len(self.layers)
         pre = 1 + (1 if self.bb_proj is not None else 0) + 1 + 6 * n_l + 2
-        return pre + (self.n_dec - 1) * (2 + 5 * n_l + 2)
+        per_layer = 4 if any(self._fused_o(l, [(0, 0, 0)]) for l in self.layers[:1]) else 5
+        return pre + (self.n_dec - 1) * (2 + per_layer * n_l + 2)
 
     @property
     def weight_bytes_per_frame(self) -> int:
@@ -154,6 +159,9 @@ class DepthDecoderLoop:
         _lib.gemv(x, qw.w, qw.wfmt, qw.N, scale=qw.scale, group=qw.group, gamma=gamma, eps=self.eps, epilogue=epi,
                   residual=res, out=out, flags=_lib.default_flags())
 
+    def _fused_o(self, l, positions) -> bool:
+        return self.fuse_attention_o and len(positions) == 1 and l.wo.wfmt == _lib.W_BF16
+
     def _layers(self, r0: int, r1: int, positions: list[tuple[int, int, int]]) -> torch.Tensor:
         """Layer pass over rows [r0, r1) of the work buffers; positions lists
         (row offset, row count, cache position) blocks for attention."""
@@ -161,12 +169,18 @@ class DepthDecoderLoop:
         for i, l in enumerate(self.layers):
             qkv = self.qkv[r0:r1, : l.wqkv.N]
             self._gemv(x, l.wqkv, qkv, gamma=l.ln1)
-            for off, n, p in positions:
-                _lib.attention_step(self.qkv[off:off + n, : l.wqkv.N], self.cos[p:p + 1], self.sin[p:p + 1],
-                                    self.pos[p], self.k_cache[i], self.v_cache[i], None, l.q_norm, l.k_norm,
-                                    self.eps, out=self.attn_out[off:off + n], flags=_lib.default_flags())
             h = self.h[r0:r1]
-            self._gemv(self.attn_out[r0:r1], l.wo, h, epi=_lib.EPI_ADD_RESIDUAL, res=x)
+            if self._fused_o(l, positions):
+                p = positions[0][2]
+                _lib.attention_o_step(qkv, self.cos[p:p + 1], self.sin[p:p + 1], self.pos[p], self.k_cache[i],
+                                      self.v_cache[i], l.q_norm, l.k_norm, self.eps, l.wo.w, x, out=h,
+                                      flags=_lib.default_flags())
+            else:
+                for off, n, p in positions:
+                    _lib.attention_step(self.qkv[off:off + n, : l.wqkv.N], self.cos[p:p + 1], self.sin[p:p + 1],
+                                        self.pos[p], self.k_cache[i], self.v_cache[i], None, l.q_norm, l.k_norm,
+                                        self.eps, out=self.attn_out[off:off + n], flags=_lib.default_flags())
+                self._gemv(self.attn_out[r0:r1], l.wo, h, epi=_lib.EPI_ADD_RESIDUAL, res=x)
             act = self.act[r0:r1, : l.wd.K]
             self._gemv(h, l.wgu, act, gamma=l.ln2, epi=_lib.EPI_SILU_MUL)
             y = self.res[i % 2][r0:r1]

@@ -29,6 +29,8 @@ constexpr int kMaxG = 8;  // query heads per kv head
 // a later call with more (row, kv head) pairs keeps its counters.
 constexpr int kAttnMaxPairs = 4096;
 constexpr size_t kAttnCounterBytes = size_t(kAttnMaxPairs) * 4;
+constexpr int kAttnOMaxB = 4;    // batch rows of the fused attention + O step
+constexpr int kAttnOMaxS = 256;  // its cache length (every chunk recomputes the attention)
 
 struct AttnParams {
     int32_t B, HQ, HKV, S, G, splits, mask_dtype, has_norm;
@@ -98,46 +100,19 @@ __device__ __forceinline__ void load_row(const __nv_bfloat16* p, float (&v)[DPL]
     }
 }
 
+// One kv head of one batch row over the cache positions [s_lo, s_hi): the
+// query heads and the new k (normed, roped, rounded to the cache dtype) and v
+// into shared memory, the new k / v into the caches when `holds_pos` (register
+// copies stand in for position pos, so nothing reads it before it is written),
+// then each warp's online-softmax state over its positions in s_red. Ends
+// with a block barrier.
 template <int DPL>
-__global__ void __launch_bounds__(kAttnThreads) attention_step_kernel(const AttnParams p) {
+__device__ __forceinline__ void attn_core(const AttnParams& p, int j, int b, int64_t pos, int s_lo, int s_hi,
+                                          bool holds_pos, float (*s_q)[32 * DPL], float* s_k, float* s_v,
+                                          float (*s_red)[kMaxG][32 * DPL + 2]) {
     constexpr int D = 32 * DPL;
-    __shared__ float s_q[kMaxG][D];
-    __shared__ float s_k[D], s_v[D];
-    __shared__ float s_red[4][kMaxG][D + 2];
-    __shared__ unsigned int s_last;
-    const int sp = blockIdx.x, j = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = p.G;
-
-    // Before the dependent-launch wait: pull this CTA's slice of the caches into
-    // L2 (positions before the current one do not depend on the preceding
-    // kernel). The position read here is only a hint; it is read again below.
-    if (threadIdx.x == 0) {
-        const int64_t hint = *reinterpret_cast<const volatile int64_t*>(p.pos);
-        if (hint >= 0 && hint < p.S) {
-            const int len = int(hint) + 1, per0 = (len + p.splits - 1) / p.splits;
-            const int lo = sp * per0, hi = min(lo + per0, len);
-            if (hi > lo) {
-                const int64_t base = ((int64_t(b) * p.HKV + j) * p.S + lo) * D;
-                const uint32_t bytes = uint32_t(hi - lo) * D * 2;
-                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.kc + base), "r"(bytes) : "memory");
-                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.vc + base), "r"(bytes) : "memory");
-            }
-        }
-    }
-    pdl_launch_dependents();
-    pdl_wait();  // qkv comes from the preceding projection
-
-    const int64_t pos = *p.pos;
-    if (pos < 0 || pos >= p.S) {  // a position outside the cache: flag it, touch nothing
-        if (threadIdx.x == 0 && sp == 0 && j == 0 && b == 0) atomicOr(&g_device_error, BQ_DEVERR_POSITION_BIT);
-        return;
-    }
-    const int kv_len = int(pos) + 1;
-    const int per = (kv_len + p.splits - 1) / p.splits;
-    const int s_lo = sp * per, s_hi = min(s_lo + per, kv_len);
-    const bool holds_pos = pos >= s_lo && pos < s_hi;
-
     float c[DPL], s[DPL];
     {
         const __nv_bfloat16* cp = p.cos + int64_t(b) * p.ldcs + lane * DPL;
@@ -275,6 +250,49 @@ __global__ void __launch_bounds__(kAttnThreads) attention_step_kernel(const Attn
         }
     }
     __syncthreads();
+}
+
+template <int DPL>
+__global__ void __launch_bounds__(kAttnThreads) attention_step_kernel(const AttnParams p) {
+    constexpr int D = 32 * DPL;
+    __shared__ float s_q[kMaxG][D];
+    __shared__ float s_k[D], s_v[D];
+    __shared__ float s_red[4][kMaxG][D + 2];
+    __shared__ unsigned int s_last;
+    const int sp = blockIdx.x, j = blockIdx.y, b = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = p.G;
+
+    // Before the dependent-launch wait: pull this CTA's slice of the caches into
+    // L2 (positions before the current one do not depend on the preceding
+    // kernel). The position read here is only a hint; it is read again below.
+    if (threadIdx.x == 0) {
+        const int64_t hint = *reinterpret_cast<const volatile int64_t*>(p.pos);
+        if (hint >= 0 && hint < p.S) {
+            const int len = int(hint) + 1, per0 = (len + p.splits - 1) / p.splits;
+            const int lo = sp * per0, hi = min(lo + per0, len);
+            if (hi > lo) {
+                const int64_t base = ((int64_t(b) * p.HKV + j) * p.S + lo) * D;
+                const uint32_t bytes = uint32_t(hi - lo) * D * 2;
+                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.kc + base), "r"(bytes) : "memory");
+                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.vc + base), "r"(bytes) : "memory");
+            }
+        }
+    }
+    pdl_launch_dependents();
+    pdl_wait();  // qkv comes from the preceding projection
+
+    const int64_t pos = *p.pos;
+    if (pos < 0 || pos >= p.S) {  // a position outside the cache: flag it, touch nothing
+        if (threadIdx.x == 0 && sp == 0 && j == 0 && b == 0) atomicOr(&g_device_error, BQ_DEVERR_POSITION_BIT);
+        return;
+    }
+    const int kv_len = int(pos) + 1;
+    const int per = (kv_len + p.splits - 1) / p.splits;
+    const int s_lo = sp * per, s_hi = min(s_lo + per, kv_len);
+    const bool holds_pos = pos >= s_lo && pos < s_hi;
+
+    attn_core<DPL>(p, j, b, pos, s_lo, s_hi, holds_pos, s_q, s_k, s_v, s_red);
     // thread t < G * D: (head g, dim d); fixed warp order
     const float* red = &s_red[0][0][0];
     constexpr int HS = kMaxG * (D + 2);  // stride between warps
@@ -329,6 +347,125 @@ __global__ void __launch_bounds__(kAttnThreads) attention_step_kernel(const Attn
     if (threadIdx.x == 0) atomicExch(p.counters + b * p.HKV + j, 0u);
 }
 
+// ---------------------------------------------------------------- attention + O projection
+// The attention step fused with the output projection and its residual add
+// (out = residual + attn @ Wo^T), for short caches. CTA (c, j, b) owns kv head
+// j of batch row b and the R output rows [c R, c R + R): before the
+// dependent-launch wait it stages its slice of Wo (R rows x the G D columns of
+// head j's query heads); after it, it computes head j's attention for row b
+// (each chunk recomputes it, cheap at these lengths; chunk 0 writes the
+// caches), rounds it to bf16 as the unfused step stores it, and writes its
+// fp32 partial rows. The last of the HKV CTAs of (chunk, row) sums the heads
+// in head order, adds the residual and stores bf16.
+struct AttnOParams {
+    AttnParams a;          // splits = 1; a.out unused
+    int32_t R, pad;        // output rows per CTA
+    const __nv_bfloat16* wo;
+    int64_t ldw;
+    const __nv_bfloat16* res;
+    int64_t ldr;
+    __nv_bfloat16* out;
+    int64_t ldo;
+    unsigned int* counters;  // [N / R][B]
+    float* partials;         // [N / R][B][HKV][R]
+};
+
+template <int DPL>
+__global__ void __launch_bounds__(kAttnThreads) attention_o_kernel(const AttnOParams p) {
+    constexpr int D = 32 * DPL;
+    __shared__ float s_q[kMaxG][D];
+    __shared__ float s_k[D], s_v[D];
+    __shared__ float s_red[4][kMaxG][D + 2];
+    __shared__ unsigned int s_last;
+    extern __shared__ __align__(16) uint8_t attn_o_dsm[];
+    const AttnParams& a = p.a;
+    const int c = blockIdx.x, j = blockIdx.y, b = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = a.G, GD = a.G * D, R = p.R;
+    const __nv_bfloat16* s_w = reinterpret_cast<const __nv_bfloat16*>(attn_o_dsm);  // [R][GD]
+    float* s_o = reinterpret_cast<float*>(attn_o_dsm + size_t(R) * GD * 2);        // [GD]
+
+    // before the wait: the static Wo slice, and an L2 hint for this head's cache rows
+    {
+        const int per_row = GD / 8;  // 16-byte pieces
+        const uint32_t w0 = smem_u32(attn_o_dsm);
+        for (int i = threadIdx.x; i < R * per_row; i += kAttnThreads) {
+            const int r = i / per_row, q = i - r * per_row;
+            cp_async16(w0 + uint32_t(r * GD * 2 + q * 16), p.wo + (int64_t(c) * R + r) * p.ldw + int64_t(j) * GD + q * 8);
+        }
+    }
+    if (threadIdx.x == 0) {
+        const int64_t hint = *reinterpret_cast<const volatile int64_t*>(a.pos);
+        if (hint >= 0 && hint < a.S) {
+            const uint32_t bytes = uint32_t(hint + 1) * D * 2;
+            const int64_t base = (int64_t(b) * a.HKV + j) * a.S * D;
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.kc + base), "r"(bytes) : "memory");
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.vc + base), "r"(bytes) : "memory");
+        }
+    }
+    pdl_launch_dependents();
+    pdl_wait();  // qkv and the residual come from preceding kernels
+
+    const int64_t pos = *a.pos;
+    if (pos < 0 || pos >= a.S) {  // a position outside the cache: flag it, touch nothing
+        cp_async_wait_all();
+        if (threadIdx.x == 0 && c == 0 && j == 0 && b == 0) atomicOr(&g_device_error, BQ_DEVERR_POSITION_BIT);
+        return;
+    }
+    const int kv_len = int(pos) + 1;
+    const float* red = &s_red[0][0][0];
+    constexpr int HS = kMaxG * (D + 2);  // stride between warps
+    {
+        attn_core<DPL>(a, j, b, pos, 0, kv_len, c == 0, s_q, s_k, s_v, s_red);
+        for (int t = threadIdx.x; t < GD; t += kAttnThreads) {
+            const int g = t / D, d = t - g * D;
+            float mm = -1e30f;
+#pragma unroll
+            for (int w = 0; w < 4; ++w) mm = fmaxf(mm, red[w * HS + g * (D + 2) + D]);
+            float ll = 0.f, aa = 0.f;
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+                const float f = __expf(red[w * HS + g * (D + 2) + D] - mm);
+                ll += red[w * HS + g * (D + 2) + D + 1] * f;
+                aa += red[w * HS + g * (D + 2) + d] * f;
+            }
+            s_o[t] = __bfloat162float(__float2bfloat16_rn(aa / ll));
+        }
+    }
+    cp_async_wait_all();  // this thread's pieces of the Wo slice
+    __syncthreads();
+
+    // partial rows: warp w takes rows w, w + 4, ...; lanes split the G D columns
+    const int64_t cb = int64_t(c) * a.B + b;  // (chunk, row)
+    float* part = p.partials + (cb * a.HKV + j) * R;
+    for (int r = warp; r < R; r += 4) {
+        const __nv_bfloat16* wr = s_w + r * GD;
+        float acc = 0.f;
+        for (int t = lane * 2; t < GD; t += 64) {
+            const uint32_t w2 = *reinterpret_cast<const uint32_t*>(wr + t);
+            acc = fmaf(__uint_as_float(w2 << 16), s_o[t], acc);
+            acc = fmaf(__uint_as_float(w2 & 0xFFFF0000u), s_o[t + 1], acc);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) __stcg(part + r, acc);
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(p.counters + cb, 1u) == unsigned(a.HKV - 1);
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const float* base = p.partials + cb * a.HKV * R;
+    for (int r = threadIdx.x; r < R; r += kAttnThreads) {
+        float v = 0.f;
+        for (int h = 0; h < a.HKV; ++h) v += __ldcg(base + int64_t(h) * R + r);
+        const int64_t n = int64_t(c) * R + r;
+        v += __bfloat162float(p.res[int64_t(b) * p.ldr + n]);
+        p.out[int64_t(b) * p.ldo + n] = __float2bfloat16_rn(v);
+    }
+    if (threadIdx.x == 0) atomicExch(p.counters + cb, 0u);
+}
+
 int attn_splits(const bq_attn_desc* d, int sm_count) {
     // enough CTAs to cover the SMs, each over >= 32 positions of the cache
     const int items = d->B * d->HKV;
@@ -361,6 +498,35 @@ int validate_attn(const bq_attn_desc* d) {
     return BQ_OK;
 }
 
+
+// Output rows per CTA of the fused attention + O projection: a multiple of 16
+// dividing N, at most 64, and the Wo slice (R x G D bf16) within 48 KB.
+int attn_o_rows(const bq_attn_o_desc* d) {
+    const int GD = d->attn.HQ / d->attn.HKV * d->attn.D;
+    for (int r = 64; r >= 16; r /= 2)
+        if (d->N % r == 0 && r * GD * 2 <= 48 * 1024) return r;
+    return 0;
+}
+
+int validate_attn_o(const bq_attn_o_desc* d) {
+    if (!d) return set_error(BQ_ERR_INVALID_ARG, "desc is NULL");
+    bq_attn_desc ad = d->attn;
+    ad.out = d->out;  // the attention output stays on chip; out / ldo are checked below
+    ad.ldo = int64_t(d->attn.HQ) * d->attn.D;
+    int rc = validate_attn(&ad);
+    if (rc) return rc;
+    if (d->attn.mask) return set_error(BQ_ERR_INVALID_ARG, "the fused attention + O step takes no mask");
+    if (d->attn.B > kAttnOMaxB) return set_error(BQ_ERR_SHAPE, "B=%d exceeds %d", d->attn.B, kAttnOMaxB);
+    if (d->attn.S > kAttnOMaxS) return set_error(BQ_ERR_SHAPE, "cache length %d exceeds %d", d->attn.S, kAttnOMaxS);
+    if (d->N < 16 || !attn_o_rows(d)) return set_error(BQ_ERR_SHAPE, "N=%d must be a positive multiple of 16", d->N);
+    if (int64_t(d->N / attn_o_rows(d)) * d->attn.B > kAttnMaxPairs) return set_error(BQ_ERR_SHAPE, "N=%d too large", d->N);
+    if (!d->wo || !d->residual || !d->out) return set_error(BQ_ERR_INVALID_ARG, "wo, residual and out must be non-NULL");
+    const int64_t K = int64_t(d->attn.HQ) * d->attn.D;
+    if (d->ldw < K || d->ldr < d->N || d->ldo < d->N) return set_error(BQ_ERR_SHAPE, "ldw, ldr or ldo too small");
+    if ((reinterpret_cast<uintptr_t>(d->wo) & 15) || (d->ldw * 2) % 16)
+        return set_error(BQ_ERR_ALIGN, "wo and its row stride must be 16-byte aligned");
+    return BQ_OK;
+}
 }  // namespace
 
 }  // namespace bq
@@ -440,6 +606,82 @@ int32_t bq_attention_step(const bq_attn_desc* d, void* workspace, size_t workspa
     void* args[] = {&p};
     cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
     if (e != cudaSuccess) return set_error(BQ_ERR_CUDA, "attention launch failed: %s", cudaGetErrorString(e));
+    return BQ_OK;
+}
+
+int32_t bq_attention_o_workspace_bytes(const bq_attn_o_desc* d, size_t* bytes) {
+    if (!bytes) return set_error(BQ_ERR_INVALID_ARG, "bytes is NULL");
+    const int rc = validate_attn_o(d);
+    if (rc) return rc;
+    const int R = attn_o_rows(d);
+    *bytes = kAttnCounterBytes + size_t(d->N / R) * d->attn.HKV * d->attn.B * R * 4;
+    return BQ_OK;
+}
+
+int32_t bq_attention_o_step(const bq_attn_o_desc* d, void* workspace, size_t workspace_bytes, void* stream) {
+    int rc = validate_attn_o(d);
+    if (rc) return rc;
+    const DeviceInfo* dev = device_info();
+    if (!dev) return BQ_ERR_CUDA;
+    if (dev->major != 10) return set_error(BQ_ERR_DEVICE, "sm_%d%d device: this library is built for sm_100a", dev->major, dev->minor);
+    const bq_attn_desc* ad = &d->attn;
+    const int R = attn_o_rows(d), chunks = d->N / R;
+    const size_t need = kAttnCounterBytes + size_t(chunks) * ad->HKV * ad->B * R * 4;
+    if (!workspace || workspace_bytes < need)
+        return set_error(BQ_ERR_WORKSPACE, "attention + O workspace of %zu bytes given, %zu needed", workspace_bytes, need);
+    if (reinterpret_cast<uintptr_t>(workspace) & 255) return set_error(BQ_ERR_ALIGN, "workspace must be 256-byte aligned");
+    AttnOParams p;
+    std::memset(&p, 0, sizeof(p));
+    p.a.B = ad->B;
+    p.a.HQ = ad->HQ;
+    p.a.HKV = ad->HKV;
+    p.a.S = ad->S;
+    p.a.G = ad->HQ / ad->HKV;
+    p.a.splits = 1;
+    p.a.mask_dtype = ad->mask_dtype;
+    p.a.has_norm = ad->q_norm != nullptr;
+    p.a.eps = ad->eps;
+    p.a.scale = 1.0f / sqrtf(float(ad->D));
+    p.a.qkv = static_cast<const __nv_bfloat16*>(ad->qkv);
+    p.a.ldqkv = ad->ldqkv;
+    p.a.cos = static_cast<const __nv_bfloat16*>(ad->cos);
+    p.a.sin = static_cast<const __nv_bfloat16*>(ad->sin);
+    p.a.ldcs = ad->ldcs;
+    p.a.pos = ad->pos;
+    p.a.kc = static_cast<__nv_bfloat16*>(ad->k_cache);
+    p.a.vc = static_cast<__nv_bfloat16*>(ad->v_cache);
+    p.a.qn = static_cast<const __nv_bfloat16*>(ad->q_norm);
+    p.a.kn = static_cast<const __nv_bfloat16*>(ad->k_norm);
+    p.R = R;
+    p.wo = static_cast<const __nv_bfloat16*>(d->wo);
+    p.ldw = d->ldw;
+    p.res = static_cast<const __nv_bfloat16*>(d->residual);
+    p.ldr = d->ldr;
+    p.out = static_cast<__nv_bfloat16*>(d->out);
+    p.ldo = d->ldo;
+    p.counters = static_cast<unsigned int*>(workspace);
+    p.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + kAttnCounterBytes);
+    const void* fn = ad->D == 128 ? reinterpret_cast<const void*>(&attention_o_kernel<4>)
+                                  : reinterpret_cast<const void*>(&attention_o_kernel<2>);
+    const uint32_t smem = uint32_t(R) * p.a.G * ad->D * 2 + uint32_t(p.a.G) * ad->D * 4;
+    rc = ensure_smem_attr(fn, smem);
+    if (rc) return rc;
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(chunks, ad->HKV, ad->B);
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    if (ad->flags & BQ_FLAG_PDL) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    void* args[] = {&p};
+    cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
+    if (e != cudaSuccess) return set_error(BQ_ERR_CUDA, "attention + O launch failed: %s", cudaGetErrorString(e));
     return BQ_OK;
 }
 

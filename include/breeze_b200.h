@@ -189,6 +189,31 @@ typedef struct bq_attn_desc {
 int32_t bq_attention_workspace_bytes(const bq_attn_desc* desc, size_t* bytes);
 int32_t bq_attention_step(const bq_attn_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- attention step fused with the output projection ------------------- */
+/* out = residual + attention_step(attn) @ wo^T, for short caches (S <= 256,
+ * B <= 4, no mask): replaces the reference FusedDecoderLayer's
+ * attention_step followed by rms_gemv(attn, wo, None, epilogue=2,
+ * residual=x) (models/fused/layer.py:89-91) with bf16 wo, as the depth
+ * decoder runs them (attn_bits=16). The attention output is rounded to bf16
+ * as the unfused step stores it and never leaves the chip; the caches are
+ * written as by bq_attention_step. attn.out / attn.ldo are ignored. */
+typedef struct bq_attn_o_desc {
+    bq_attn_desc attn;
+    int32_t N;                 /* O outputs (multiple of 16) */
+    int32_t reserved;
+    const void* wo;            /* bf16 [N, ldw], K = HQ D columns; 16-byte aligned rows */
+    int64_t ldw;
+    const void* residual;      /* bf16 [B, ldr] */
+    int64_t ldr;
+    void* out;                 /* bf16 [B, ldo] */
+    int64_t ldo;
+} bq_attn_o_desc;
+
+/* The workspace (256-byte aligned) starts with arrival counters that the
+ * kernel leaves at zero; it may be shared with bq_attention_step's. */
+int32_t bq_attention_o_workspace_bytes(const bq_attn_o_desc* desc, size_t* bytes);
+int32_t bq_attention_o_step(const bq_attn_o_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- fp32 output heads -------------------------------------------------- */
 /* out[M, N] (fp32) = y @ W, W fp32, where y is x or, when gamma is given, the
  * reference's BreezeRMSNorm of x (models/breeze.py:115-120: xh = bf16(x *

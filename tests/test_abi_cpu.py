@@ -133,3 +133,43 @@ def test_attention_desc_validation_without_gpu(lib):
     assert lib.bq_attention_workspace_bytes(ctypes.byref(d), ctypes.byref(need)) == L.BQ_ERR_SHAPE
     d.HKV = 16
     assert lib.bq_attention_step(ctypes.byref(d), None, 0, None) == L.BQ_ERR_INVALID_ARG
+
+
+def test_attention_o_desc_validation_without_gpu(lib):
+    """bq_attention_o_step (attention fused with the O projection): the
+    descriptor mirrors the header (bq_attn_desc + 2 x 4 + 6 x 8 bytes) and
+    its host-side checks need no GPU."""
+    import ctypes
+
+    from breeze_b200 import _lib as L
+
+    assert ctypes.sizeof(L.AttnDesc) == 8 * 4 + 14 * 8
+    assert ctypes.sizeof(L.AttnODesc) == ctypes.sizeof(L.AttnDesc) + 2 * 4 + 6 * 8
+    assert L.AttnODesc.N.offset == ctypes.sizeof(L.AttnDesc)
+    od = L.AttnODesc()
+    a = od.attn
+    a.B, a.HQ, a.HKV, a.D, a.S = 1, 8, 8, 128, 17
+    a.qkv = a.cos = a.sin = a.pos = a.k_cache = a.v_cache = 256
+    a.ldqkv = (8 + 16) * 128
+    od.attn = a
+    od.N, od.wo, od.ldw, od.residual, od.ldr, od.out, od.ldo = 1024, 256, 1024, 256, 1024, 256, 1024
+    need = ctypes.c_size_t(0)
+    assert lib.bq_attention_o_workspace_bytes(ctypes.byref(od), ctypes.byref(need)) == 0
+    assert need.value > 0
+    for field, value, code, text in [("N", 1000, L.BQ_ERR_SHAPE, b"multiple of 16"),
+                                     ("ldw", 512, L.BQ_ERR_SHAPE, b"too small"),
+                                     ("wo", 0, L.BQ_ERR_INVALID_ARG, b"non-NULL"),
+                                     ("wo", 264, L.BQ_ERR_ALIGN, b"16-byte")]:
+        bad = L.AttnODesc.from_buffer_copy(od)
+        setattr(bad, field, value)
+        assert lib.bq_attention_o_workspace_bytes(ctypes.byref(bad), ctypes.byref(need)) == code, field
+        assert text in lib.bq_last_error_string()
+    for field, value, text in [("B", 5, b"exceeds"), ("S", 300, b"cache length")]:
+        bad = L.AttnODesc.from_buffer_copy(od)
+        setattr(bad.attn, field, value)
+        assert lib.bq_attention_o_workspace_bytes(ctypes.byref(bad), ctypes.byref(need)) == L.BQ_ERR_SHAPE, field
+        assert text in lib.bq_last_error_string()
+    bad = L.AttnODesc.from_buffer_copy(od)
+    bad.attn.mask = 256
+    assert lib.bq_attention_o_workspace_bytes(ctypes.byref(bad), ctypes.byref(need)) == L.BQ_ERR_INVALID_ARG
+    assert lib.bq_attention_o_step(ctypes.byref(od), None, 0, None) != 0

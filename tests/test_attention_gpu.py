@@ -128,3 +128,54 @@ def test_attention_graph_replay_follows_cache_position():
     from breeze_b200 import _lib
 
     assert _lib.device_status(0) == 0
+
+
+FUSED_O_CASES = [
+    # B, HQ, HKV, D, S, pos, norm, N, bcast_rope
+    (1, 8, 8, 128, 17, 16, True, 1024, True),    # depth decoder step
+    (2, 8, 8, 128, 17, 0, True, 1024, True),
+    (3, 4, 2, 64, 48, 30, False, 256, False),
+    (4, 16, 8, 128, 256, 255, True, 2048, False),
+    (1, 8, 8, 128, 64, 40, True, 48, True),      # 16-row chunks
+]
+
+
+@pytest.mark.parametrize("case", FUSED_O_CASES)
+def test_attention_o_step_matches_oracle(case):
+    """bq_attention_o_step: residual + attention @ Wo^T in one launch, against
+    the attention oracle (output rounded to bf16, as the unfused step stores
+    it) followed by an fp32 projection: within 1e-2; caches written as by
+    attention_step; a rerun is bit-identical."""
+    from breeze_b200 import _lib as L
+
+    B, HQ, HKV, D, S, pos, norm, N, bcast = case
+    g = torch.Generator().manual_seed(B * 7 + HQ + D + S + N)
+    qkv = torch.randn(B, (HQ + 2 * HKV) * D, generator=g).to(torch.bfloat16)
+    k0 = (torch.randn(B, HKV, S, D, generator=g) * 0.5).to(torch.bfloat16)
+    v0 = torch.randn(B, HKV, S, D, generator=g).to(torch.bfloat16)
+    qn = (1 + 0.1 * torch.randn(D, generator=g)).to(torch.bfloat16) if norm else None
+    kn = (1 + 0.1 * torch.randn(D, generator=g)).to(torch.bfloat16) if norm else None
+    ang = torch.rand(1 if bcast else B, 1, D // 2, generator=g) * 6.0
+    emb = torch.cat([ang, ang], -1)
+    cos, sin = emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
+    wo = (torch.randn(N, HQ * D, generator=g) * 0.02).to(torch.bfloat16)
+    res = torch.randn(B, N, generator=g).to(torch.bfloat16)
+    ref_attn, ref_k, ref_v = oa.attention_step(qkv, cos, sin, pos, k0.clone(), v0.clone(), torch.zeros(B, S), qn, kn,
+                                               1e-6)
+    ref = res.float() + ref_attn.float() @ wo.float().T
+    keys, values = k0.to(DEV), v0.to(DEV)
+    args = (qkv.to(DEV), cos.to(DEV), sin.to(DEV), torch.tensor([pos], device=DEV), keys, values,
+            None if qn is None else qn.to(DEV), None if kn is None else kn.to(DEV), 1e-6, wo.to(DEV), res.to(DEV))
+    out = L.attention_o_step(*args, flags=L.default_flags())
+    again = L.attention_o_step(*args, flags=L.default_flags())
+    torch.cuda.synchronize()
+    assert out.shape == (B, N)
+    assert og.max_rel_err(out.cpu().float(), ref) < TOL
+    assert torch.equal(out, again)
+    assert torch.equal(values.cpu()[:, :, pos], ref_v[:, :, pos])
+    kd = (keys.cpu()[:, :, pos].float() - ref_k[:, :, pos].float()).abs()
+    assert (kd <= ref_k[:, :, pos].float().abs() * 2 ** -7 + 1e-6).all()
+    other = torch.ones(S, dtype=torch.bool)
+    other[pos] = False
+    assert torch.equal(keys.cpu()[:, :, other], k0[:, :, other])
+    assert L.device_status() == 0

@@ -23,10 +23,10 @@ CFG = dict(hidden=256, inter=256, q_heads=2, kv_heads=1, head_dim=128, emb_width
 CODEBOOK = 296
 
 
-def _build(fmt, dev, batch, **kw):
+def _build(fmt, dev, batch, attn_fmt=None, **kw):
     from breeze_b200.fused import depth
 
-    layers, norm_w, head, embed, in_proj = depth.synthetic_depth(fmt, 2, dev, seed=5, **CFG)
+    layers, norm_w, head, embed, in_proj = depth.synthetic_depth(fmt, 2, dev, seed=5, attn_fmt=attn_fmt, **CFG)
     loop = depth.DepthDecoderLoop(layers, norm_w, head, embed, in_proj, batch, codebook_size=CODEBOOK,
                                   kv_heads=CFG["kv_heads"], **kw)
     return loop
@@ -42,6 +42,10 @@ def test_depth_loop_shapes_cpu():
         loop.run()
     with pytest.raises(ValueError):
         loop.set_top_k(5000)
+    # bf16 O: the single steps fuse attention, O projection and residual (one launch fewer per layer)
+    fused = _build("int8", "cpu", 2, attn_fmt="bf16")
+    assert fused.launches == (1 + 1 + 6 * 2 + 2) + 3 * (2 + 4 * 2 + 2)
+    assert _build("int8", "cpu", 2, attn_fmt="bf16", fuse_attention_o=False).launches == loop.launches
 
 
 def _deq(qw):
@@ -76,11 +80,12 @@ def _inputs(loop, seed):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("fmt", ["int4", "fp8"])
+@pytest.mark.parametrize("fmt,attn_fmt", [("int4", None), ("fp8", None), ("int4", "bf16")])
 @pytest.mark.parametrize("batch", [1, 2, 4])
-def test_depth_greedy_frame_matches_oracle(fmt, batch):
+def test_depth_greedy_frame_matches_oracle(fmt, attn_fmt, batch):
+    """attn_fmt bf16 runs the single steps through the fused attention + O launch."""
     dev = torch.device("cuda", 0)
-    loop = _build(fmt, dev, batch, do_sample=False, guidance_scale=2.0)
+    loop = _build(fmt, dev, batch, attn_fmt=attn_fmt, do_sample=False, guidance_scale=2.0)
     bb, first = _inputs(loop, 11 + batch)
     loop.run()
     torch.cuda.synchronize()
@@ -124,9 +129,10 @@ def test_depth_sampled_frame_uses_philox_draws():
 
 
 @pytest.mark.gpu
-def test_depth_graph_replay_matches_eager():
+@pytest.mark.parametrize("attn_fmt", [None, "bf16"])
+def test_depth_graph_replay_matches_eager(attn_fmt):
     dev = torch.device("cuda", 0)
-    loop = _build("int4", dev, 2, do_sample=False)
+    loop = _build("int4", dev, 2, attn_fmt=attn_fmt, do_sample=False)
     _inputs(loop, 21)
     loop.run()
     torch.cuda.synchronize()
@@ -149,3 +155,38 @@ def test_depth_graph_replay_matches_eager():
     from breeze_b200 import _lib
 
     assert _lib.device_status(0) == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("batch", [1, 2])
+def test_depth_fused_attention_o_matches_separate_launches(batch):
+    """The fused attention + O step against attention_step + O GEMV on the same
+    weights and inputs: caches within bf16 rounding of each other, per-step
+    logits within 1e-2, greedy tokens equal where the margin allows."""
+    dev = torch.device("cuda", 0)
+    runs = []
+    for fuse in (False, True):
+        loop = _build("int4", dev, batch, attn_fmt="bf16", do_sample=False, guidance_scale=2.0, fuse_attention_o=fuse)
+        _inputs(loop, 31 + batch)
+        loop.run()
+        torch.cuda.synchronize()
+        runs.append(loop)
+    a, b = runs
+    assert b.launches == a.launches - (a.n_dec - 1) * len(a.layers)
+    # compare until the first token that may differ (a near-tie); later steps depend on it
+    same = True
+    for j in range(a.n_dec):
+        assert og.max_rel_err(b.step_logits[j].cpu(), a.step_logits[j].cpu()) < TOL, f"step {j}"
+        mixed = osm.mixed_logits(a.step_logits[j].cpu(), a.half, torch.full((a.half,), 2.0) if a.cfg else None,
+                                 mask=(CODEBOOK, a.vocab))
+        for r in range(a.half):
+            top2 = torch.topk(mixed[r], 2).values
+            if float(top2[0] - top2[1]) > 1e-2 * float(mixed[r][mixed[r] > -1e30].abs().max()):
+                assert int(b.output_tokens[r, j]) == int(a.output_tokens[r, j]), f"step {j} row {r}"
+        if not torch.equal(b.output_tokens[:, j], a.output_tokens[:, j]):
+            same = False
+            break
+    if same:
+        for i in range(len(a.layers)):
+            for ca, cb in ((a.k_cache[i], b.k_cache[i]), (a.v_cache[i], b.v_cache[i])):
+                assert og.max_rel_err(cb.float().cpu(), ca.float().cpu()) < TOL
