@@ -470,13 +470,14 @@ def attention_step(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, cach
 
 def attention_o_step(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, cache_position: torch.Tensor,
                      keys: torch.Tensor, values: torch.Tensor, q_norm_w, k_norm_w, eps: float, wo: torch.Tensor,
-                     residual: torch.Tensor, out: torch.Tensor | None = None, flags: int = 0) -> torch.Tensor:
+                     residual: torch.Tensor, out: torch.Tensor | None = None, flags: int = 0,
+                     mask: torch.Tensor | None = None) -> torch.Tensor:
     """The attention step fused with the output projection and residual add,
     through bq_attention_o_step: out = residual + attention_step(...) @ wo^T
-    (wo bf16 [N, HQ D]); caches written as by attention_step. Short caches
-    only (see the header)."""
-    dev = _require_cuda(qkv, cos, sin, cache_position, keys, values, q_norm_w, k_norm_w, wo, residual, out)
-    ad, keep = _attn_desc(qkv, cos, sin, cache_position, keys, values, None, q_norm_w, k_norm_w, eps, flags)
+    (wo bf16 [N, HQ D]); caches written as by attention_step; ``mask`` as
+    attention_step takes it. Short caches only (see the header)."""
+    dev = _require_cuda(qkv, cos, sin, cache_position, keys, values, q_norm_w, k_norm_w, wo, residual, out, mask)
+    ad, keep = _attn_desc(qkv, cos, sin, cache_position, keys, values, mask, q_norm_w, k_norm_w, eps, flags)
     if wo.dtype != torch.bfloat16 or residual.dtype != torch.bfloat16:
         raise ValueError("wo and residual must be bf16")
     wo = _rowmajor(wo, "wo")

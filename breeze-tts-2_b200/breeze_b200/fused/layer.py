@@ -112,11 +112,16 @@ class FusedDecoderLayer(nn.Module):
         x = hidden_states[:, 0]
         qkv = rms_gemv(x, self.wqkv, self.ln1, self.eps)
         cos, sin = position_embeddings
-        attn = attention_step(qkv, cos, sin, cache_position, cache.keys, cache.values, attention_mask, self.qn,
-                              self.kn, self.eps)
+        if self.wo.bits == 16 and x.dtype == torch.bfloat16 and cache.keys.shape[2] <= 256 and x.shape[0] <= 4:
+            # short cache (the depth decoder): attention, O projection and residual in one launch
+            h = _lib.attention_o_step(qkv, cos, sin, cache_position, cache.keys, cache.values, self.qn, self.kn,
+                                      self.eps, self.wo.w, x, flags=_lib.default_flags(), mask=attention_mask)
+        else:
+            attn = attention_step(qkv, cos, sin, cache_position, cache.keys, cache.values, attention_mask, self.qn,
+                                  self.kn, self.eps)
+            h = rms_gemv(attn, self.wo, None, epilogue=_lib.EPI_ADD_RESIDUAL, residual=x)
         if hasattr(cache, "cumulative_length"):
             cache.cumulative_length.add_(1)  # the kernel wrote the new k / v; keep the cache's own count
-        h = rms_gemv(attn, self.wo, None, epilogue=_lib.EPI_ADD_RESIDUAL, residual=x)
         if self.qgu is not None:
             act = self._gemv(h, self.qgu, gamma=self.ln2, epilogue=_lib.EPI_SILU_MUL)
             out = self._gemv(act, self.qd, epilogue=_lib.EPI_ADD_RESIDUAL, residual=h)

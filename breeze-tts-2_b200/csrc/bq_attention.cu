@@ -515,7 +515,6 @@ int validate_attn_o(const bq_attn_o_desc* d) {
     ad.ldo = int64_t(d->attn.HQ) * d->attn.D;
     int rc = validate_attn(&ad);
     if (rc) return rc;
-    if (d->attn.mask) return set_error(BQ_ERR_INVALID_ARG, "the fused attention + O step takes no mask");
     if (d->attn.B > kAttnOMaxB) return set_error(BQ_ERR_SHAPE, "B=%d exceeds %d", d->attn.B, kAttnOMaxB);
     if (d->attn.S > kAttnOMaxS) return set_error(BQ_ERR_SHAPE, "cache length %d exceeds %d", d->attn.S, kAttnOMaxS);
     if (d->N < 16 || !attn_o_rows(d)) return set_error(BQ_ERR_SHAPE, "N=%d must be a positive multiple of 16", d->N);
@@ -650,6 +649,8 @@ int32_t bq_attention_o_step(const bq_attn_o_desc* d, void* workspace, size_t wor
     p.a.pos = ad->pos;
     p.a.kc = static_cast<__nv_bfloat16*>(ad->k_cache);
     p.a.vc = static_cast<__nv_bfloat16*>(ad->v_cache);
+    p.a.mask = ad->mask;
+    p.a.ldm = ad->ldm;
     p.a.qn = static_cast<const __nv_bfloat16*>(ad->q_norm);
     p.a.kn = static_cast<const __nv_bfloat16*>(ad->k_norm);
     p.R = R;

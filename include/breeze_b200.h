@@ -191,7 +191,7 @@ int32_t bq_attention_step(const bq_attn_desc* desc, void* workspace, size_t work
 
 /* ---- attention step fused with the output projection ------------------- */
 /* out = residual + attention_step(attn) @ wo^T, for short caches (S <= 256,
- * B <= 4, no mask): replaces the reference FusedDecoderLayer's
+ * B <= 4; the additive mask as in bq_attention_step): replaces the reference FusedDecoderLayer's
  * attention_step followed by rms_gemv(attn, wo, None, epilogue=2,
  * residual=x) (models/fused/layer.py:89-91) with bf16 wo, as the depth
  * decoder runs them (attn_bits=16). The attention output is rounded to bf16

@@ -170,6 +170,6 @@ def test_attention_o_desc_validation_without_gpu(lib):
         assert lib.bq_attention_o_workspace_bytes(ctypes.byref(bad), ctypes.byref(need)) == L.BQ_ERR_SHAPE, field
         assert text in lib.bq_last_error_string()
     bad = L.AttnODesc.from_buffer_copy(od)
-    bad.attn.mask = 256
+    bad.attn.mask, bad.attn.mask_dtype = 256, 9
     assert lib.bq_attention_o_workspace_bytes(ctypes.byref(bad), ctypes.byref(need)) == L.BQ_ERR_INVALID_ARG
     assert lib.bq_attention_o_step(ctypes.byref(od), None, 0, None) != 0

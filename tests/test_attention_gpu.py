@@ -131,12 +131,13 @@ def test_attention_graph_replay_follows_cache_position():
 
 
 FUSED_O_CASES = [
-    # B, HQ, HKV, D, S, pos, norm, N, bcast_rope
-    (1, 8, 8, 128, 17, 16, True, 1024, True),    # depth decoder step
-    (2, 8, 8, 128, 17, 0, True, 1024, True),
-    (3, 4, 2, 64, 48, 30, False, 256, False),
-    (4, 16, 8, 128, 256, 255, True, 2048, False),
-    (1, 8, 8, 128, 64, 40, True, 48, True),      # 16-row chunks
+    # B, HQ, HKV, D, S, pos, norm, N, bcast_rope, mask
+    (1, 8, 8, 128, 17, 16, True, 1024, True, None),    # depth decoder step
+    (2, 8, 8, 128, 17, 0, True, 1024, True, None),
+    (3, 4, 2, 64, 48, 30, False, 256, False, "bool"),
+    (4, 16, 8, 128, 256, 255, True, 2048, False, "float"),
+    (1, 8, 8, 128, 64, 40, True, 48, True, None),      # 16-row chunks
+    (2, 8, 8, 128, 17, 9, True, 1024, True, "float"),  # the HF causal mask of a decoder layer
 ]
 
 
@@ -148,7 +149,7 @@ def test_attention_o_step_matches_oracle(case):
     attention_step; a rerun is bit-identical."""
     from breeze_b200 import _lib as L
 
-    B, HQ, HKV, D, S, pos, norm, N, bcast = case
+    B, HQ, HKV, D, S, pos, norm, N, bcast, mk = case
     g = torch.Generator().manual_seed(B * 7 + HQ + D + S + N)
     qkv = torch.randn(B, (HQ + 2 * HKV) * D, generator=g).to(torch.bfloat16)
     k0 = (torch.randn(B, HKV, S, D, generator=g) * 0.5).to(torch.bfloat16)
@@ -160,14 +161,24 @@ def test_attention_o_step_matches_oracle(case):
     cos, sin = emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
     wo = (torch.randn(N, HQ * D, generator=g) * 0.02).to(torch.bfloat16)
     res = torch.randn(B, N, generator=g).to(torch.bfloat16)
-    ref_attn, ref_k, ref_v = oa.attention_step(qkv, cos, sin, pos, k0.clone(), v0.clone(), torch.zeros(B, S), qn, kn,
-                                               1e-6)
+    mask = None
+    if mk == "bool":
+        mask = torch.zeros(B, 1, 1, S, dtype=torch.bool)
+        mask[:, :, :, : pos + 1] = True
+        mask[1, :, :, : min(3, pos)] = False
+    elif mk == "float":
+        mask = torch.full((B, 1, 1, S), torch.finfo(torch.bfloat16).min)
+        mask[:, :, :, : pos + 1] = 0.0
+        mask = mask.to(torch.bfloat16)
+    ref_attn, ref_k, ref_v = oa.attention_step(qkv, cos, sin, pos, k0.clone(), v0.clone(),
+                                               mask if mask is not None else torch.zeros(B, S), qn, kn, 1e-6)
     ref = res.float() + ref_attn.float() @ wo.float().T
     keys, values = k0.to(DEV), v0.to(DEV)
     args = (qkv.to(DEV), cos.to(DEV), sin.to(DEV), torch.tensor([pos], device=DEV), keys, values,
             None if qn is None else qn.to(DEV), None if kn is None else kn.to(DEV), 1e-6, wo.to(DEV), res.to(DEV))
-    out = L.attention_o_step(*args, flags=L.default_flags())
-    again = L.attention_o_step(*args, flags=L.default_flags())
+    m = None if mask is None else mask.to(DEV)
+    out = L.attention_o_step(*args, flags=L.default_flags(), mask=m)
+    again = L.attention_o_step(*args, flags=L.default_flags(), mask=m)
     torch.cuda.synchronize()
     assert out.shape == (B, N)
     assert og.max_rel_err(out.cpu().float(), ref) < TOL
