@@ -9,6 +9,7 @@
 // G = HQ / HKV query heads and the new k / v itself, so no CTA reads the
 // cache at `pos` before it is written (the split holding `pos` uses the new
 // values from registers and is the one that writes them back).
+#include <cooperative_groups.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -31,6 +32,7 @@ constexpr int kAttnMaxPairs = 4096;
 constexpr size_t kAttnCounterBytes = size_t(kAttnMaxPairs) * 4;
 constexpr int kAttnOMaxB = 4;    // batch rows of the fused attention + O step
 constexpr int kAttnOMaxS = 256;  // its cache length (every chunk recomputes the attention)
+constexpr int kAttnOMaxR = 64;   // its output rows per CTA
 
 struct AttnParams {
     int32_t B, HQ, HKV, S, G, splits, mask_dtype, has_norm;
@@ -370,9 +372,14 @@ struct AttnOParams {
     float* partials;         // [N / R][B][HKV][R]
 };
 
-template <int DPL>
+// CLUSTER: the HKV CTAs of one (chunk, row) form a thread-block cluster
+// (HKV <= 8); the partial rows stay in shared memory and each CTA sums its
+// share of the rows over the heads through distributed shared memory, with
+// no global partials, fences or arrival counters.
+template <int DPL, bool CLUSTER>
 __global__ void __launch_bounds__(kAttnThreads) attention_o_kernel(const AttnOParams p) {
     constexpr int D = 32 * DPL;
+    __shared__ float s_part[kAttnOMaxR];  // cluster mode: this head's partial rows
     __shared__ float s_q[kMaxG][D];
     __shared__ float s_k[D], s_v[D];
     __shared__ float s_red[4][kMaxG][D + 2];
@@ -437,7 +444,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_o_kernel(const AttnOPa
 
     // partial rows: warp w takes rows w, w + 4, ...; lanes split the G D columns
     const int64_t cb = int64_t(c) * a.B + b;  // (chunk, row)
-    float* part = p.partials + (cb * a.HKV + j) * R;
+    float* part = CLUSTER ? s_part : p.partials + (cb * a.HKV + j) * R;
     for (int r = warp; r < R; r += 4) {
         const __nv_bfloat16* wr = s_w + r * GD;
         float acc = 0.f;
@@ -447,7 +454,27 @@ __global__ void __launch_bounds__(kAttnThreads) attention_o_kernel(const AttnOPa
             acc = fmaf(__uint_as_float(w2 & 0xFFFF0000u), s_o[t + 1], acc);
         }
         acc = warp_sum(acc);
-        if (lane == 0) __stcg(part + r, acc);
+        if (lane == 0) {
+            if constexpr (CLUSTER)
+                part[r] = acc;
+            else
+                __stcg(part + r, acc);
+        }
+    }
+    if constexpr (CLUSTER) {
+        namespace cg = cooperative_groups;
+        cg::cluster_group cluster = cg::this_cluster();
+        cluster.sync();  // every head's partial rows are in its shared memory
+        // cluster rank = kv head j; this CTA finishes rows j, j + HKV, ...
+        for (int r = j + a.HKV * int(threadIdx.x); r < R; r += a.HKV * kAttnThreads) {
+            float v = 0.f;
+            for (int h = 0; h < a.HKV; ++h) v += cluster.map_shared_rank(s_part, h)[r];
+            const int64_t n = int64_t(c) * R + r;
+            v += __bfloat162float(p.res[int64_t(b) * p.ldr + n]);
+            p.out[int64_t(b) * p.ldo + n] = __float2bfloat16_rn(v);
+        }
+        cluster.sync();  // no CTA leaves while another may still read its partials
+        return;
     }
     __threadfence();
     __syncthreads();
@@ -662,8 +689,12 @@ int32_t bq_attention_o_step(const bq_attn_o_desc* d, void* workspace, size_t wor
     p.ldo = d->ldo;
     p.counters = static_cast<unsigned int*>(workspace);
     p.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + kAttnCounterBytes);
-    const void* fn = ad->D == 128 ? reinterpret_cast<const void*>(&attention_o_kernel<4>)
-                                  : reinterpret_cast<const void*>(&attention_o_kernel<2>);
+    // a cluster of the HKV head CTAs of each (chunk, row) when it fits the portable size
+    const bool cluster = ad->HKV <= 8;
+    const void* fn = ad->D == 128 ? (cluster ? reinterpret_cast<const void*>(&attention_o_kernel<4, true>)
+                                             : reinterpret_cast<const void*>(&attention_o_kernel<4, false>))
+                                  : (cluster ? reinterpret_cast<const void*>(&attention_o_kernel<2, true>)
+                                             : reinterpret_cast<const void*>(&attention_o_kernel<2, false>));
     const uint32_t smem = uint32_t(R) * p.a.G * ad->D * 2 + uint32_t(p.a.G) * ad->D * 4;
     rc = ensure_smem_attr(fn, smem);
     if (rc) return rc;
@@ -673,13 +704,22 @@ int32_t bq_attention_o_step(const bq_attn_o_desc* d, void* workspace, size_t wor
     cfg.blockDim = dim3(kAttnThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = static_cast<cudaStream_t>(stream);
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
+    int na = 0;
     if (ad->flags & BQ_FLAG_PDL) {
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
     }
+    if (cluster) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = 1;
+        attr[na].val.clusterDim.y = unsigned(ad->HKV);
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    cfg.attrs = na ? attr : nullptr;
+    cfg.numAttrs = na;
     void* args[] = {&p};
     cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
     if (e != cudaSuccess) return set_error(BQ_ERR_CUDA, "attention + O launch failed: %s", cudaGetErrorString(e));

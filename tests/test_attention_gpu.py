@@ -138,6 +138,7 @@ FUSED_O_CASES = [
     (4, 16, 8, 128, 256, 255, True, 2048, False, "float"),
     (1, 8, 8, 128, 64, 40, True, 48, True, None),      # 16-row chunks
     (2, 8, 8, 128, 17, 9, True, 1024, True, "float"),  # the HF causal mask of a decoder layer
+    (2, 16, 16, 128, 64, 30, True, 512, True, None),   # HKV > 8: global partials, no cluster
 ]
 
 
