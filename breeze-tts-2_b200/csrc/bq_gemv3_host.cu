@@ -275,6 +275,22 @@ int plan_gemv3_uncached(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int slot
         for (int ks = 8; ks >= 2; ks /= 2)
             if (plan_gemv3_ks(d, rows, pl, dev->sm_count, ks) == BQ_OK) return BQ_OK;
     }
+    if (slots == 0) {
+        // Two CTAs of this GEMV per SM when both fit one SM's shared memory (the
+        // SM's capacity is the per-block opt-in plus 1 KB, each block reserving
+        // 1 KB): every CTA's serial chain (staging, group sums, main loop,
+        // epilogue) covers half as many units, which outweighs parking the next
+        // launch beside it. Plans that would need two waves keep one CTA per SM,
+        // and so do the f16-activation formats (fp8, int8) and M > 8, where it
+        // measured no better.
+        Gemv3Plan t2;
+        if ((int4fmt(d->wfmt) || d->wfmt == BQ_W_BF16) && rows <= 8 &&
+            plan_gemv3_ks(d, rows, &t2, 2 * dev->sm_count, 1) == BQ_OK &&
+            2 * (int64_t(t2.smem_total) + 1024) <= int64_t(dev->smem_optin) + 1024) {
+            *pl = t2;
+            return BQ_OK;
+        }
+    }
     return plan_gemv3_ks(d, rows, pl, slots > 0 ? slots : dev->sm_count, 1);
 }
 }  // namespace
