@@ -59,7 +59,7 @@ def measured_peak():
 
 # DRAM bytes (read + write) of one gemv3_kernel launch on this workload (mean of
 # two launches), from the ncu capture summarised in profiles/gemv3_int4_plain_config1.md.
-NCU_TRAFFIC_BYTES = 6_765_184
+NCU_TRAFFIC_BYTES = 6_769_920
 
 
 class ClockSampler:
