@@ -121,6 +121,8 @@ _SIGS = {
     "bq_gemv_chain_launch": (ctypes.c_int32, [ctypes.POINTER(GemvDesc), ctypes.c_int32, ctypes.c_void_p,
                                               ctypes.c_size_t, ctypes.c_void_p]),
     "bq_attention_workspace_bytes": (ctypes.c_int32, [ctypes.POINTER(AttnDesc), ctypes.POINTER(ctypes.c_size_t)]),
+    "bq_gemv_host_io": (ctypes.c_int32, [ctypes.POINTER(GemvDesc), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                          ctypes.c_size_t, ctypes.c_void_p]),
     "bq_attention_step": (ctypes.c_int32, [ctypes.POINTER(AttnDesc), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     "bq_attention_o_workspace_bytes": (ctypes.c_int32, [ctypes.POINTER(AttnODesc), ctypes.POINTER(ctypes.c_size_t)]),
     "bq_attention_o_step": (ctypes.c_int32, [ctypes.POINTER(AttnODesc), ctypes.c_void_p, ctypes.c_size_t,
@@ -304,19 +306,15 @@ def _gemv_key(x, w, wfmt, n, scale, group, gamma, eps, epilogue, residual, bias,
             out.data_ptr(), out.shape, out.stride(), out.dtype, flags)
 
 
-def gemv(x: torch.Tensor, w: torch.Tensor, wfmt: int, n: int, *, scale=None, group: int = 128, gamma=None,
-         eps: float = 1e-6, epilogue: int = EPI_NONE, residual=None, bias=None, out: torch.Tensor | None = None,
-         out_dtype: torch.dtype | None = None, flags: int = 0) -> torch.Tensor:
-    """out = epilogue(rmsnorm(x) @ dequant(w)^T) on the current stream."""
+def _gemv_prepared(x, w, wfmt, n, scale, group, gamma, eps, epilogue, residual, bias, out, out_dtype, flags):
+    """(descriptor, workspace, out) of one GEMV; descriptors over the caller's
+    own tensors are cached by the tensors' addresses, shapes and options."""
     key = None
     if out is not None and x.is_cuda:
         key = _gemv_key(x, w, wfmt, n, scale, group, gamma, eps, epilogue, residual, bias, out, flags)
         hit = _GEMV_CACHE.get(key)
         if hit is not None:
-            d, ws = hit
-            check(_lib.bq_gemv(ctypes.byref(d), ws.data_ptr(), ws.numel(), torch.cuda.current_stream(x.device).cuda_stream),
-                  "bq_gemv")
-            return out
+            return hit[0], hit[1], out
     dev = _require_cuda(x, w, scale, gamma, residual, bias, out)
     own = (_ptr(gamma), _ptr(bias))  # the caller's own tensors, before any dtype conversion
     x = _rowmajor(x, "x")
@@ -341,13 +339,42 @@ def gemv(x: torch.Tensor, w: torch.Tensor, wfmt: int, n: int, *, scale=None, gro
     need = ctypes.c_size_t(0)
     check(lib.bq_gemv_workspace_bytes(ctypes.byref(d), ctypes.byref(need)), "bq_gemv_workspace_bytes")
     ws = WORKSPACE.get(dev, need.value)
-    check(lib.bq_gemv(ctypes.byref(d), ws.data_ptr(), ws.numel(), _stream(dev)), "bq_gemv")
     # cache only descriptors that point at the caller's own tensors (no converted copies)
     if key is not None and (d.gamma, d.bias) == own:
         if len(_GEMV_CACHE) >= _GEMV_CACHE_MAX:
             _GEMV_CACHE.clear()
         _GEMV_CACHE[key] = (d, ws)
+    return d, ws, out
+
+
+def gemv(x: torch.Tensor, w: torch.Tensor, wfmt: int, n: int, *, scale=None, group: int = 128, gamma=None,
+         eps: float = 1e-6, epilogue: int = EPI_NONE, residual=None, bias=None, out: torch.Tensor | None = None,
+         out_dtype: torch.dtype | None = None, flags: int = 0) -> torch.Tensor:
+    """out = epilogue(rmsnorm(x) @ dequant(w)^T) on the current stream."""
+    d, ws, out = _gemv_prepared(x, w, wfmt, n, scale, group, gamma, eps, epilogue, residual, bias, out, out_dtype,
+                                flags)
+    check(_lib.bq_gemv(ctypes.byref(d), ws.data_ptr(), ws.numel(), torch.cuda.current_stream(x.device).cuda_stream),
+          "bq_gemv")
     return out
+
+
+def gemv_host_io(x_host: torch.Tensor, x: torch.Tensor, w: torch.Tensor, wfmt: int, n: int, *, out: torch.Tensor,
+                 out_host: torch.Tensor, scale=None, group: int = 128, gamma=None, eps: float = 1e-6,
+                 epilogue: int = EPI_NONE, residual=None, bias=None, flags: int = 0) -> torch.Tensor:
+    """gemv with host-side input and output in one call (bq_gemv_host_io):
+    x_host -> x, the GEMV into out, out -> out_host, enqueued on the current
+    stream without waiting. x_host / out_host: dense CPU tensors shaped like x
+    and out (pinned for asynchronous copies). Returns out_host."""
+    if x_host.is_cuda or out_host.is_cuda:
+        raise ValueError("x_host and out_host must be CPU tensors")
+    if x_host.shape != x.shape or x_host.dtype != x.dtype or not x_host.is_contiguous():
+        raise ValueError("x_host must be a dense CPU copy of x's shape and dtype")
+    d, ws, out = _gemv_prepared(x, w, wfmt, n, scale, group, gamma, eps, epilogue, residual, bias, out, None, flags)
+    if out_host.shape != out.shape or out_host.dtype != out.dtype or not out_host.is_contiguous():
+        raise ValueError("out_host must be a dense CPU tensor of out's shape and dtype")
+    check(_lib.bq_gemv_host_io(ctypes.byref(d), x_host.data_ptr(), out_host.data_ptr(), ws.data_ptr(), ws.numel(),
+                               torch.cuda.current_stream(x.device).cuda_stream), "bq_gemv_host_io")
+    return out_host
 
 
 def gemv_desc(x: torch.Tensor, w: torch.Tensor, wfmt: int, n: int, *, out: torch.Tensor, scale=None,

@@ -124,6 +124,21 @@ def rms_gemv(x, fw: FusedWeight, norm_weight=None, eps: float = 1e-6, epilogue: 
                      out_dtype=torch.bfloat16 if residual is None else residual.dtype, flags=_lib.default_flags())
 
 
+def rms_gemv_host_io(x_host, fw: FusedWeight, norm_weight=None, eps: float = 1e-6, epilogue: int = 0, residual=None,
+                     *, x, out, out_host):
+    """rms_gemv on host data in one call: x_host (dense CPU, pinned for an
+    asynchronous copy) is copied into the device buffer ``x``, the GEMV writes
+    ``out``, and ``out`` is copied into ``out_host``; everything is enqueued on
+    the current stream (bq_gemv_host_io). Returns out_host, valid once the
+    stream reaches it."""
+    if x.shape[1] != fw.K:
+        raise ValueError(f"x has K={x.shape[1]}, weight has K={fw.K}")
+    a = fw.gemv_args()
+    return _lib.gemv_host_io(x_host, x, fw.w, a["wfmt"], fw.N, out=out, out_host=out_host, scale=a["scale"],
+                             group=GROUP, gamma=norm_weight, eps=eps, epilogue=epilogue, residual=residual,
+                             flags=_lib.default_flags())
+
+
 def attention_step(qkv, cos, sin, cache_position, keys, values, mask, q_norm_w=None, k_norm_w=None, eps=1e-6,
                    out=None, q_buf=None):  # noqa: ARG001 - q_buf: API parity (the kernel keeps q on chip)
     """qkv (B, (HQ+2HKV)*D) bf16 -> attention output (B, HQ*D) bf16, with the

@@ -260,4 +260,24 @@ int32_t bq_gemv(const bq_gemv_desc* desc, void* workspace, size_t workspace_byte
     return BQ_OK;
 }
 
+int32_t bq_gemv_host_io(const bq_gemv_desc* desc, const void* x_host, void* out_host, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+    int rc = validate_gemv(desc);
+    if (rc) return rc;
+    if (!x_host || !out_host) return set_error(BQ_ERR_INVALID_ARG, "x_host and out_host must be non-NULL");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t xs = size_t(dtype_size(desc->x_dtype)), os = size_t(dtype_size(desc->out_dtype));
+    const size_t n_out = size_t(desc->epilogue == BQ_EPI_SILU_MUL ? desc->N / 2 : desc->N);
+    // dense host rows into the (possibly strided) device activations
+    cudaError_t e = cudaMemcpy2DAsync(const_cast<void*>(desc->x), size_t(desc->ldx) * xs, x_host, size_t(desc->K) * xs,
+                                      size_t(desc->K) * xs, size_t(desc->M), cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return set_error(BQ_ERR_CUDA, "input copy failed: %s", cudaGetErrorString(e));
+    rc = bq_gemv(desc, workspace, workspace_bytes, stream);
+    if (rc) return rc;
+    e = cudaMemcpy2DAsync(out_host, n_out * os, desc->out, size_t(desc->ldo) * os, n_out * os, size_t(desc->M),
+                          cudaMemcpyDeviceToHost, st);
+    if (e != cudaSuccess) return set_error(BQ_ERR_CUDA, "output copy failed: %s", cudaGetErrorString(e));
+    return BQ_OK;
+}
+
 }  // extern "C"

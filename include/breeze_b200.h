@@ -125,6 +125,16 @@ int32_t bq_gemv_workspace_bytes(const bq_gemv_desc* desc, size_t* bytes);
  * models/int8_linear.py:50-53. */
 int32_t bq_gemv(const bq_gemv_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
 
+/* bq_gemv with host-side input and output: x_host (M rows of K values, dense,
+ * x_dtype) is copied into desc->x, the GEMV runs, and the output (M rows of
+ * N, or N / 2 with the SiLU epilogue, dense, out_dtype) is copied from
+ * desc->out into out_host, all enqueued on `stream` (pinned host memory makes
+ * the copies asynchronous); the call does not wait. Replaces rms_gemv
+ * (models/fused/kernels.py:334-351) on tensors that the caller moves to the
+ * device and back around it. */
+int32_t bq_gemv_host_io(const bq_gemv_desc* desc, const void* x_host, void* out_host, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
 /* Same computation as bq_gemv, for callers that cannot allocate device
  * memory (fixed VRAM budgets, hosts that own all allocations, real-time
  * threads that must not call cudaMalloc/cudaFree). No counterpart in the

@@ -173,3 +173,17 @@ def test_attention_o_desc_validation_without_gpu(lib):
     bad.attn.mask, bad.attn.mask_dtype = 256, 9
     assert lib.bq_attention_o_workspace_bytes(ctypes.byref(bad), ctypes.byref(need)) == L.BQ_ERR_INVALID_ARG
     assert lib.bq_attention_o_step(ctypes.byref(od), None, 0, None) != 0
+
+
+def test_gemv_host_io_argument_checks(lib):
+    """bq_gemv_host_io validates the descriptor and its host pointers before
+    any copy or launch (no GPU needed)."""
+    import ctypes
+
+    from breeze_b200 import _lib as L
+
+    d = _desc()
+    assert lib.bq_gemv_host_io(ctypes.byref(d), None, None, None, 0, None) == L.BQ_ERR_INVALID_ARG
+    assert b"x_host" in lib.bq_last_error_string()
+    bad = _desc(K=200)
+    assert lib.bq_gemv_host_io(ctypes.byref(bad), 16, 16, None, 0, None) == L.BQ_ERR_SHAPE

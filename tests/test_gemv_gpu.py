@@ -397,3 +397,30 @@ def test_gemv_k_split_large_m(fmt, m, n, k, epi):
     ref = gemv.fused_reference(x, case["deq"], None, 1e-6, epi, res)
     assert gemv.max_rel_err(got.float(), ref) < TOL
     assert torch.equal(got, again)
+
+
+@pytest.mark.parametrize("fmt", ["int4_plain", "int4_tinygemm", "fp8"])
+@pytest.mark.parametrize("m,epi", [(1, 0), (2, 1), (3, 2)])
+def test_gemv_host_io_matches_device_call(fmt, m, epi):
+    """bq_gemv_host_io (host input and output, copies enqueued with the GEMV)
+    gives bit-for-bit the output of bq_gemv on the same data."""
+    L = _lib()
+    n, k = 256, 512
+    case = make_weight(fmt, n, k, seed=m + epi)
+    g = torch.Generator().manual_seed(17 * m + epi)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    gamma = (1 + 0.1 * torch.randn(k, generator=g)).to(torch.bfloat16) if epi != 2 else None
+    n_out = n // 2 if epi == 1 else n
+    res = torch.randn(m, n_out, generator=g).to(torch.bfloat16) if epi == 2 else None
+    ref = run_gemv(case, x, n, gamma=gamma, epilogue=epi, residual=res, fmt=fmt)
+    w = case["w"].to(DEV)
+    scale = None if case["scale"] is None else case["scale"].to(DEV)
+    xd = torch.zeros(m, k, device=DEV, dtype=torch.bfloat16)
+    out = torch.empty(m, n_out, device=DEV, dtype=torch.bfloat16)
+    x_host, out_host = x.pin_memory(), torch.zeros(m, n_out, dtype=torch.bfloat16).pin_memory()
+    got = L.gemv_host_io(x_host, xd, w, wfmt_code(fmt), n, out=out, out_host=out_host, scale=scale,
+                         group=case["group"], gamma=None if gamma is None else gamma.to(DEV), eps=1e-6, epilogue=epi,
+                         residual=None if res is None else res.to(DEV), flags=L.default_flags())
+    torch.cuda.synchronize()
+    assert torch.equal(got, ref)
+    assert torch.equal(xd.cpu(), x)
