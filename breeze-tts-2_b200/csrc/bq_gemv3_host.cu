@@ -258,12 +258,20 @@ int plan_gemv3_uncached(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int slot
     // split (more partial sums to reduce) must shorten it by a fifth.
     if (slots == 0 && !d->gamma && d->epilogue != BQ_EPI_SILU_MUL) {
         const int KB = d->K / kKB;
+        // Long K (8 or more k-blocks per warp over the whole K: the down projections)
+        // with int4 or bf16 weights and M <= 8: plan for two CTAs per SM, so that K
+        // slices halve every warp's serial chain (depth down 1024x8192 M=2 7.46 ->
+        // 6.63 us, backbone down 2048x8192 M=2 10.21 -> 8.76 us). Shorter K
+        // (O 2048x2048: 3.86 -> 5.98 us) and fp8 / int8 measured slower that way.
+        const bool two_per_sm = (int4fmt(d->wfmt) || d->wfmt == BQ_W_BF16) && rows <= 8 && KB / 8 >= 8;
+        const int sms = two_per_sm ? 2 * dev->sm_count : dev->sm_count;
         bool found = false;
         int64_t best = 0;
         for (int ks = 1; ks <= 8; ks *= 2) {
             Gemv3Plan t;
-            if (plan_gemv3_ks(d, rows, &t, dev->sm_count, ks) != BQ_OK || t.smem_total > kTargetSmem) continue;
-            const int64_t cost = warp_load_max(t, KB, dev->sm_count);
+            if (plan_gemv3_ks(d, rows, &t, sms, ks) != BQ_OK || t.smem_total > kTargetSmem) continue;
+            if (two_per_sm && 2 * (int64_t(t.smem_total) + 1024) > int64_t(dev->smem_optin) + 1024) continue;
+            const int64_t cost = warp_load_max(t, KB, sms);
             if (!found || 5 * cost <= 4 * best) {
                 *pl = t;
                 best = cost;
