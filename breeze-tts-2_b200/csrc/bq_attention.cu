@@ -651,7 +651,14 @@ int32_t bq_attention_o_step(const bq_attn_o_desc* d, void* workspace, size_t wor
     if (!dev) return BQ_ERR_CUDA;
     if (dev->major != 10) return set_error(BQ_ERR_DEVICE, "sm_%d%d device: this library is built for sm_100a", dev->major, dev->minor);
     const bq_attn_desc* ad = &d->attn;
-    const int R = attn_o_rows(d), chunks = d->N / R;
+    // 32-row chunks when the grid still fits two CTAs per SM: each CTA's Wo slice
+    // and partial rows halve (depth frame at B = 1: 6156 -> 5947 us); beyond that
+    // the CTAs run in waves (B = 2: 6392 -> 7030 us) and 64-row chunks stay
+    int R = attn_o_rows(d);
+    if (R > 32 && d->N % 32 == 0 && int64_t(d->N / 32) * ad->HKV * ad->B <= 2 * int64_t(dev->sm_count) &&
+        int64_t(d->N / 32) * ad->B <= kAttnMaxPairs)
+        R = 32;
+    const int chunks = d->N / R;
     const size_t need = kAttnCounterBytes + size_t(chunks) * ad->HKV * ad->B * R * 4;
     if (!workspace || workspace_bytes < need)
         return set_error(BQ_ERR_WORKSPACE, "attention + O workspace of %zu bytes given, %zu needed", workspace_bytes, need);
