@@ -454,6 +454,10 @@ def run_reference(args, rank):
         return
     from oracle import cpu_path
 
+    # rank 0 alone runs the CPU path: every host core this process may use (torchrun
+    # sets OMP_NUM_THREADS=1 for its ranks)
+    torch.set_num_threads(len(os.sched_getaffinity(0)))
+
     x, packed, scale, mn, gamma = _cpu_inputs()
     for _ in range(args.warmup):
         cpu_path.rms_gemv_int4_plain(x, packed, scale, mn, gamma, EPS)
