@@ -163,28 +163,30 @@ def load_tuning(device) -> None:  # noqa: ARG001 - API parity: launch shapes nee
     """No-op: bq_gemv derives its launch shape from the device."""
 
 
-def graph_time_us(fn, iters: int = 20) -> float:
-    """GPU time per call of ``fn`` measured as CUDA-graph replays
-    (the reference's timing method, models/fused/kernels.py:222-243)."""
-    fn()
+def graph_time_us(fn, iters: int = 20, replays: int = 7) -> float:
+    """Device time per call of ``fn`` in microseconds, the way the decode
+    graphs pay for it: ``iters`` calls are recorded into one CUDA graph, the
+    graph is replayed ``replays`` times with CUDA events around each replay,
+    and the median replay is divided by ``iters``. Same name, arguments and
+    unit as the reference's helper (models/fused/kernels.py:222-243)."""
+    fn()  # outside capture: workspaces reach their size, descriptors are cached
     torch.cuda.synchronize()
-    st = torch.cuda.Stream()
-    st.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(st):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=st):
-            for _ in range(iters):
-                fn()
-    torch.cuda.current_stream().wait_stream(st)
-    g.replay()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side), torch.cuda.graph(graph, stream=side):
+        for _ in range(iters):
+            fn()
+    torch.cuda.current_stream().wait_stream(side)
+    graph.replay()
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(replays + 1)]
+    marks[0].record()
+    for i in range(replays):
+        graph.replay()
+        marks[i + 1].record()
     torch.cuda.synchronize()
-    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s_ev.record()
-    for _ in range(5):
-        g.replay()
-    e_ev.record()
-    torch.cuda.synchronize()
-    return s_ev.elapsed_time(e_ev) / (5 * iters) * 1000
+    per_replay = sorted(a.elapsed_time(b) for a, b in zip(marks, marks[1:]))
+    return per_replay[len(per_replay) // 2] * 1e3 / iters
 
 
 def cold_copies(fw: FusedWeight, budget_bytes: int | None = None) -> list:

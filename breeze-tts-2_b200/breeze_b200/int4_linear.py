@@ -86,6 +86,26 @@ class Int4Linear(nn.Module):
         return (f"in_features={self.in_features}, out_features={self.out_features}, "
                 f"int4=True, group={self.group_size}")
 
+    # manifest record of a quantized checkpoint (quantized_checkpoint.py:39-48 of the reference)
+    MANIFEST_KIND = "int4"
+    MANIFEST_BUFFERS = (("weight_int4", torch.int32), ("scales_zeros", torch.bfloat16))
+
+    def manifest_entry(self) -> dict:
+        return {"kind": self.MANIFEST_KIND, "in_features": self.in_features, "out_features": self.out_features,
+                "group_size": self.group_size,
+                "shapes": {name: list(getattr(self, name).shape) for name, _ in self.MANIFEST_BUFFERS}}
+
+    @classmethod
+    def from_manifest(cls, entry: dict, device) -> "Int4Linear":
+        """An uninitialised module with the recorded geometry, for a checkpoint's
+        tensors to be assigned into; the packed shapes come from the manifest."""
+        m = cls.__new__(cls)
+        nn.Module.__init__(m)
+        m.in_features, m.out_features, m.group_size = entry["in_features"], entry["out_features"], entry["group_size"]
+        for name, dtype in cls.MANIFEST_BUFFERS:
+            m.register_buffer(name, torch.empty(entry["shapes"][name], dtype=dtype, device=device))
+        return m
+
 
 def quantize_module_int4(root: nn.Module, *, target_names: tuple[str, ...] = DEFAULT_TARGET_NAMES,
                          min_bytes: int = MIN_QUANT_BYTES, device: torch.device | str | None = None,

@@ -48,6 +48,28 @@ class Int8Linear(nn.Module):
     def extra_repr(self) -> str:
         return f"in_features={self.in_features}, out_features={self.out_features}, int8=True"
 
+    # manifest record of a quantized checkpoint (quantized_checkpoint.py:50-59 of the reference)
+    MANIFEST_KIND = "int8"
+    MANIFEST_BUFFERS = (("weight_int8", torch.int8), ("weight_scale", torch.float32))
+
+    def manifest_entry(self) -> dict:
+        return {"kind": self.MANIFEST_KIND, "in_features": self.in_features, "out_features": self.out_features,
+                "has_bias": self.bias is not None,
+                "shapes": {name: list(getattr(self, name).shape) for name, _ in self.MANIFEST_BUFFERS}}
+
+    @classmethod
+    def from_manifest(cls, entry: dict, device) -> "Int8Linear":
+        """An uninitialised module with the recorded geometry (and a bias slot
+        when the entry has one), for a checkpoint's tensors to be assigned into."""
+        m = cls.__new__(cls)
+        nn.Module.__init__(m)
+        m.in_features, m.out_features = entry["in_features"], entry["out_features"]
+        for name, dtype in cls.MANIFEST_BUFFERS:
+            m.register_buffer(name, torch.empty(entry["shapes"][name], dtype=dtype, device=device))
+        m.register_buffer("bias", torch.empty(m.out_features, dtype=torch.bfloat16, device=device)
+                          if entry.get("has_bias") else None)
+        return m
+
 
 def quantize_module_int8(root: nn.Module, *, target_names: tuple[str, ...] | None = None,
                          min_bytes: int = MIN_QUANT_BYTES) -> dict[str, int]:

@@ -1,5 +1,5 @@
 // C ABI entry points (include/breeze_b200.h), argument validation, error
-// reporting, device property cache and TMA descriptor encoding.
+// reporting and the device property cache.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -14,6 +14,10 @@
 #include "bq_host.h"
 
 namespace bq {
+
+// Device error word, one per device: bounded waits that give up set bits here
+// (read and cleared through bq_device_status / bq_device_status_clear).
+__device__ unsigned int g_device_error = 0;
 
 namespace {
 thread_local char g_err[512] = "no error";
@@ -75,69 +79,6 @@ int ensure_smem_attr(const void* fn, uint32_t bytes) {
     (void)bytes;
     std::lock_guard<std::mutex> lk(g_mu);
     g_smem_attr.emplace_back(fn, dev);
-    return BQ_OK;
-}
-
-// ---- TMA descriptors ------------------------------------------------------
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(p);
-    });
-    return fn;
-}
-
-static int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
-                     uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer) {
-    EncodeTiledFn fn = encode_fn();
-    if (!fn) return set_error(BQ_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-    cuuint64_t dims[2] = {inner, outer};
-    cuuint64_t strides[1] = {row_stride_bytes};
-    cuuint32_t box[2] = {box_inner, box_outer};
-    cuuint32_t es[2] = {1, 1};
-    CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return set_error(BQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
-    return BQ_OK;
-}
-
-int encode_weight_maps(const bq_gemv_desc* d, CUtensorMap* tm_w, CUtensorMap* tm_sz) {
-    const uint64_t N = d->N, K = d->K;
-    int rc = BQ_OK;
-    switch (d->wfmt) {
-        case BQ_W_INT4_TINYGEMM:
-            rc = encode_2d(tm_w, CU_TENSOR_MAP_DATA_TYPE_INT32, d->w, K, N / 8, K * 4, 128, 2);
-            break;
-        case BQ_W_INT4_PLAIN:
-            rc = encode_2d(tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, d->w, K / 2, N, K / 2, 64, 16);
-            break;
-        case BQ_W_FP8_E4M3:
-        case BQ_W_INT8:
-            rc = encode_2d(tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, d->w, K, N, K, 64, 16);
-            break;
-        case BQ_W_BF16:
-            rc = encode_2d(tm_w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d->w, K, N, K * 2, 32, 16);
-            break;
-        default:
-            return set_error(BQ_ERR_FORMAT, "unknown weight format %d", d->wfmt);
-    }
-    if (rc) return rc;
-    if (d->wfmt == BQ_W_INT4_TINYGEMM || d->wfmt == BQ_W_INT4_PLAIN) {
-        const int g = d->group;
-        const uint32_t rows = g >= 128 ? 1 : 128 / g;
-        return encode_2d(tm_sz, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d->scale, 2 * N, K / g, 4 * N, 32, rows);
-    }
-    *tm_sz = *tm_w;
     return BQ_OK;
 }
 

@@ -1,6 +1,6 @@
-// Device helpers for sm_100a: mbarriers, TMA tile loads, programmatic
+// Device helpers for sm_100a: mbarriers, cp.async copies, programmatic
 // dependent launch, m16n8k16 tensor-core MMA and in-register dequantization
-// of int4 / fp8 / int8 weights into f16 pairs. Hand-written inline PTX.
+// of int4 / fp8 / int8 weights into bf16 / f16 pairs. Hand-written inline PTX.
 #pragma once
 
 #include <cuda.h>
@@ -73,27 +73,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     return true;
 }
 
-// ---------------------------------------------------------------- TMA
-// 2-D tiled bulk tensor load global -> shared, completion on an mbarrier.
-// No cluster multicast: every CTA fetches its own tiles.
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int32_t c0, int32_t c1,
-                                            uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
-        : "memory");
-}
-
-__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
-}
-
 // ---------------------------------------------------------------- cp.async
-// 8-byte asynchronous global -> shared copy (L2 only, no registers used).
-__device__ __forceinline__ void cp_async8(uint32_t dst, const void* src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
-}
 // 16-byte asynchronous global -> shared copy, L2 only (both addresses 16-byte aligned).
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
@@ -109,23 +89,6 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // ---------------------------------------------------------------- loads
-__device__ __forceinline__ uint4 lds128(uint32_t addr) {
-    uint4 v;
-    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "r"(addr));
-    return v;
-}
-__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
-    uint32_t v;
-    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
-    return v;
-}
-__device__ __forceinline__ float2 lds_f2(uint32_t addr) {
-    float2 v;
-    asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
-    return v;
-}
 // L2-coherent loads of data written by other CTAs during this kernel.
 __device__ __forceinline__ float4 ldcg_f4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
 
@@ -165,44 +128,10 @@ __device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b) {
     asm("sub.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
     return d;
 }
-__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
-    uint32_t d;
-    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-    return d;
-}
-
-// Two int4 codes sitting in bits [0,4) and [16,20) of `w` (the 0x000F000F
-// lanes) -> f16x2 {code - OFS}, exact. 0x6400 is 1024.0 in f16; OR-ing a
-// 4-bit code into its mantissa gives 1024 + code.
-template <int OFS>
-__device__ __forceinline__ uint32_t i4lo_to_f16x2(uint32_t w) {
-    constexpr uint32_t kBias = (OFS == 8) ? 0x64086408u : 0x64006400u;  // 1032 / 1024
-    return hsub2(lop3<(0xF0 & 0xCC) | 0xAA>(w, 0x000F000Fu, 0x64006400u), kBias);
-}
-// Codes in bits [4,8) and [20,24) (the 0x00F000F0 lanes): 1024 + 16*code,
-// then (v * 1/16) - (64 + OFS) = code - OFS, exact.
-template <int OFS>
-__device__ __forceinline__ uint32_t i4hi_to_f16x2(uint32_t w) {
-    constexpr uint32_t kScale = 0x2C002C00u;                             // 1/16
-    constexpr uint32_t kBias = (OFS == 8) ? 0xD480D480u : 0xD400D400u;  // -72 / -64
-    return hfma2(lop3<(0xF0 & 0xCC) | 0xAA>(w, 0x00F000F0u, 0x64006400u), kScale, kBias);
-}
-
-// int4 codes -> f16 pairs WITHOUT removing the magic offset (one LOP3 each).
-// Low lanes (bits 0-3 / 16-19): 1024 + q. High lanes (bits 4-7 / 20-23):
-// 1024 + 16 q. The GEMV pre-scales the activations that meet high lanes by
-// 1/16 and subtracts the offsets once per group from precomputed sums.
 // bf16 pair 128 + q from nibbles 0 and 4 of w (bits 0-3, 16-19): exact, one LOP3.
 __device__ __forceinline__ uint32_t i4_bf16(uint32_t w) {
     return lop3<(0xF0 & 0xCC) | 0xAA>(w, 0x000F000Fu, 0x43004300u);
 }
-__device__ __forceinline__ uint32_t i4lo_raw(uint32_t w) {
-    return lop3<(0xF0 & 0xCC) | 0xAA>(w, 0x000F000Fu, 0x64006400u);
-}
-__device__ __forceinline__ uint32_t i4hi_raw(uint32_t w) {
-    return lop3<(0xF0 & 0xCC) | 0xAA>(w, 0x00F000F0u, 0x64006400u);
-}
-
 // Two e4m3 bytes (low byte -> low half) -> f16x2, exact (hardware cvt).
 __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint16_t v) {
     uint32_t d;

@@ -16,14 +16,6 @@ struct DeviceInfo {
     int major, minor;
 };
 
-struct GemvPlan {
-    int mt, gpk;
-    int grid, workers, ring_slots, slot_bytes, xfrag_kb, p_max, n_units;
-    int64_t total_chunks;
-    uint32_t smem;
-    int64_t counters_bytes, partials_bytes;
-};
-
 // Records a thread-local error message and returns `code`.
 int set_error(int code, const char* fmt, ...);
 
@@ -34,10 +26,6 @@ int dtype_size(int dt);
 
 // Raises the kernel's dynamic shared memory limit once per (kernel, device).
 int ensure_smem_attr(const void* fn, uint32_t bytes);
-
-// Builds the TMA descriptors for the weight tensor and, for int4, the
-// [K/g, N, 2] scale/zero tensor.
-int encode_weight_maps(const bq_gemv_desc* d, CUtensorMap* tm_w, CUtensorMap* tm_sz);
 
 struct Gemv3Plan {
     int rows, mt, upc, tpu, gpk, ug, ksplit;
@@ -54,9 +42,5 @@ int plan_gemv3(const bq_gemv_desc* d, int rows, Gemv3Plan* pl, int slots = 0);
 int gemv3_tile_bytes(int fmt, int gpk);
 int gemv3_gpk(const bq_gemv_desc* d);
 int launch_gemv3(const bq_gemv_desc* d, const Gemv3Plan& pl, int row0, void* workspace, cudaStream_t stream);
-
-int plan_gemv(const bq_gemv_desc* d, int rows, GemvPlan* pl);
-int launch_gemv(const bq_gemv_desc* d, const GemvPlan& pl, int row0, int rows, void* workspace,
-                cudaStream_t stream);
 
 }  // namespace bq

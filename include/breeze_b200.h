@@ -99,7 +99,7 @@ typedef struct bq_gemv_desc {
     const void* gamma;    /* bf16 [K] RMSNorm weight, or NULL for no norm */
     const void* w;        /* packed weights, 16-byte aligned */
     const void* scale;    /* see BQ_W_* */
-    const void* bias;     /* bf16 [N] or NULL (int8 / bf16 formats) */
+    const void* bias;     /* [N] in out_dtype (the output's element type), or NULL */
     const void* residual; /* [M, ldr] for BQ_EPI_ADD_RESIDUAL, else NULL */
     int64_t ldr;
     void* out;            /* [M, ldo] */
@@ -135,15 +135,17 @@ int32_t bq_gemv(const bq_gemv_desc* desc, void* workspace, size_t workspace_byte
 int32_t bq_gemv_host_io(const bq_gemv_desc* desc, const void* x_host, void* out_host, void* workspace,
                         size_t workspace_bytes, void* stream);
 
-/* Same computation as bq_gemv, for callers that cannot allocate device
- * memory (fixed VRAM budgets, hosts that own all allocations, real-time
- * threads that must not call cudaMalloc/cudaFree). No counterpart in the
- * reference. Instead of a caller workspace it uses one 4 MiB scratch array
- * built into the library (held by every GPU that loads it until exit);
- * shapes needing more scratch return BQ_ERR_WORKSPACE without launching.
- * The first call on a device sets the array up (blocking; make it before
- * any stream capture). All calls on a device share the array: calls whose
- * kernels can overlap on the GPU race and must be serialized. */
+/* bq_gemv for callers that cannot allocate device memory (fixed VRAM
+ * budgets, hosts that own every allocation, real-time threads that must not
+ * call cudaMalloc/cudaFree). No counterpart in the reference. The same kernel
+ * and launch plan as bq_gemv, with one 4 MiB scratch array built into the
+ * library (held by every GPU that loads it until exit) in place of the
+ * caller's workspace; shapes whose bq_gemv_workspace_bytes exceed it return
+ * BQ_ERR_WORKSPACE without launching. The first call on a device (and the
+ * first after a cudaDeviceReset) clears the array's counters with a blocking
+ * memset: make it before any stream capture. All calls on a device share the
+ * array: calls whose kernels can overlap on the GPU race and must be
+ * serialized on one stream. */
 int32_t bq_gemv_noalloc(const bq_gemv_desc* desc, void* stream);
 
 /* ---- decode chain: a list of GEMVs in one launch ------------------------ */

@@ -111,8 +111,9 @@ def tinygemm_pack(packed_u8: torch.Tensor, inner_k_tiles: int = INNER_K_TILES) -
     return torch.from_numpy(word.view(np.int32).copy())
 
 
-def tinygemm_unpack(weight_int4: torch.Tensor) -> torch.Tensor:
-    """Inverse of tinygemm_pack: int32 tiles -> (N, K/2) uint8 (odd k low)."""
+def tinygemm_unpack_indexed(weight_int4: torch.Tensor) -> torch.Tensor:
+    """Inverse of tinygemm_pack through the explicit index map (slow; the
+    check for ``tinygemm_unpack``)."""
     w = weight_int4.numpy().view(np.uint32)
     nt, kt, _, half = w.shape
     n, k, ik = nt * 8, kt * half * 2 * 16, half * 2
@@ -123,6 +124,21 @@ def tinygemm_unpack(weight_int4: torch.Tensor) -> torch.Tensor:
         lo = (w >> (16 + 4 * i)) & 15
         out[row[..., i], byte[..., i]] = ((hi << 4) | lo).astype(np.uint8)
     return torch.from_numpy(out)
+
+
+def tinygemm_unpack(weight_int4: torch.Tensor) -> torch.Tensor:
+    """Inverse of tinygemm_pack: int32 tiles -> (N, K/2) uint8 (odd k low).
+
+    The index map of ``_tinygemm_byte_index`` is a permutation of axes: with
+    lane = 4r + c, word [nt, ko, lane, j] byte i lands in row 8nt + r at byte
+    ko*ik*8 + 16j + 4i + c, i.e. a row's bytes run in (ko, j, i, c) order. So
+    the unpack is one transpose of [nt, ko, r, c, j, i] to [nt, r, ko, j, i, c]
+    (identical to the indexed form, which the oracle tests compare)."""
+    w = weight_int4.numpy().view(np.uint32)
+    nt, kt, _, half = w.shape
+    by = np.stack([(((w >> (4 * i)) & 15) << 4) | ((w >> (16 + 4 * i)) & 15) for i in range(4)], -1)
+    by = by.astype(np.uint8).reshape(nt, kt, 8, 4, half, 4)  # [nt, ko, r, c, j, i]
+    return torch.from_numpy(np.ascontiguousarray(by.transpose(0, 2, 1, 4, 5, 3)).reshape(nt * 8, kt * half * 16))
 
 
 def codes_from_odd_low(packed_u8: torch.Tensor) -> torch.Tensor:
@@ -148,20 +164,22 @@ def quantize_int4(weight: torch.Tensor, group_size: int = GROUP_SIZE):
     return tinygemm_pack(pack_odd_low(q)), scales_zeros(scale, lo)
 
 
-def _fmaf(a: np.ndarray, b: np.ndarray, c: np.ndarray) -> np.ndarray:
-    """fp32 fused multiply-add. Exact here: a*b+c is formed in float64 (the
-    operands carry <= 24 significant bits and the product of a 4/8-bit code
-    with a bf16/fp32 scale is exact in float64) and rounded once."""
-    return (a.astype(np.float64) * b.astype(np.float64) + c.astype(np.float64)).astype(np.float32)
+def _grouped_fma(q: np.ndarray, s: np.ndarray, z: np.ndarray, group: int) -> np.ndarray:
+    """fp32 W[N, K] = q * s + z per group of ``group`` along K, with q (N, K)
+    small integers and s, z (N, K/group) bf16-valued. q * s is exact in fp32
+    (a 4-bit integer times an 8-bit significand), so the single rounding of
+    the add equals fmaf(q, s, z), the reference's dequant rounding."""
+    n, k = q.shape
+    w = q.astype(np.float32).reshape(n, k // group, group) * s[..., None] + z[..., None]
+    return w.reshape(n, k)
 
 
 def dequant_int4_tinygemm(weight_int4: torch.Tensor, sz: torch.Tensor, group_size: int) -> torch.Tensor:
     """fp32 W[N, K] = (q - 8) * scale + zero, one rounding (fmaf)."""
     q = codes_from_odd_low(tinygemm_unpack(weight_int4)).numpy()
     szf = sz.float().numpy()  # [K/g, N, 2]
-    s = np.repeat(szf[..., 0].T, group_size, axis=1)
-    z = np.repeat(szf[..., 1].T, group_size, axis=1)
-    return torch.from_numpy(_fmaf(q.astype(np.float32) - 8.0, s, z))
+    return torch.from_numpy(_grouped_fma(q - 8, np.ascontiguousarray(szf[..., 0].T),
+                                         np.ascontiguousarray(szf[..., 1].T), group_size))
 
 
 # --------------------------------------------------------------------------
@@ -190,10 +208,8 @@ def codes_from_even_low(packed_u8: torch.Tensor) -> torch.Tensor:
 
 def dequant_int4_plain(packed: torch.Tensor, scale: torch.Tensor, mn: torch.Tensor, group: int = 128) -> torch.Tensor:
     """fp32 W = q * scale + min (bench_gemv.py:51-52; q*s is exact, one rounding)."""
-    q = codes_from_even_low(packed).numpy().astype(np.float32)
-    s = np.repeat(scale.float().numpy(), group, axis=1)
-    z = np.repeat(mn.float().numpy(), group, axis=1)
-    return torch.from_numpy(_fmaf(q, s, z))
+    q = codes_from_even_low(packed).numpy()
+    return torch.from_numpy(_grouped_fma(q, scale.float().numpy(), mn.float().numpy(), group))
 
 
 # --------------------------------------------------------------------------

@@ -52,3 +52,19 @@ def wfmt_code(fmt: str) -> int:
 
     return {"bf16": _lib.W_BF16, "int4_tinygemm": _lib.W_INT4_TINYGEMM, "int4_plain": _lib.W_INT4_PLAIN,
             "fp8": _lib.W_FP8_E4M3, "int8": _lib.W_INT8}[fmt]
+
+
+def dequant_qweight(qw) -> torch.Tensor:
+    """The oracle's fp32 (N, K) weight for a breeze_b200 QWeight, whatever its format."""
+    from breeze_b200 import _lib
+
+    w, s = qw.w.cpu(), None if qw.scale is None else qw.scale.cpu()
+    if qw.wfmt == _lib.W_INT4_TINYGEMM:
+        return quant.dequant_int4_tinygemm(w, s, qw.group)
+    if qw.wfmt == _lib.W_INT4_PLAIN:
+        return quant.dequant_int4_plain(w, s[..., 0].t().contiguous(), s[..., 1].t().contiguous(), qw.group)
+    if qw.wfmt == _lib.W_FP8_E4M3:
+        return quant.dequant_fp8(w, s)
+    if qw.wfmt == _lib.W_INT8:
+        return quant.dequant_int8(w, s, dtype=torch.float32)
+    return w.float()

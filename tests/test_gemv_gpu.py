@@ -424,3 +424,32 @@ def test_gemv_host_io_matches_device_call(fmt, m, epi):
     torch.cuda.synchronize()
     assert torch.equal(got, ref)
     assert torch.equal(xd.cpu(), x)
+
+
+@pytest.mark.parametrize("fmt", ["int8", "bf16", "int4_plain"])
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_bias_in_output_dtype_through_raw_abi(fmt, out_dtype):
+    """The descriptor's bias holds [N] values of the output's dtype (the
+    header's contract). Called through ctypes with a descriptor built by hand
+    from the tensors, no Python-side conversion."""
+    import ctypes
+
+    L = _lib()
+    n, k, m = 384, 512, 3
+    case = make_weight(fmt, n, k, seed=31)
+    g = torch.Generator().manual_seed(32)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(DEV)
+    bias = (torch.randn(n, generator=g) * 0.5).to(out_dtype).to(DEV)
+    out = torch.full((m, n), float("nan"), dtype=out_dtype, device=DEV)
+    w = case["w"].to(DEV)
+    scale = None if case["scale"] is None else case["scale"].to(DEV)
+    d = L.make_desc(x, w, wfmt_code(fmt), n, scale=scale, group=case["group"], bias=bias, out=out,
+                    flags=L.default_flags())
+    need = ctypes.c_size_t(0)
+    L.check(L.load().bq_gemv_workspace_bytes(ctypes.byref(d), ctypes.byref(need)), "bq_gemv_workspace_bytes")
+    ws = torch.zeros(max(need.value, 256), dtype=torch.uint8, device=DEV)
+    L.check(L.load().bq_gemv(ctypes.byref(d), ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream),
+            "bq_gemv")
+    torch.cuda.synchronize()
+    ref = gemv.linear_epilogue(x.cpu().float(), case["deq"], bias=bias.cpu().float())
+    assert gemv.max_rel_err(out.cpu().float(), ref) < TOL

@@ -32,6 +32,28 @@ def test_tinygemm_pack_matches_aten(golden, n, k, ik):
     assert torch.equal(quant.tinygemm_unpack(torch.from_numpy(ref)), src)
 
 
+def test_tinygemm_unpack_transpose_equals_index_map():
+    """The fast unpack (an axis permutation) against the explicit index map."""
+    g = torch.Generator().manual_seed(3)
+    for n, k, ik in ((8, 128, 8), (64, 512, 8), (16, 512, 2), (24, 1024, 4)):
+        packed = torch.randint(0, 256, (n, k // 2), generator=g, dtype=torch.int32).to(torch.uint8)
+        w = quant.tinygemm_pack(packed, ik)
+        assert torch.equal(quant.tinygemm_unpack(w), quant.tinygemm_unpack_indexed(w))
+        assert torch.equal(quant.tinygemm_unpack(w), packed)
+
+
+def test_grouped_dequant_is_one_rounding():
+    """fp32 (q - 8) * s + z equals the fma formed in float64 and rounded once."""
+    g = torch.Generator().manual_seed(4)
+    q = torch.randint(0, 16, (64, 512), generator=g, dtype=torch.int32).numpy()
+    s = ((torch.randn(64, 4, generator=g) * 0.02).abs() / 7).to(torch.bfloat16).float().numpy()
+    z = (torch.randn(64, 4, generator=g) * 0.01).to(torch.bfloat16).float().numpy()
+    got = quant._grouped_fma(q - 8, s, z, 128)
+    want = ((q - 8).astype(np.float64) * np.repeat(s, 128, 1).astype(np.float64)
+            + np.repeat(z, 128, 1).astype(np.float64)).astype(np.float32)
+    assert (got.view(np.uint32) == want.view(np.uint32)).all()
+
+
 @pytest.mark.parametrize("n,k,gs", [(256, 512, 128), (128, 1024, 64), (64, 256, 32), (256, 512, 256)])
 def test_int4_linear_quantize_and_forward(golden, n, k, gs):
     d = golden("int4_linear.npz")
