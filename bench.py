@@ -49,6 +49,37 @@ def dist_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
 
 
+class Ranks:
+    """Start / finish lines and the max of per-rank timings across the replica
+    processes (breeze_b200.replicas: a TCP store with deadlines, no collective
+    and no NCCL). A rank that misses a deadline is reported in
+    ``replicas_failed`` and the others carry on."""
+
+    def __init__(self, rank: int, world: int):
+        self.rank, self.world, self.n, self.grp = rank, world, 0, None
+        if world > 1:
+            from breeze_b200.replicas import ReplicaGroup
+
+            self.grp = ReplicaGroup(rank, world, os.environ.get("MASTER_ADDR", "127.0.0.1"), timeout_s=300.0)
+
+    def meet(self) -> None:
+        if self.grp is not None:
+            self.n += 1
+            self.grp.meet(f"meet{self.n}")
+
+    def max(self, value: float) -> float:
+        """Max over the ranks that arrived (rank 0); a rank's own value elsewhere."""
+        if self.grp is None:
+            return value
+        self.n += 1
+        got = self.grp.gather(f"max{self.n}", value)
+        return value if got is None else max(got.values())
+
+    @property
+    def failed(self) -> list[int]:
+        return sorted(self.grp.failed) if self.grp is not None else []
+
+
 def measured_peak():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -124,12 +155,7 @@ def run_ours(args, rank, local_rank, world):
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    if world > 1:
-        import torch.distributed as dist
-
-        from datetime import timedelta
-
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    ranks = Ranks(rank, world)
     fw, x, gamma = make_inputs(device, seed=1234 + rank)
     l2 = torch.cuda.get_device_properties(device).L2_cache_size
     R = max(8, -(-4 * l2 // fw.w.numel()))  # copies totalling >= 4x L2
@@ -148,11 +174,7 @@ def run_ours(args, rank, local_rank, world):
     torch.cuda.current_stream(device).wait_stream(stream)
     torch.cuda.synchronize(device)
 
-    def barrier():
-        if world > 1:
-            import torch.distributed as dist
-
-            dist.barrier(device_ids=[local_rank])
+    barrier = ranks.meet
 
     for _ in range(args.warmup):
         graph.replay()
@@ -171,13 +193,7 @@ def run_ours(args, rank, local_rank, world):
     torch.cuda.synchronize(device)
     barrier()
     clock = clocks.stop()
-    ms = e0.elapsed_time(e1)
-    t = torch.tensor([ms], device=device, dtype=torch.float64)
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max = ranks.max(e0.elapsed_time(e1))
 
     # ---- end to end through the public API: per call, the host x is copied in, the
     # GEMV runs and the output is copied back to host memory (rms_gemv_host_io: the
@@ -200,22 +216,17 @@ def run_ours(args, rank, local_rank, world):
         e2e_step()
     h1.record(cur)
     torch.cuda.synchronize(device)
-    e2e_ms = h0.elapsed_time(h1)
-    te = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        dist.barrier(device_ids=[local_rank])
-    e2e_ms = float(te.item())
+    e2e_ms = ranks.max(h0.elapsed_time(h1))
+    barrier()
     status = _lib.device_status(local_rank)
 
     if rank == 0:
         peak, peak_kind = measured_peak()
         per_launch_s = ms_max / 1e3 / (args.steps * R)
         achieved = ALGO_BYTES / per_launch_s / 1e9
-        value = world * ALGO_BYTES * R * args.steps / (ms_max / 1e3) / 1e9
-        e2e_val = world * ALGO_BYTES * R * e2e_steps / (e2e_ms / 1e3) / 1e9
+        alive = world - len(ranks.failed)  # replicas that reached every meeting
+        value = alive * ALGO_BYTES * R * args.steps / (ms_max / 1e3) / 1e9
+        e2e_val = alive * ALGO_BYTES * R * e2e_steps / (e2e_ms / 1e3) / 1e9
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
@@ -237,19 +248,17 @@ def run_ours(args, rank, local_rank, world):
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
-    decode = None if args.no_decode_step else decode_step_bench(device, world, local_rank)
-    depth = None if args.no_decode_step else depth_frame_bench(device, world, local_rank)
+    decode = None if args.no_decode_step else decode_step_bench(device, ranks)
+    depth = None if args.no_decode_step else depth_frame_bench(device, ranks)
     if rank == 0:
         if decode is not None:
             line["decode_step"] = decode
         if depth is not None:
             line["depth_frame"] = depth
+        if world > 1:
+            line["replicas_failed"] = ranks.failed
         print(json.dumps(line), flush=True)
-    if world > 1:
-        import torch.distributed as dist
-
-        del graph
-        dist.destroy_process_group()
+    ranks.meet()  # rank 0 hosts the store: the others finish before it exits
 
 
 DECODE_FORMATS = ("int4", "fp8", "int8")
@@ -258,7 +267,7 @@ DECODE_ROWS_INT4 = (1, 2, 4, 8, 16, 32, 64)  # config 4 adds 32 and 64 concurren
 DECODE_LAYERS = 28
 
 
-def decode_step_bench(device, world: int, local_rank: int, replays: int = 10, warmup: int = 3):
+def decode_step_bench(device, ranks: Ranks, replays: int = 10, warmup: int = 3):
     """Decode-step leg (the 28-layer projection stack + head as one CUDA graph,
     breeze_b200.fused.stack.DecodeStack) for each weight format and row count.
     The stack's weights (1.0 GB int4, 1.9 GB fp8/int8) exceed L2 by far, so
@@ -287,22 +296,15 @@ def decode_step_bench(device, world: int, local_rank: int, replays: int = 10, wa
                 for _ in range(warmup):
                     st.replay()
                 torch.cuda.synchronize(device)
-                if world > 1:
-                    import torch.distributed as dist
-
-                    dist.barrier(device_ids=[local_rank])
+                ranks.meet()
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record(cur)
                 for _ in range(replays):
                     st.replay()
                 e1.record(cur)
                 torch.cuda.synchronize(device)
-                t = torch.tensor([e0.elapsed_time(e1) / replays], device=device, dtype=torch.float64)
-                if world > 1:
-                    import torch.distributed as dist
-
-                    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-                step_us = float(t.item()) * 1e3
+                step_us = ranks.max(e0.elapsed_time(e1) / replays) * 1e3
+                world = ranks.world - len(ranks.failed)
                 wb = st.weight_bytes
                 entry[mode] = {"step_us": round(step_us, 1), "us_per_row": round(step_us / rows, 2),
                                "tokens_per_s_all_gpus": round(world * rows / step_us * 1e6, 1),
@@ -325,7 +327,7 @@ def decode_step_bench(device, world: int, local_rank: int, replays: int = 10, wa
 DEPTH_LAYERS = 12
 
 
-def depth_frame_bench(device, world: int, local_rank: int, replays: int = 10, warmup: int = 3):
+def depth_frame_bench(device, ranks: Ranks, replays: int = 10, warmup: int = 3):
     """Depth-decoder frame leg (breeze_b200.fused.depth.DepthDecoderLoop): one
     CUDA graph of a whole frame (2-position prefill + 14 single steps over 12
     layers, fp32 codebook head and CFG sampling per step) at the depth shapes
@@ -345,22 +347,14 @@ def depth_frame_bench(device, world: int, local_rank: int, replays: int = 10, wa
         for _ in range(warmup):
             loop.replay()
         torch.cuda.synchronize(device)
-        if world > 1:
-            import torch.distributed as dist
-
-            dist.barrier(device_ids=[local_rank])
+        ranks.meet()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(cur)
         for _ in range(replays):
             loop.replay()
         e1.record(cur)
         torch.cuda.synchronize(device)
-        t = torch.tensor([e0.elapsed_time(e1) / replays], device=device, dtype=torch.float64)
-        if world > 1:
-            import torch.distributed as dist
-
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        us = float(t.item()) * 1e3
+        us = ranks.max(e0.elapsed_time(e1) / replays) * 1e3
         out.append({"batch": batch, "frame_us": round(us, 1), "us_per_codebook_step": round(us / loop.n_dec, 1),
                     "launches": loop.launches, "weight_GBps": round(loop.weight_bytes_per_frame / us / 1e3, 1),
                     "tokens_valid": bool(((loop.output_tokens >= 0) & (loop.output_tokens < 2048)).all().item())})
@@ -513,7 +507,7 @@ def main():
     if args.depth_only:
         device = torch.device("cuda", local_rank)
         torch.cuda.set_device(device)
-        print(json.dumps({"depth_frame": depth_frame_bench(device, 1, local_rank)}), flush=True)
+        print(json.dumps({"depth_frame": depth_frame_bench(device, Ranks(0, 1))}), flush=True)
         return
     run_ours(args, rank, local_rank, world)
 
