@@ -103,6 +103,12 @@ class SampleDesc(ctypes.Structure):
     ]
 
 
+class ChainOptions(ctypes.Structure):
+    """bq_chain_options (include/breeze_b200.h)."""
+
+    _fields_ = [("wait_cycles", ctypes.c_uint64), ("start_flag", ctypes.c_void_p), ("start_target", ctypes.c_uint32)]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -118,6 +124,8 @@ _SIGS = {
                                                        ctypes.POINTER(ctypes.c_size_t)]),
     "bq_gemv_chain_prepare": (ctypes.c_int32, [ctypes.POINTER(GemvDesc), ctypes.c_int32, ctypes.c_void_p,
                                                ctypes.c_size_t]),
+    "bq_gemv_chain_prepare_ex": (ctypes.c_int32, [ctypes.POINTER(GemvDesc), ctypes.c_int32,
+                                                  ctypes.POINTER(ChainOptions), ctypes.c_void_p, ctypes.c_size_t]),
     "bq_gemv_chain_launch": (ctypes.c_int32, [ctypes.POINTER(GemvDesc), ctypes.c_int32, ctypes.c_void_p,
                                               ctypes.c_size_t, ctypes.c_void_p]),
     "bq_attention_workspace_bytes": (ctypes.c_int32, [ctypes.POINTER(AttnDesc), ctypes.POINTER(ctypes.c_size_t)]),
@@ -393,22 +401,34 @@ def gemv_desc(x: torch.Tensor, w: torch.Tensor, wfmt: int, n: int, *, out: torch
 
 
 class GemvChain:
-    """A list of GEMVs run as one cooperative launch (bq_gemv_chain_*).
+    """A list of GEMVs run as one persistent launch (bq_gemv_chain_*).
 
     The descriptors' tensors must stay alive and in place; ``launch()`` is
     capture-safe once the chain is built (``prepare`` runs here, outside any
-    capture).
+    capture). ``wait_cycles`` bounds every device-side wait (0: the library's
+    default, ~2 s); ``start_flag`` (an int32 device tensor written by the host
+    or by earlier work, never by a kernel running at the same time) makes the
+    first GEMV also wait until it reaches ``start_target``. ``prepare()``
+    rewrites the workspace: call it again after a launch that set a device
+    error bit.
     """
 
-    def __init__(self, descs: list[GemvDesc], device: torch.device):
+    def __init__(self, descs: list[GemvDesc], device: torch.device, wait_cycles: int = 0,
+                 start_flag: torch.Tensor | None = None, start_target: int = 0):
         lib = load()
         self.n = len(descs)
         self._arr = (GemvDesc * self.n)(*descs)
         need = ctypes.c_size_t(0)
         check(lib.bq_gemv_chain_workspace_bytes(self._arr, self.n, ctypes.byref(need)), "bq_gemv_chain_workspace_bytes")
         self.ws = torch.zeros(max(int(need.value), 256), dtype=torch.uint8, device=device)
-        check(lib.bq_gemv_chain_prepare(self._arr, self.n, self.ws.data_ptr(), self.ws.numel()), "bq_gemv_chain_prepare")
+        self._opts = ChainOptions(wait_cycles, _ptr(start_flag), start_target)
+        self._flag = start_flag
         self.device = device
+        self.prepare()
+
+    def prepare(self) -> None:
+        check(load().bq_gemv_chain_prepare_ex(self._arr, self.n, ctypes.byref(self._opts), self.ws.data_ptr(),
+                                              self.ws.numel()), "bq_gemv_chain_prepare_ex")
 
     def launch(self) -> None:
         check(load().bq_gemv_chain_launch(self._arr, self.n, self.ws.data_ptr(), self.ws.numel(), _stream(self.device)),

@@ -1,18 +1,20 @@
-// Host side of the decode chain: one cooperative launch running a list of
-// GEMVs (bq_gemv_chain_*). The op table, the grid-barrier words and the
-// split-K scratch live in the caller's workspace:
-//   [0, 256)                  barrier {count, generation}
-//   [256, 256 + n * op size)  op table (Gemv3Params, written by prepare)
-//   then, 256-aligned          split-K counters and partial sums
+// Host side of the decode chain (bq_gemv_chain_*): planning, the op table and
+// the launch of the persistent kernel in bq_chain.cuh.
+//
+// Workspace layout (caller-provided, 256-byte aligned, sized by
+// bq_gemv_chain_workspace_bytes):
+//   [0, 256)                   ChainHeader: epoch, wait limit, start flag, finish count
+//   [256, 256 + 128 n)         per-op completion counters, one 128-byte line each
+//   then (256-aligned)         op table: n ChainOp
+//   then (256-aligned, each)   tile-major copies of the int4 ops' scale/zero pairs,
+//                              [N/16][K/g][16][2] bf16, written by prepare
 #include <cuda_runtime.h>
 
 #include <algorithm>
-#include <cstdlib>
 #include <cstring>
 #include <vector>
 
-#include "bq_gemv3.cuh"
-#include "bq_gemv3_kinst.h"
+#include "bq_chain.cuh"
 #include "bq_host.h"
 
 namespace bq {
@@ -20,33 +22,40 @@ namespace bq {
 int validate_gemv(const bq_gemv_desc* d);
 
 namespace {
-constexpr int64_t kBarrierBytes = 256;
 inline int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
 inline uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
+bool is_int4(int fmt) { return fmt == BQ_W_INT4_TINYGEMM || fmt == BQ_W_INT4_PLAIN; }
+int row_kb_bytes(int fmt) { return fmt == BQ_W_BF16 ? 256 : (fmt == BQ_W_FP8_E4M3 || fmt == BQ_W_INT8) ? 128 : 64; }
 
-struct ChainPlan {
-    int n, mt, gpk, fmt, grid;
-    uint32_t smem;
-    int64_t table_off, split_off, ws_bytes;
-    std::vector<Gemv3Plan> ops;
+struct ChainPlanH {
+    int n = 0, M = 0, mt = 1, grid = 0, R = 0;
+    uint32_t slot = 0, smem = 0, smem_x = 0, smem_xsum = 0, smem_part = 0, smem_misc = 0, smem_bar = 0;
+    uint32_t xw_bytes = 0, xw_pitch = 0, xsum_w_bytes = 0, part_bytes = 0;
+    int64_t off_counters = 256, off_table = 0, ws_bytes = 0;
+    std::vector<ChainOp> ops;
+    std::vector<int64_t> scale_off;  // workspace offset of each int4 op's tile-major scales (-1: none)
 };
 
-const void* chain_kernel(int fmt, int mt, int gpk) {
-    if (fmt == BQ_W_INT4_TINYGEMM || fmt == BQ_W_INT4_PLAIN) return gemv_chain_kernel_int4(fmt, mt, gpk);
-    if (fmt == BQ_W_BF16) return gemv_chain_kernel_bf16(mt);
-    return gemv_chain_kernel_f8(fmt, mt);
+// Scale bytes of one 16-row piece for a chunk of kbc k-blocks.
+uint32_t piece_scale_bytes(const bq_gemv_desc* d, int kbc) {
+    if (is_int4(d->wfmt)) return uint32_t(kbc * kKB / d->group) * 64u;
+    if (d->wfmt == BQ_W_FP8_E4M3 || d->wfmt == BQ_W_INT8) return 64u;
+    return 0u;
 }
 
-int plan_chain(const bq_gemv_desc* descs, int n, ChainPlan* cp) {
+int plan_chain(const bq_gemv_desc* descs, int n, ChainPlanH* cp) {
     if (!descs || n < 1) return set_error(BQ_ERR_INVALID_ARG, "chain needs at least one GEMV");
     const DeviceInfo* dev = device_info();
     if (!dev) return BQ_ERR_CUDA;
     if (dev->major != 10) return set_error(BQ_ERR_DEVICE, "sm_%d%d device: this library is built for sm_100a", dev->major, dev->minor);
     cp->n = n;
-    cp->fmt = descs[0].wfmt;
-    cp->gpk = gemv3_gpk(&descs[0]);
-    const int M = descs[0].M;
-    cp->mt = M > 8 ? 2 : 1;
+    cp->M = descs[0].M;
+    cp->mt = cp->M > 8 ? 2 : 1;
+    cp->grid = dev->sm_count;
+    if (cp->M > 16) return set_error(BQ_ERR_SHAPE, "the decode chain takes at most 16 rows (got %d)", cp->M);
+    auto fail = [&](int i, int code, const char* what) {
+        return set_error(code, "chain op %d: %s", i, what);
+    };
     for (int i = 0; i < n; ++i) {
         const bq_gemv_desc* d = &descs[i];
         int rc = validate_gemv(d);
@@ -56,93 +65,158 @@ int plan_chain(const bq_gemv_desc* descs, int n, ChainPlan* cp) {
             msg[sizeof(msg) - 1] = 0;
             return set_error(rc, "chain op %d: %s", i, msg);
         }
-        if (d->gamma && (reinterpret_cast<uintptr_t>(d->gamma) & 15))
-            return set_error(BQ_ERR_ALIGN, "chain op %d: gamma must be 16-byte aligned", i);
-        if (d->wfmt != cp->fmt || gemv3_gpk(d) != cp->gpk || d->M != M)
-            return set_error(BQ_ERR_SHAPE, "chain op %d: every GEMV of a chain needs the same format, group and M", i);
+        if (d->M != cp->M) return fail(i, BQ_ERR_SHAPE, "every GEMV of a chain has the same M");
+        const int n_tile_rows = d->epilogue == BQ_EPI_SILU_MUL ? d->N / 2 : d->N;
+        if (n_tile_rows % 16) return fail(i, BQ_ERR_SHAPE, "N (N / 2 with SiLU*up) must be a multiple of 16");
+        if (d->x_dtype != BQ_DT_BF16 || (reinterpret_cast<uintptr_t>(d->x) & 15) || (d->ldx % 8))
+            return fail(i, BQ_ERR_ALIGN, "x must be bf16 with 16-byte aligned rows");
+        if (d->gamma && (reinterpret_cast<uintptr_t>(d->gamma) & 15)) return fail(i, BQ_ERR_ALIGN, "gamma must be 16-byte aligned");
+        if (d->epilogue == BQ_EPI_ADD_RESIDUAL &&
+            (d->res_dtype != BQ_DT_BF16 || (reinterpret_cast<uintptr_t>(d->residual) & 15) || (d->ldr % 8)))
+            return fail(i, BQ_ERR_ALIGN, "the residual must be bf16 with 16-byte aligned rows");
+        if ((d->wfmt == BQ_W_FP8_E4M3 || d->wfmt == BQ_W_INT8) && (reinterpret_cast<uintptr_t>(d->scale) & 15))
+            return fail(i, BQ_ERR_ALIGN, "the row scales must be 16-byte aligned");
+        const int tiles = n_tile_rows / 16;
+        if ((tiles + cp->grid - 1) / cp->grid > kChainMaxTiles)
+            return fail(i, BQ_ERR_SHAPE, "too many output rows for one chain op");
     }
-    // Two CTAs per SM when the shared layout allows a double-buffered ring,
-    // else one; a single-buffered ring only as the last resort.
-    const int tb = gemv3_tile_bytes(cp->fmt, cp->gpk);
-    // BQ_CHAIN_CTAS_PER_SM=1 pins one CTA per SM (for comparisons)
-    const char* env = std::getenv("BQ_CHAIN_CTAS_PER_SM");
-    const int first = (env && std::atoi(env) == 1) ? 1 : 0;
-    for (int attempt = first; attempt < 3; ++attempt) {
-        const int per_sm = attempt == 0 ? 2 : 1;
-        const int min_rs = attempt < 2 ? 2 : 1;
-        const int slots = per_sm * dev->sm_count;
-        // per-CTA dynamic shared memory: 228 KB per SM, 1 KB reserved per CTA,
-        // 1 KB kept for the kernel's static op slots
-        const uint32_t budget =
-            std::min<uint32_t>(uint32_t(dev->smem_optin) - 1024u, (233472u - 1024u * per_sm) / per_sm - 1024u);
-        cp->grid = slots;
-        cp->ops.assign(n, Gemv3Plan());
-        uint32_t x_max = 0, g_max = 0, part_max = 0, xs_max = 0;
-        int64_t split_need = 0;
+    // chunking and shared-memory layout for a chunk-size cap; more ring slots win
+    for (const uint32_t cap : {34u * 1024u, 17u * 1024u}) {
+        ChainPlanH P = *cp;
+        P.ops.assign(n, ChainOp());
+        uint32_t slot = 0;
+        int nkw_max = 0, gpk_max = 1;
         bool ok = true;
         for (int i = 0; i < n && ok; ++i) {
             const bq_gemv_desc* d = &descs[i];
-            if (plan_gemv3(d, M, &cp->ops[i], slots) != BQ_OK) {
+            const int KB = d->K / kKB, rkb = row_kb_bytes(d->wfmt);
+            const int pieces = d->epilogue == BQ_EPI_SILU_MUL ? 2 : 1;
+            int kbc = 0;
+            for (int nch = 1; nch <= KB; ++nch) {
+                if (KB % nch) continue;
+                const int c = KB / nch;
+                if (is_int4(d->wfmt) && (c * kKB) % d->group) continue;  // whole groups per chunk
+                const uint32_t bytes = uint32_t(pieces) * (uint32_t(c) * 16u * uint32_t(rkb) + piece_scale_bytes(d, c));
+                if (bytes <= cap) {
+                    kbc = c;
+                    break;
+                }
+            }
+            if (!kbc) {
                 ok = false;
                 break;
             }
-            const Gemv3Plan& pl = cp->ops[i];
-            x_max = std::max<uint32_t>(x_max, uint32_t(8 * (M * pl.xrow_pitch + 256)));
-            if (d->gamma) g_max = std::max<uint32_t>(g_max, uint32_t(8 * pl.nkbw * 256));
-            if (cp->fmt == BQ_W_INT4_TINYGEMM || cp->fmt == BQ_W_INT4_PLAIN)
-                xs_max = std::max<uint32_t>(xs_max, uint32_t(8 * pl.nkbw * pl.gpk * pl.mt * 64));
-            const int nq = M >= 7 ? 4 : (M + 1) / 2;
-            part_max = std::max<uint32_t>(part_max, uint32_t(pl.upc * 8 * pl.tpu * pl.mt * 128 * nq));
-            split_need = std::max(split_need, pl.ws_bytes);
+            ChainOp& o = P.ops[i];
+            std::memset(&o, 0, sizeof(o));
+            o.fmt = d->wfmt;
+            o.M = d->M;
+            o.N = d->N;
+            o.K = d->K;
+            o.KB = KB;
+            o.group = d->group;
+            o.gpk = (d->wfmt == BQ_W_INT4_TINYGEMM && d->group < 128) ? 128 / d->group : 1;
+            o.epi = d->epilogue;
+            o.norm = d->gamma ? 1 : 0;
+            o.x_dtype = d->x_dtype;
+            o.out_dtype = d->out_dtype;
+            o.res_dtype = d->res_dtype;
+            o.flags = d->flags;
+            o.eps = d->eps;
+            o.n_half = d->N / 2;
+            o.pieces = pieces;
+            o.tiles = (pieces == 2 ? d->N / 2 : d->N) / 16;
+            o.kbc = kbc;
+            o.nchunk = KB / kbc;
+            o.wpiece = uint32_t(kbc) * 16u * uint32_t(rkb);
+            o.piece_bytes = o.wpiece + piece_scale_bytes(d, kbc);
+            o.chunk_bytes = uint32_t(pieces) * o.piece_bytes;
+            o.row_copies = d->wfmt == BQ_W_INT4_TINYGEMM ? 2 : (o.nchunk == 1 ? 1 : 16);
+            o.x = d->x;
+            o.ldx = d->ldx;
+            o.w = d->w;
+            o.scale = d->scale;
+            o.gamma = d->gamma;
+            o.bias = d->bias;
+            o.residual = d->residual;
+            o.ldr = d->ldr;
+            o.out = d->out;
+            o.ldo = d->ldo;
+            slot = std::max(slot, o.chunk_bytes);
+            if (o.norm) slot = std::max(slot, uint32_t(d->K) * 2u);
+            nkw_max = std::max(nkw_max, o.nchunk * ((kbc + 7) / 8));
+            gpk_max = std::max(gpk_max, o.gpk);
         }
         if (!ok) continue;
-        // shared layout for every op: ring | x | gamma | partials | misc
-        int upc_max = 1;
-        for (int i = 0; i < n; ++i) upc_max = std::max(upc_max, cp->ops[i].upc);
-        const uint32_t misc = misc3_bytes(upc_max, M);
-        const uint32_t fixed = align_up(x_max, 16) + align_up(xs_max, 16) + align_up(g_max, 16) + align_up(part_max, 16) + misc;
-        if (fixed >= budget) continue;
-        const uint32_t ring_w = ((budget - fixed) / 8) / 128 * 128;  // ring bytes per warp
-        const uint32_t smem_x = 8 * ring_w;
-        const uint32_t smem_xsum = align_up(smem_x + x_max, 16);
-        const uint32_t smem_gamma = align_up(smem_xsum + xs_max, 16);
-        const uint32_t smem_part = align_up(smem_gamma + g_max, 16);
-        const uint32_t smem_misc = align_up(smem_part + part_max, 16);
-        for (int i = 0; i < n && ok; ++i) {
-            Gemv3Plan& pl = cp->ops[i];
-            const int ugm = 1;  // kernel ug_max()
-            const int kps = pl.mt == 1 ? 2 : 1;
-            const int nkp = (pl.nkbw + kps - 1) / kps;
-            int ug = std::min(ugm, pl.upc), rs = 0;
-            for (; ug >= 1; --ug) {
-                const int slot = kps * ug * pl.tpu * tb;
-                const int max_seq = std::min(kMaxRing, ((pl.upc + ug - 1) / ug) * nkp);
-                rs = std::min<int>(max_seq, int(ring_w / uint32_t(slot)));
-                if (rs >= std::min(min_rs, max_seq)) break;
-            }
-            if (ug < 1 || rs < 1) {
-                ok = false;
-                break;
-            }
-            pl.ug = ug;
-            pl.slot_bytes = kps * ug * pl.tpu * tb;
-            pl.ring_slots = rs;
-            pl.smem_ring = 0;
-            pl.smem_x = smem_x;
-            pl.smem_xsum = smem_xsum;
-            pl.smem_gamma = smem_gamma;
-            pl.smem_part = smem_part;
-            pl.smem_misc = smem_misc;
+        slot = align_up(slot, 128);
+        // tile rotation: op i's tiles start where op i-1's ended, spreading every CTA's weight bytes evenly
+        int64_t base = 0;
+        for (int i = 0; i < n; ++i) {
+            P.ops[i].base = int(base % P.grid);
+            base += P.ops[i].tiles;
         }
-        if (!ok) continue;
-        cp->smem = smem_misc + misc;
-        for (int i = 0; i < n; ++i) cp->ops[i].smem_total = cp->smem;
-        cp->table_off = kBarrierBytes;
-        cp->split_off = align256(kBarrierBytes + int64_t(n) * int64_t(sizeof(Gemv3Params)));
-        cp->ws_bytes = cp->split_off + split_need;
-        return BQ_OK;
+        const int M = P.M, MT = P.mt;
+        P.xw_pitch = uint32_t(nkw_max) * 256u + 16u;
+        P.xw_bytes = align_up(uint32_t(M) * P.xw_pitch + 256u, 16);
+        bool any_int4 = false;
+        for (int i = 0; i < n; ++i) any_int4 |= is_int4(descs[i].wfmt);
+        P.xsum_w_bytes = any_int4 ? uint32_t(nkw_max * gpk_max * MT) * 64u : 0u;
+        const int nq = M >= 7 ? 4 : (M + 1) / 2;
+        P.part_bytes = uint32_t(8 * 2 * MT * 8 * nq) * 16u;
+        const uint32_t fixed = 8 * P.xw_bytes + 8 * P.xsum_w_bytes + 2 * P.part_bytes + chain_misc_bytes(M);
+        // the kernel's static shared memory (abort flag, epoch) and 1 KB per-CTA reserve fit in the opt-in limit
+        const uint32_t budget = uint32_t(dev->smem_optin) - 256u;
+        if (fixed + 2 * (slot + 16) > budget) continue;
+        P.R = int(std::min<uint32_t>((budget - fixed) / (slot + 16), 64u));
+        P.slot = slot;
+        uint32_t o = 0;
+        o += uint32_t(P.R) * slot;
+        P.smem_x = o;
+        o += 8 * P.xw_bytes;
+        P.smem_xsum = o;
+        o += 8 * P.xsum_w_bytes;
+        P.smem_part = o;
+        o += 2 * P.part_bytes;
+        P.smem_misc = o;
+        o += chain_misc_bytes(M);
+        o = align_up(o, 16);
+        P.smem_bar = o;
+        o += 16u * uint32_t(P.R);
+        P.smem = o;
+        if (P.R < 3 && cap != 17u * 1024u) {
+            *cp = P;  // keep as a fallback, try smaller chunks
+            continue;
+        }
+        *cp = P;
+        break;
     }
-    return set_error(BQ_ERR_SHAPE, "chain of %d GEMVs with M=%d does not fit in shared memory", n, M);
+    if (cp->R < 2) return set_error(BQ_ERR_SHAPE, "a chain of %d GEMVs with M=%d does not fit in shared memory", n, cp->M);
+    // workspace: header, counters, op table, int4 scale copies
+    cp->off_counters = 256;
+    cp->off_table = align256(cp->off_counters + int64_t(n) * kCounterStride * 4);
+    int64_t off = align256(cp->off_table + int64_t(n) * int64_t(sizeof(ChainOp)));
+    cp->scale_off.assign(n, -1);
+    for (int i = 0; i < n; ++i) {
+        const bq_gemv_desc* d = &descs[i];
+        if (!is_int4(d->wfmt)) continue;
+        cp->scale_off[i] = off;
+        off = align256(off + int64_t(d->N) * (d->K / d->group) * 4);
+    }
+    cp->ws_bytes = off;
+    return BQ_OK;
+}
+
+// scales_zeros [K/g, N, 2] bf16 -> tile-major [N/16][K/g][16][2]: one 32-bit pair per thread.
+__global__ void scales_tile_major_kernel(const uint32_t* __restrict__ src, uint32_t* __restrict__ dst, int n, int groups) {
+    const int64_t total = int64_t(n) * groups;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t g = i / n, row = i - g * n;  // source order: coalesced reads
+        dst[((row / 16) * groups + g) * 16 + (row & 15)] = src[i];
+    }
+}
+
+const void* chain_kernel(int mt) {
+    return mt == 1 ? reinterpret_cast<const void*>(&gemv_chain_kernel<1>)
+                   : reinterpret_cast<const void*>(&gemv_chain_kernel<2>);
 }
 }  // namespace
 
@@ -154,15 +228,16 @@ extern "C" {
 
 int32_t bq_gemv_chain_workspace_bytes(const bq_gemv_desc* descs, int32_t n, size_t* bytes) {
     if (!bytes) return set_error(BQ_ERR_INVALID_ARG, "bytes is NULL");
-    ChainPlan cp;
+    ChainPlanH cp;
     int rc = plan_chain(descs, n, &cp);
     if (rc) return rc;
     *bytes = size_t(cp.ws_bytes);
     return BQ_OK;
 }
 
-int32_t bq_gemv_chain_prepare(const bq_gemv_desc* descs, int32_t n, void* workspace, size_t workspace_bytes) {
-    ChainPlan cp;
+int32_t bq_gemv_chain_prepare_ex(const bq_gemv_desc* descs, int32_t n, const bq_chain_options* opts, void* workspace,
+                                 size_t workspace_bytes) {
+    ChainPlanH cp;
     int rc = plan_chain(descs, n, &cp);
     if (rc) return rc;
     if (!workspace || int64_t(workspace_bytes) < cp.ws_bytes)
@@ -170,42 +245,79 @@ int32_t bq_gemv_chain_prepare(const bq_gemv_desc* descs, int32_t n, void* worksp
                          (long long)cp.ws_bytes);
     if (reinterpret_cast<uintptr_t>(workspace) & 255) return set_error(BQ_ERR_ALIGN, "workspace must be 256-byte aligned");
     char* ws = static_cast<char*>(workspace);
-    std::vector<Gemv3Params> table(n);
-    for (int i = 0; i < n; ++i) fill_gemv3_params(&descs[i], cp.ops[i], 0, ws + cp.split_off, &table[i]);
-    cudaError_t e = cudaMemset(ws, 0, size_t(cp.table_off));
-    if (e == cudaSuccess) e = cudaMemset(ws + cp.split_off, 0, size_t(cp.ws_bytes - cp.split_off));
-    if (e == cudaSuccess) e = cudaMemcpy(ws + cp.table_off, table.data(), sizeof(Gemv3Params) * size_t(n), cudaMemcpyHostToDevice);
+    ChainHeader h;
+    std::memset(&h, 0, sizeof(h));
+    if (opts) {
+        h.wait_cycles = (long long)opts->wait_cycles;
+        h.start_flag = opts->start_flag;
+        h.start_target = opts->start_target;
+    }
+    std::vector<ChainOp> table = cp.ops;
+    cudaError_t e = cudaSuccess;
+    for (int i = 0; i < n && e == cudaSuccess; ++i) {
+        if (cp.scale_off[i] < 0) continue;
+        const bq_gemv_desc* d = &descs[i];
+        uint32_t* dst = reinterpret_cast<uint32_t*>(ws + cp.scale_off[i]);
+        const int groups = d->K / d->group;
+        const int64_t total = int64_t(d->N) * groups;
+        const int blocks = int(std::min<int64_t>((total + 255) / 256, 4096));
+        scales_tile_major_kernel<<<blocks, 256>>>(static_cast<const uint32_t*>(d->scale), dst, d->N, groups);
+        e = cudaGetLastError();
+        table[i].scale = dst;
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(ws, &h, sizeof(h), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemset(ws + cp.off_counters, 0, size_t(cp.off_table - cp.off_counters));
+    if (e == cudaSuccess)
+        e = cudaMemcpy(ws + cp.off_table, table.data(), sizeof(ChainOp) * size_t(n), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return set_error(BQ_ERR_CUDA, "chain prepare: %s", cudaGetErrorString(e));
     return BQ_OK;
 }
 
+int32_t bq_gemv_chain_prepare(const bq_gemv_desc* descs, int32_t n, void* workspace, size_t workspace_bytes) {
+    return bq_gemv_chain_prepare_ex(descs, n, nullptr, workspace, workspace_bytes);
+}
+
 int32_t bq_gemv_chain_launch(const bq_gemv_desc* descs, int32_t n, void* workspace, size_t workspace_bytes,
                              void* stream) {
-    ChainPlan cp;
+    ChainPlanH cp;
     int rc = plan_chain(descs, n, &cp);
     if (rc) return rc;
     if (!workspace || int64_t(workspace_bytes) < cp.ws_bytes)
         return set_error(BQ_ERR_WORKSPACE, "chain workspace of %zu bytes given, %lld needed", workspace_bytes,
                          (long long)cp.ws_bytes);
-    const void* fn = chain_kernel(cp.fmt, cp.mt, cp.gpk);
-    if (!fn) return set_error(BQ_ERR_FORMAT, "no chain kernel for format %d", cp.fmt);
+    if (reinterpret_cast<uintptr_t>(workspace) & 255) return set_error(BQ_ERR_ALIGN, "workspace must be 256-byte aligned");
+    const void* fn = chain_kernel(cp.mt);
     rc = ensure_smem_attr(fn, cp.smem);
     if (rc) return rc;
     int per_sm = 0;
-    const DeviceInfo* dev = device_info();
-    const int want = cp.grid / dev->sm_count;
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads3, cp.smem);
-    if (e != cudaSuccess || per_sm < want)
-        return set_error(BQ_ERR_CUDA, "chain kernel cannot keep %d CTAs per SM (%d, %s)", want, per_sm, cudaGetErrorString(e));
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kChainThreads, cp.smem);
+    if (e != cudaSuccess || per_sm < 1)
+        return set_error(BQ_ERR_CUDA, "chain kernel does not fit one CTA per SM (%u bytes of shared memory): %s",
+                         cp.smem, cudaGetErrorString(e));
     char* ws = static_cast<char*>(workspace);
-    const Gemv3Params* ops = reinterpret_cast<const Gemv3Params*>(ws + cp.table_off);
-    int n_ops = n;
-    unsigned int* bar = reinterpret_cast<unsigned int*>(ws);
-    void* args[] = {&ops, &n_ops, &bar};
+    ChainArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.ops = reinterpret_cast<const ChainOp*>(ws + cp.off_table);
+    a.n_ops = n;
+    a.ring_slots = cp.R;
+    a.slot_bytes = cp.slot;
+    a.smem_x = cp.smem_x;
+    a.smem_xsum = cp.smem_xsum;
+    a.smem_part = cp.smem_part;
+    a.smem_misc = cp.smem_misc;
+    a.smem_bar = cp.smem_bar;
+    a.xw_bytes = cp.xw_bytes;
+    a.xw_pitch = cp.xw_pitch;
+    a.xsum_w_bytes = cp.xsum_w_bytes;
+    a.part_bytes = cp.part_bytes;
+    a.counters = reinterpret_cast<unsigned int*>(ws + cp.off_counters);
+    a.hdr = reinterpret_cast<ChainHeader*>(ws);
+    void* args[] = {&a};
     cudaLaunchConfig_t cfg;
     std::memset(&cfg, 0, sizeof(cfg));
     cfg.gridDim = dim3(cp.grid);
-    cfg.blockDim = dim3(kThreads3);
+    cfg.blockDim = dim3(kChainThreads);
     cfg.dynamicSmemBytes = cp.smem;
     cfg.stream = static_cast<cudaStream_t>(stream);
     cudaLaunchAttribute attr[2];

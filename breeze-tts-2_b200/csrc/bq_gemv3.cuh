@@ -154,8 +154,7 @@ __device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, 
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(ok ? 16 : 0) : "memory");
 }
 
-// Phases of one CTA's share of a GEMV. A single launch runs them all in order;
-// the decode-chain kernel interleaves the phases of consecutive GEMVs.
+// Phases of one CTA's share of a GEMV (a single launch runs them all in order).
 constexpr int kPhL2 = 1;       // bulk L2 prefetch of the CTA's weight slice
 constexpr int kPhPrefill = 2;  // gamma and the first ring slots (static data only)
 constexpr int kPhPdl = 4;      // programmatic-dependent-launch trigger and wait
@@ -1063,89 +1062,6 @@ __global__ void __launch_bounds__(kThreads3, 2) gemv3_kernel(const Gemv3Params p
     extern __shared__ __align__(1024) uint8_t smem[];
     RingState rst;
     gemv_cta<FMT, MT, TPU, GPK, RECT, EVEN>(p, smem, int(blockIdx.x), kPhAll, rst);
-}
-
-// ---------------------------------------------------------------- decode chain
-// One cooperative launch runs a list of GEMVs (a decode step's projections).
-// Two CTAs per SM, every CTA resident; between GEMVs a grid barrier. While a
-// GEMV runs, the next one's weight slice is pulled into L2, and as soon as
-// its main loop ends the next one's gamma and first ring slots are issued,
-// so the barrier is all that separates two projections.
-
-// Sense-reversing grid barrier on {count, generation}: bounded wait, error
-// word on timeout. The counter returns to zero after every barrier, so the
-// pair needs no reset between launches.
-__device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* p) {
-    unsigned int v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void grid_barrier(unsigned int* bar, unsigned int nblocks) {
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const unsigned int my = ld_acquire_u32(bar + 1);
-        __threadfence();
-        const unsigned int old = atomicAdd(bar, 1u);
-        if (old == nblocks - 1) {
-            atomicExch(bar, 0u);
-            __threadfence();
-            atomicAdd(bar + 1, 1u);
-        } else {
-            const long long t0 = clock64();
-            while (ld_acquire_u32(bar + 1) == my) {
-                if (clock64() - t0 > kWaitCycles) {
-                    atomicOr(&g_device_error, BQ_DEVERR_WAIT_TIMEOUT_BIT);
-                    break;
-                }
-            }
-        }
-        __threadfence();
-    }
-    __syncthreads();
-}
-
-template <int FMT, int MT, int GPK>
-__global__ void __launch_bounds__(kThreads3, 2)
-    gemv_chain_kernel(const Gemv3Params* __restrict__ ops, int n_ops, unsigned int* bar) {
-    extern __shared__ __align__(1024) uint8_t smem[];
-    __shared__ __align__(16) Gemv3Params sp[2];
-    auto load_op = [&](int i) {
-        const uint32_t* src = reinterpret_cast<const uint32_t*>(ops + i);
-        uint32_t* dst = reinterpret_cast<uint32_t*>(&sp[i & 1]);
-        for (int t = threadIdx.x; t < int(sizeof(Gemv3Params) / 4); t += blockDim.x) dst[t] = __ldg(src + t);
-        __syncthreads();
-    };
-    RingState rs[2];
-    load_op(0);
-    // Step sequence (one call site per tile count keeps the code compact):
-    //   0: L2 + prefill of op 0, then the dependent-launch wait
-    //   per op i: L2 of op i+1, run op i, prefill op i+1, epilogue op i, grid barrier
-    for (int s = 0; s < 4 * n_ops + 1; ++s) {
-        int op, ph;
-        if (s == 0) {
-            op = 0;
-            ph = kPhL2 | kPhPrefill | kPhRing;
-        } else {
-            const int i = (s - 1) >> 2, k = (s - 1) & 3;
-            op = (k == 0 || k == 2) ? i + 1 : i;
-            ph = k == 0 ? kPhL2 : k == 1 ? (kPhStatic | kPhRun) : k == 2 ? (kPhPrefill | kPhRing) : kPhEpi;
-            if (op >= n_ops) continue;
-            if (k == 0) load_op(op);
-        }
-        const Gemv3Params& p = sp[op & 1];
-        if (int(blockIdx.x) < p.grid) {
-            if (p.tpu == 1)
-                gemv_cta<FMT, MT, 1, GPK>(p, smem, int(blockIdx.x), ph, rs[op & 1]);
-            else
-                gemv_cta<FMT, MT, 2, GPK>(p, smem, int(blockIdx.x), ph, rs[op & 1]);
-        }
-        if (s == 0) {
-            pdl_launch_dependents();
-            pdl_wait();  // the first GEMV's inputs may come from a preceding kernel
-        } else if (((s - 1) & 3) == 3 && ((s - 1) >> 2) + 1 < n_ops) {
-            grid_barrier(bar, gridDim.x);
-        }
-    }
 }
 
 // Host: kernel parameters of one launch from a descriptor and its plan.

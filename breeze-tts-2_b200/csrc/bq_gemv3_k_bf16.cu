@@ -3,5 +3,4 @@
 
 namespace bq {
 const void* gemv3_kernel_bf16(int mt, int tpu, bool rect, bool even) { return k3_select<BQ_W_BF16, 1>(mt, tpu, rect, even); }
-const void* gemv_chain_kernel_bf16(int mt) { return kc_select<BQ_W_BF16, 1>(mt); }
 }  // namespace bq

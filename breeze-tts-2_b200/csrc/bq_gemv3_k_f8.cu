@@ -6,7 +6,4 @@ const void* gemv3_kernel_f8(int fmt, int mt, int tpu, bool rect, bool even) {
     if (fmt == BQ_W_FP8_E4M3) return k3_select<BQ_W_FP8_E4M3, 1>(mt, tpu, rect, even);
     return k3_select<BQ_W_INT8, 1>(mt, tpu, rect, even);
 }
-const void* gemv_chain_kernel_f8(int fmt, int mt) {
-    return fmt == BQ_W_FP8_E4M3 ? kc_select<BQ_W_FP8_E4M3, 1>(mt) : kc_select<BQ_W_INT8, 1>(mt);
-}
 }  // namespace bq

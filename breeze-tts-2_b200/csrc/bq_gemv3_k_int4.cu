@@ -9,11 +9,4 @@ const void* gemv3_kernel_int4(int fmt, int mt, int tpu, int gpk, bool rect, bool
     if (gpk == 4) return k3_select<BQ_W_INT4_TINYGEMM, 4>(mt, tpu, rect, even);
     return nullptr;
 }
-const void* gemv_chain_kernel_int4(int fmt, int mt, int gpk) {
-    if (fmt == BQ_W_INT4_PLAIN) return gpk == 1 ? kc_select<BQ_W_INT4_PLAIN, 1>(mt) : nullptr;
-    if (gpk == 1) return kc_select<BQ_W_INT4_TINYGEMM, 1>(mt);
-    if (gpk == 2) return kc_select<BQ_W_INT4_TINYGEMM, 2>(mt);
-    if (gpk == 4) return kc_select<BQ_W_INT4_TINYGEMM, 4>(mt);
-    return nullptr;
-}
 }  // namespace bq

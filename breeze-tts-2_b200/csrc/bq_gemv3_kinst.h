@@ -25,15 +25,6 @@ inline const void* k3_select(int mt, int tpu, bool rect, bool even) {
     return tpu == 1 ? k3<FMT, 2, 1, GPK>() : k3<FMT, 2, 2, GPK>();
 }
 
-template <int FMT, int GPK>
-inline const void* kc_select(int mt) {
-    return mt == 1 ? reinterpret_cast<const void*>(&gemv_chain_kernel<FMT, 1, GPK>)
-                   : reinterpret_cast<const void*>(&gemv_chain_kernel<FMT, 2, GPK>);
-}
-
-const void* gemv_chain_kernel_int4(int fmt, int mt, int gpk);
-const void* gemv_chain_kernel_f8(int fmt, int mt);
-const void* gemv_chain_kernel_bf16(int mt);
 const void* gemv3_kernel_int4(int fmt, int mt, int tpu, int gpk, bool rect, bool even);
 const void* gemv3_kernel_f8(int fmt, int mt, int tpu, bool rect, bool even);
 const void* gemv3_kernel_bf16(int mt, int tpu, bool rect, bool even);

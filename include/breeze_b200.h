@@ -149,20 +149,43 @@ int32_t bq_gemv_host_io(const bq_gemv_desc* desc, const void* x_host, void* out_
 int32_t bq_gemv_noalloc(const bq_gemv_desc* desc, void* stream);
 
 /* ---- decode chain: a list of GEMVs in one launch ------------------------ */
-/* Runs descs[0..n) in order as one cooperative launch (two CTAs per SM, a
- * grid barrier between GEMVs, the next GEMV's weights prefetched while the
- * current one runs). Replaces the per-projection rms_gemv / Int4Linear
- * launches of one decode step (models/fused/layer.py:87-98 over every layer,
- * as captured by cudagraph/backbone_graph.py:254-285); a GEMV may read any
- * earlier GEMV's output. Every GEMV of a chain has the same weight format,
- * group and M, and its M rows must fit one pass (BQ_ERR_SHAPE otherwise).
+/* Runs descs[0..n) in order as ONE persistent cooperative launch, one CTA per
+ * SM: a producer warp per CTA streams the weights of the CTA's share of every
+ * GEMV through a shared-memory ring with bulk copies, running ahead across
+ * GEMV boundaries, while eight consumer warps compute each GEMV as soon as
+ * the previous one is complete (per-GEMV completion counters in the
+ * workspace; no grid barrier). Replaces the per-projection rms_gemv /
+ * Int4Linear launches of one decode step (models/fused/layer.py:87-98 over
+ * every layer, as captured by cudagraph/backbone_graph.py:254-285); GEMV i
+ * may read the output of any earlier GEMV. Every GEMV of a chain has the same
+ * M (<= 16); formats, groups and epilogues may differ. Each needs bf16 x with
+ * 16-byte aligned rows, N (N / 2 with SiLU*up) a multiple of 16, a bf16
+ * residual with 16-byte aligned rows, 16-byte aligned gamma and row scales
+ * (BQ_ERR_SHAPE / BQ_ERR_ALIGN otherwise).
  * The workspace (size from bq_gemv_chain_workspace_bytes, 256-byte aligned)
- * holds the op table and barrier words: bq_gemv_chain_prepare writes it
- * (synchronously, outside stream capture), after which
- * bq_gemv_chain_launch is capture-safe and may be replayed. Re-prepare when
- * any pointer in the descriptors changes. No counterpart in the reference. */
+ * holds the op table, the completion counters and a tile-major copy of every
+ * int4 GEMV's scale/zero pairs: bq_gemv_chain_prepare writes it
+ * (synchronously, outside stream capture), after which bq_gemv_chain_launch
+ * is capture-safe and may be replayed. Re-prepare when any pointer in the
+ * descriptors, or the contents of an int4 scale tensor, change, and after a
+ * launch that set a device error bit (its counters are then inconsistent).
+ * No counterpart in the reference. */
+typedef struct bq_chain_options {
+    uint64_t wait_cycles;        /* bound of every device-side wait in SM clock cycles; 0: ~2 s */
+    const uint32_t* start_flag;  /* NULL, or a word the device can read (device memory or mapped host
+                                  * memory) written by the host or by work finished before the launch
+                                  * -- never by a kernel running at the same time: the first GEMV also
+                                  * waits until *start_flag >= start_target */
+    uint32_t start_target;
+} bq_chain_options;
+
 int32_t bq_gemv_chain_workspace_bytes(const bq_gemv_desc* descs, int32_t n, size_t* bytes);
 int32_t bq_gemv_chain_prepare(const bq_gemv_desc* descs, int32_t n, void* workspace, size_t workspace_bytes);
+/* bq_gemv_chain_prepare with options (NULL: the defaults). A wait that runs
+ * out sets BQ_DEVERR_WAIT_TIMEOUT in bq_device_status; the kernel then stops
+ * at its next wait, lets its copies in flight land, and returns. */
+int32_t bq_gemv_chain_prepare_ex(const bq_gemv_desc* descs, int32_t n, const bq_chain_options* opts, void* workspace,
+                                 size_t workspace_bytes);
 int32_t bq_gemv_chain_launch(const bq_gemv_desc* descs, int32_t n, void* workspace, size_t workspace_bytes,
                              void* stream);
 

@@ -33,7 +33,7 @@ def _replica(rank, world, port, mode, out):
     from breeze_b200.replicas import ReplicaGroup
 
     grp = ReplicaGroup(rank, world, "127.0.0.1", port, timeout_s=3.0, prefix=f"t{port}")
-    started = grp.meet("start")
+    started = grp.meet("start", timeout_s=120.0)  # process start-up (imports) is not what is tested
     time.sleep(0.05)  # the replica's own work
     if rank == 1 and mode == "exit":
         os._exit(3)
