@@ -44,8 +44,9 @@ class ReplicaGroup:
         port = int(port if port is not None else os.environ.get("MASTER_PORT", 29500))
         agent = os.environ.get("TORCHELASTIC_USE_AGENT_STORE", "").lower() == "true"
         host = agent is False and rank == 0
+        # the store's own timeout covers connecting while the other processes start up
         self.store = TCPStore(addr, port, world_size=None if agent else world, is_master=host,
-                              timeout=timedelta(seconds=max(timeout_s, 1.0)), wait_for_workers=False)
+                              timeout=timedelta(seconds=max(timeout_s, 120.0)), wait_for_workers=False)
 
     def _key(self, name: str, what: str) -> str:
         return f"{self.prefix}{name}/{what}"

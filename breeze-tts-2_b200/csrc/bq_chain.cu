@@ -159,10 +159,10 @@ int plan_chain(const bq_gemv_desc* descs, int n, ChainPlanH* cp) {
         P.xw_bytes = align_up(uint32_t(M) * P.xw_pitch + 256u, 16);
         bool any_int4 = false;
         for (int i = 0; i < n; ++i) any_int4 |= is_int4(descs[i].wfmt);
-        P.xsum_w_bytes = any_int4 ? uint32_t(nkw_max * gpk_max * MT) * 64u : 0u;
+        P.xsum_w_bytes = any_int4 ? uint32_t(nkw_max * gpk_max) * 16u * 4u : 0u;  // [block][sub-group][16 rows] fp32
         const int nq = M >= 7 ? 4 : (M + 1) / 2;
-        P.part_bytes = uint32_t(8 * 2 * MT * 8 * nq) * 16u;
-        const uint32_t fixed = 8 * P.xw_bytes + 8 * P.xsum_w_bytes + 2 * P.part_bytes + chain_misc_bytes(M);
+        P.part_bytes = uint32_t(8 * 2 * MT * 8 * nq) * 16u;  // one tile's partial sums
+        const uint32_t fixed = 8 * P.xw_bytes + 8 * P.xsum_w_bytes + kChainMaxTiles * P.part_bytes + chain_misc_bytes();
         // the kernel's static shared memory (abort flag, epoch) and 1 KB per-CTA reserve fit in the opt-in limit
         const uint32_t budget = uint32_t(dev->smem_optin) - 256u;
         if (fixed + 2 * (slot + 16) > budget) continue;
@@ -175,9 +175,9 @@ int plan_chain(const bq_gemv_desc* descs, int n, ChainPlanH* cp) {
         P.smem_xsum = o;
         o += 8 * P.xsum_w_bytes;
         P.smem_part = o;
-        o += 2 * P.part_bytes;
+        o += kChainMaxTiles * P.part_bytes;
         P.smem_misc = o;
-        o += chain_misc_bytes(M);
+        o += chain_misc_bytes();
         o = align_up(o, 16);
         P.smem_bar = o;
         o += 16u * uint32_t(P.R);
@@ -214,9 +214,27 @@ __global__ void scales_tile_major_kernel(const uint32_t* __restrict__ src, uint3
     }
 }
 
-const void* chain_kernel(int mt) {
-    return mt == 1 ? reinterpret_cast<const void*>(&gemv_chain_kernel<1>)
-                   : reinterpret_cast<const void*>(&gemv_chain_kernel<2>);
+template <int MT>
+const void* chain_kernel_mt(int fmt, int gpk) {
+    switch (fmt) {
+        case BQ_W_INT4_TINYGEMM:
+            if (gpk == 4) return reinterpret_cast<const void*>(&gemv_chain_kernel<MT, BQ_W_INT4_TINYGEMM, 4>);
+            if (gpk == 2) return reinterpret_cast<const void*>(&gemv_chain_kernel<MT, BQ_W_INT4_TINYGEMM, 2>);
+            return reinterpret_cast<const void*>(&gemv_chain_kernel<MT, BQ_W_INT4_TINYGEMM, 1>);
+        case BQ_W_INT4_PLAIN: return reinterpret_cast<const void*>(&gemv_chain_kernel<MT, BQ_W_INT4_PLAIN, 1>);
+        case BQ_W_FP8_E4M3: return reinterpret_cast<const void*>(&gemv_chain_kernel<MT, BQ_W_FP8_E4M3, 1>);
+        case BQ_W_INT8: return reinterpret_cast<const void*>(&gemv_chain_kernel<MT, BQ_W_INT8, 1>);
+        case BQ_W_BF16: return reinterpret_cast<const void*>(&gemv_chain_kernel<MT, BQ_W_BF16, 1>);
+        default: return reinterpret_cast<const void*>(&gemv_chain_kernel<MT, -1, 1>);  // mixed formats
+    }
+}
+
+// The kernel for a chain: specialised to its format when every op shares one.
+const void* chain_kernel(const ChainPlanH& cp) {
+    int fmt = cp.ops[0].fmt, gpk = cp.ops[0].gpk;
+    for (const ChainOp& o : cp.ops)
+        if (o.fmt != fmt || o.gpk != gpk) fmt = -1;
+    return cp.mt == 1 ? chain_kernel_mt<1>(fmt, gpk) : chain_kernel_mt<2>(fmt, gpk);
 }
 }  // namespace
 
@@ -287,7 +305,7 @@ int32_t bq_gemv_chain_launch(const bq_gemv_desc* descs, int32_t n, void* workspa
         return set_error(BQ_ERR_WORKSPACE, "chain workspace of %zu bytes given, %lld needed", workspace_bytes,
                          (long long)cp.ws_bytes);
     if (reinterpret_cast<uintptr_t>(workspace) & 255) return set_error(BQ_ERR_ALIGN, "workspace must be 256-byte aligned");
-    const void* fn = chain_kernel(cp.mt);
+    const void* fn = chain_kernel(cp);
     rc = ensure_smem_attr(fn, cp.smem);
     if (rc) return rc;
     int per_sm = 0;

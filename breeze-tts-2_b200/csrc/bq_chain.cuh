@@ -36,7 +36,7 @@ namespace bq {
 
 constexpr int kChainWarps = 8;                      // consumer warps
 constexpr int kChainThreads = (kChainWarps + 1) * 32;  // + the producer warp
-constexpr int kChainMaxTiles = 8;                   // tiles one CTA may own in one op
+constexpr int kChainMaxTiles = 4;                   // tiles one CTA may own in one op
 constexpr int kCounterStride = 32;                  // 128 bytes between per-op counters
 
 // One GEMV of the chain (device copy written by bq_gemv_chain_prepare).
@@ -86,8 +86,8 @@ struct ChainArgs {
     uint32_t smem_x, smem_xsum, smem_part, smem_misc, smem_bar;
     uint32_t xw_bytes;     // staged activations per warp (M rows + a zero block)
     uint32_t xw_pitch;     // bytes per staged row
-    uint32_t xsum_w_bytes; // int4 group sums per warp
-    uint32_t part_bytes;   // one partial-sum buffer
+    uint32_t xsum_w_bytes; // int4 group sums per warp: [block][sub-group][16 rows] fp32
+    uint32_t part_bytes;   // partial sums of one tile (the area holds kChainMaxTiles of them)
     unsigned int* counters;  // [n_ops][kCounterStride]
     ChainHeader* hdr;
 };
@@ -147,12 +147,15 @@ __device__ __forceinline__ bool chain_aborted(ChainCtl* ctl) {
 }
 
 // Bounded mbarrier wait; false (and the CTA aborts) on timeout or abort.
-__device__ __forceinline__ bool chain_mbar_wait(uint32_t bar, uint32_t parity, ChainCtl* ctl) {
+// backoff_ns > 0: sleep between polls (the producer's waits for a free slot,
+// so its spinning does not take issue slots from the consumer warps).
+__device__ __forceinline__ bool chain_mbar_wait(uint32_t bar, uint32_t parity, ChainCtl* ctl, int backoff_ns) {
     const long long limit = ctl->limit;
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     int spins = 0;
     while (!mbar_try_wait(bar, parity)) {
+        if (backoff_ns > 0) __nanosleep(backoff_ns);
         if ((++spins & 255) == 0) {
             if (chain_aborted(ctl)) return false;
             if (clock64() - t0 > limit) {
@@ -213,20 +216,26 @@ __device__ __forceinline__ void chain_producer(const ChainArgs& a, uint8_t* smem
     const uint32_t ring = smem_u32(smem);
     const uint32_t bars = smem_u32(smem + a.smem_bar);  // full[R] then empty[R], 8 bytes each
     const int R = a.ring_slots;
-    uint32_t q = 0;
+    uint32_t q = 0, s = 0, phase = 0;  // fills issued; next slot and the parity of its current fill
     bool ok = true;
     auto acquire_slot = [&](uint32_t bytes, uint32_t& dst, uint32_t& full) -> bool {
-        const uint32_t s = q % uint32_t(R), round = q / uint32_t(R);
-        if (!chain_mbar_wait(bars + 8u * (R + s), (round & 1u) ^ 1u, ctl)) return false;
+        // lane 0 decides for the warp, so every lane takes the same path
+        int free_slot = 0;
+        if (lane == 0) free_slot = chain_mbar_wait(bars + 8u * (R + s), phase ^ 1u, ctl, 128) ? 1 : 0;
+        if (!__shfl_sync(0xffffffffu, free_slot, 0)) return false;
         dst = ring + s * a.slot_bytes;
         full = bars + 8u * s;
         if (lane == 0) mbar_arrive_expect_tx(full, bytes);
         __syncwarp();
         ++q;
+        if (++s == uint32_t(R)) {
+            s = 0;
+            phase ^= 1u;
+        }
         return true;
     };
     for (int j = 0; j < a.n_ops && ok; ++j) {
-        const ChainOp& op = a.ops[j];
+        const ChainOp op = a.ops[j];  // private copy, as in the consumers
         const int t0 = chain_first_tile(op, cta, grid);
         if (t0 >= op.tiles) continue;
         uint32_t dst, full;
@@ -277,7 +286,7 @@ __device__ __forceinline__ void chain_producer(const ChainArgs& a, uint8_t* smem
     // Wait (bounded) for the copies in flight in every slot before leaving:
     // the last use of each slot is its only pending fill.
     const uint32_t first = q > uint32_t(R) ? q - uint32_t(R) : 0u;
-    for (uint32_t u = first; u < q; ++u) {
+    for (uint32_t u = first; u < q && lane == 0; ++u) {
         const uint32_t s = u % uint32_t(R);
         const long long t0 = clock64();
         while (!mbar_try_wait(bars + 8u * s, (u / uint32_t(R)) & 1u)) {
@@ -309,8 +318,9 @@ __device__ __forceinline__ ChainWarpK chain_warp_k(const ChainOp& op, int warp) 
     return k;
 }
 
-// Misc area (floats): ss[8][16], up[8][16], rscale[2 buffers][2 pieces][16],
-// then the residual rows of the CTA's tiles (bf16 [kChainMaxTiles][16 rows of M][16]).
+// Misc area (floats): ss[8 warps][16 rows], up[8][16], rscale[kChainMaxTiles][2
+// pieces][16], then the residual rows of the CTA's tiles (bf16
+// [kChainMaxTiles][16 rows of M][16 columns]).
 struct ChainMisc {
     float* ss;
     float* up;
@@ -319,52 +329,66 @@ struct ChainMisc {
 };
 __device__ __forceinline__ ChainMisc chain_misc(const ChainArgs& a, uint8_t* smem) {
     float* f = reinterpret_cast<float*>(smem + a.smem_misc);
-    return ChainMisc{f, f + 128, f + 256, reinterpret_cast<__nv_bfloat16*>(f + 256 + 64)};
+    return ChainMisc{f, f + 128, f + 256, reinterpret_cast<__nv_bfloat16*>(f + 256 + kChainMaxTiles * 32)};
 }
-constexpr uint32_t chain_misc_bytes(int rows) { return (256 + 64) * 4 + kChainMaxTiles * 16 * 16 * 2 * ((rows + 15) / 16); }
+constexpr uint32_t chain_misc_bytes() { return (256 + kChainMaxTiles * 32) * 4 + kChainMaxTiles * 16 * 16 * 2; }
 
 // Staging of this warp's activations after its x copies landed: bf16 x*gamma
 // in place for int4 / bf16 weights (sum of x^2 per row kept per lane, reduced
-// later), f16 scaled by a per-(warp, row) power of two for fp8 / int8
-// (exact conversions of the weights), as bq_gemv stages them.
-template <int FMT>
-__device__ __forceinline__ float chain_stage(const ChainOp& op, const ChainWarpK& wk, uint8_t* xw, uint32_t pitch,
-                                             const uint8_t* gam, ChainMisc& mc, int warp, int lane) {
+// across the row's lanes), f16 scaled by a per-(warp, row) power of two for
+// fp8 / int8 (exact conversions of the weights), as bq_gemv stages them. For
+// int4 weights the same pass sums the staged (bf16-rounded) activations of
+// every group: xs[(j * GPK + sg) * 16 + m], the X of the group term
+// s * (C - (128 + offset) X) + z * X. Local block j = c * cnt + i holds global
+// k-block c * kbc + lo + i; the loops walk chunks and blocks without divisions.
+template <int FMT, int GPK>
+__device__ __forceinline__ void chain_stage(const ChainOp& op, const ChainWarpK& wk, uint8_t* xw, uint32_t pitch,
+                                            const uint8_t* gam, ChainMisc& mc, float* xs, int warp, int lane) {
     using F = Fmt3<FMT>;
     const int M = op.M;
     const bool norm = op.norm != 0;
     int lg = 0;
     while ((1 << lg) < M) ++lg;
-    const int kp_log = 5 - lg, kp = 1 << kp_log;
+    const int kp_log = 5 - lg, kp = 1 << kp_log;  // lanes per row
     const int lm = lane >> kp_log, lk = lane & (kp - 1);
     const bool rowok = lm < M;
     uint8_t* xrow = xw + lm * pitch;
-    const int nunits = 16 * wk.nkw;
-    auto gamma8 = [&](int t, float (&g)[8]) {
-        const uint4 gv = *reinterpret_cast<const uint4*>(gam + (wk.global_kb(op, t >> 4) * 128 + (t & 15) * 8) * 2);
-        g[0] = bf16lo(gv.x); g[1] = bf16hi(gv.x); g[2] = bf16lo(gv.y); g[3] = bf16hi(gv.y);
-        g[4] = bf16lo(gv.z); g[5] = bf16hi(gv.z); g[6] = bf16lo(gv.w); g[7] = bf16hi(gv.w);
-    };
-    auto x8 = [&](int t, float (&v)[8]) {
-        const uint4 r = *reinterpret_cast<const uint4*>(xrow + (t >> 4) * 256 + (t & 15) * 16);
-        v[0] = bf16lo(r.x); v[1] = bf16hi(r.x); v[2] = bf16lo(r.y); v[3] = bf16hi(r.y);
-        v[4] = bf16lo(r.z); v[5] = bf16hi(r.z); v[6] = bf16lo(r.w); v[7] = bf16hi(r.w);
-    };
+    // unit u (8 values) of the warp's blocks: local block u >> 4, 8 values at (u & 15) * 8.
+    // Lane lk of a row takes units lk, lk + kp, ...: with kp >= 16 one pass covers
+    // kp / 16 blocks, else 16 / kp passes cover one block.
+    const int units = 16 * wk.nkw;
+    const int upb = kp >= 16 ? 16 : kp;  // lanes of one block within a row group
+    auto gkb = [&](int j) { return (j / (wk.cnt > 0 ? wk.cnt : 1)) * op.kbc + wk.lo + j % (wk.cnt > 0 ? wk.cnt : 1); };
     float ss_lane = 0.f;
     if constexpr (!F::kF16) {
-        const bool identity = FMT != BQ_W_INT4_PLAIN && !norm;
-        if (rowok && !identity) {
-#pragma unroll 2
-            for (int t = lk; t < nunits; t += kp) {
+        const bool identity = FMT != BQ_W_INT4_PLAIN && !norm && !F::kInt4;
+        float xg[GPK];
+#pragma unroll
+        for (int g = 0; g < GPK; ++g) xg[g] = 0.f;
+        if (!identity) {
+            // warp-uniform trip count (the group-sum shuffles need every lane)
+#pragma unroll 1
+            for (int base = 0; base < units; base += kp) {
+                const int u = base + lk;
+                const bool ok = rowok && u < units;
+                const int j = u >> 4, off = j * 256 + (u & 15) * 16;
                 float v[8];
-                x8(t, v);
-                if (norm) {
-                    float g[8];
-                    gamma8(t, g);
+                if (ok) {
+                    const uint4 r = *reinterpret_cast<const uint4*>(xrow + off);
+                    v[0] = bf16lo(r.x); v[1] = bf16hi(r.x); v[2] = bf16lo(r.y); v[3] = bf16hi(r.y);
+                    v[4] = bf16lo(r.z); v[5] = bf16hi(r.z); v[6] = bf16lo(r.w); v[7] = bf16hi(r.w);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) v[e] = 0.f;
+                }
+                if (norm && ok) {
+                    const uint4 gv = *reinterpret_cast<const uint4*>(gam + (gkb(j) * 128 + (u & 15) * 8) * 2);
+                    const float g8[8] = {bf16lo(gv.x), bf16hi(gv.x), bf16lo(gv.y), bf16hi(gv.y),
+                                         bf16lo(gv.z), bf16hi(gv.z), bf16lo(gv.w), bf16hi(gv.w)};
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
                         ss_lane = fmaf(v[e], v[e], ss_lane);
-                        v[e] *= g[e];
+                        v[e] *= g8[e];
                     }
                 }
                 uint4 o;
@@ -379,31 +403,56 @@ __device__ __forceinline__ float chain_stage(const ChainOp& op, const ChainWarpK
                     o.z = pack_bf162(v[4], v[5]);
                     o.w = pack_bf162(v[6], v[7]);
                 }
-                *reinterpret_cast<uint4*>(xrow + (t >> 4) * 256 + (t & 15) * 16) = o;
+                if (ok && (norm || FMT == BQ_W_INT4_PLAIN)) *reinterpret_cast<uint4*>(xrow + off) = o;
+                if constexpr (F::kInt4) {
+                    // this unit's share of its group: the rounded values the MMAs read
+                    const float part = ((bf16lo(o.x) + bf16hi(o.x)) + (bf16lo(o.y) + bf16hi(o.y))) +
+                                       ((bf16lo(o.z) + bf16hi(o.z)) + (bf16lo(o.w) + bf16hi(o.w)));
+                    xg[GPK == 1 ? 0 : ((u & 15) * GPK) >> 4] += part;
+                    // a block is complete for this row group after its last unit: reduce
+                    // over the lanes that share it and store the row's X
+                    const bool last = kp >= 16 ? true : ((u & 15) + kp >= 16);
+                    if (last) {
+#pragma unroll
+                        for (int g = 0; g < GPK; ++g) {
+                            float t = xg[g];
+                            for (int o2 = 1; o2 < upb; o2 <<= 1) t += __shfl_xor_sync(0xffffffffu, t, o2);
+                            xg[g] = 0.f;
+                            if (ok && (lk & (upb - 1)) == 0) xs[(j * GPK + g) * 16 + lm] = t;
+                        }
+                    }
+                }
             }
         }
         if (norm) {
-            for (int o = kp >> 1; o; o >>= 1) ss_lane += __shfl_xor_sync(0xffffffffu, ss_lane, o);
+            for (int o2 = kp >> 1; o2; o2 >>= 1) ss_lane += __shfl_xor_sync(0xffffffffu, ss_lane, o2);
             if (lk == 0 && rowok) mc.ss[warp * 16 + lm] = ss_lane;
         }
     } else {
         float ss = 0.f, amax = 0.f;
         if (rowok) {
 #pragma unroll 2
-            for (int t = lk; t < nunits; t += kp) {
-                float v[8], g[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
-                x8(t, v);
-                if (norm) gamma8(t, g);
+            for (int u = lk; u < units; u += kp) {
+                const int j = u >> 4, off = j * 256 + (u & 15) * 16;
+                const uint4 r = *reinterpret_cast<const uint4*>(xrow + off);
+                const float v[8] = {bf16lo(r.x), bf16hi(r.x), bf16lo(r.y), bf16hi(r.y),
+                                    bf16lo(r.z), bf16hi(r.z), bf16lo(r.w), bf16hi(r.w)};
+                float g8[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
+                if (norm) {
+                    const uint4 gv = *reinterpret_cast<const uint4*>(gam + (gkb(j) * 128 + (u & 15) * 8) * 2);
+                    g8[0] = bf16lo(gv.x); g8[1] = bf16hi(gv.x); g8[2] = bf16lo(gv.y); g8[3] = bf16hi(gv.y);
+                    g8[4] = bf16lo(gv.z); g8[5] = bf16hi(gv.z); g8[6] = bf16lo(gv.w); g8[7] = bf16hi(gv.w);
+                }
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
                     ss = fmaf(v[e], v[e], ss);
-                    amax = fmaxf(amax, fabsf(v[e] * g[e]));
+                    amax = fmaxf(amax, fabsf(v[e] * g8[e]));
                 }
             }
         }
-        for (int o = kp >> 1; o; o >>= 1) {
-            ss += __shfl_xor_sync(0xffffffffu, ss, o);
-            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        for (int o2 = kp >> 1; o2; o2 >>= 1) {
+            ss += __shfl_xor_sync(0xffffffffu, ss, o2);
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o2));
         }
         int e = 0;
         if (amax > 0.f && amax < INFINITY) {
@@ -418,21 +467,26 @@ __device__ __forceinline__ float chain_stage(const ChainOp& op, const ChainWarpK
         }
         if (rowok) {
 #pragma unroll 2
-            for (int t = lk; t < nunits; t += kp) {
-                float v[8], g[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
-                x8(t, v);
-                if (norm) gamma8(t, g);
+            for (int u = lk; u < units; u += kp) {
+                const int j = u >> 4, off = j * 256 + (u & 15) * 16;
+                const uint4 r = *reinterpret_cast<const uint4*>(xrow + off);
+                float v[8] = {bf16lo(r.x), bf16hi(r.x), bf16lo(r.y), bf16hi(r.y),
+                              bf16lo(r.z), bf16hi(r.z), bf16lo(r.w), bf16hi(r.w)};
+                if (norm) {
+                    const uint4 gv = *reinterpret_cast<const uint4*>(gam + (gkb(j) * 128 + (u & 15) * 8) * 2);
+                    v[0] *= bf16lo(gv.x); v[1] *= bf16hi(gv.x); v[2] *= bf16lo(gv.y); v[3] *= bf16hi(gv.y);
+                    v[4] *= bf16lo(gv.z); v[5] *= bf16hi(gv.z); v[6] *= bf16lo(gv.w); v[7] *= bf16hi(gv.w);
+                }
                 uint4 o;
-                o.x = pack_half2(v[0] * g[0] * down, v[1] * g[1] * down);
-                o.y = pack_half2(v[2] * g[2] * down, v[3] * g[3] * down);
-                o.z = pack_half2(v[4] * g[4] * down, v[5] * g[5] * down);
-                o.w = pack_half2(v[6] * g[6] * down, v[7] * g[7] * down);
-                *reinterpret_cast<uint4*>(xrow + (t >> 4) * 256 + (t & 15) * 16) = o;
+                o.x = pack_half2(v[0] * down, v[1] * down);
+                o.y = pack_half2(v[2] * down, v[3] * down);
+                o.z = pack_half2(v[4] * down, v[5] * down);
+                o.w = pack_half2(v[6] * down, v[7] * down);
+                *reinterpret_cast<uint4*>(xrow + off) = o;
             }
         }
     }
     __syncwarp();
-    return ss_lane;
 }
 
 // Activation fragments (B operand) of staged local block j, per M tile.
@@ -481,75 +535,36 @@ __device__ __forceinline__ void chain_bfrag(const uint8_t* xw, uint32_t xw_s, ui
     }
 }
 
-// int4: per-group activation sums of columns m0, m0+1 for every staged block
-// of this warp, from MMAs with a 0/1 indicator operand (as bq_gemv): lanes
-// tg == 0 keep {A(m0), X(m0), A(m0+1), X(m0+1)}, A = (128 + offset) * X.
-template <int FMT, int MT, int GPK>
-__device__ __forceinline__ void chain_group_sums(const uint8_t* xw, uint32_t xw_s, uint32_t pitch, int M, int nkw,
-                                                 int lane, const uint8_t* xzero, uint32_t xzero_s, float4* xsum4) {
-    using F = Fmt3<FMT>;
-    const int tq = lane & 3, tg = lane >> 2;
-#pragma unroll 1
-    for (int j = 0; j < nkw; ++j) {
-        uint32_t bf[MT][16];
-        chain_bfrag<FMT, MT>(xw, xw_s, pitch, M, j, lane, xzero, xzero_s, bf);
-#pragma unroll
-        for (int sg = 0; sg < GPK; ++sg) {
-            float c2[2][MT][4];
-#pragma unroll
-            for (int h = 0; h < 2; ++h)
-#pragma unroll
-                for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-                    for (int d = 0; d < 4; ++d) c2[h][mt][d] = 0.f;
-#pragma unroll
-            for (int ii = 0; ii < 8 / GPK; ++ii) {
-                const int i = sg * (8 / GPK) + ii;
-#pragma unroll
-                for (int mt = 0; mt < MT; ++mt)
-                    mma_bf16(c2[ii & 1][mt], 0x3F803F80u, 0u, 0x3F803F80u, 0u, bf[mt][2 * i], bf[mt][2 * i + 1]);
-            }
-            if (tg == 0) {
-#pragma unroll
-                for (int mt = 0; mt < MT; ++mt) {
-                    const float x0 = c2[0][mt][0] + c2[1][mt][0], x1 = c2[0][mt][1] + c2[1][mt][1];
-                    constexpr float kMagic = 128.f + float(F::kOfs);
-                    xsum4[((j * GPK + sg) * MT + mt) * 4 + tq] = make_float4(kMagic * x0, x0, kMagic * x1, x1);
-                }
-            }
-        }
-    }
-    __syncwarp();
-}
-
 // One chunk of one tile: this warp's k-blocks [wk.lo, wk.lo + wk.cnt) of the
 // chunk in ring slot `slot`, accumulated into acc[piece][mt]. Local staged
 // block index of the first one: j0.
 template <int FMT, int MT, int GPK>
 __device__ __forceinline__ void chain_chunk(const ChainOp& op, const uint8_t* slot, const ChainWarpK& wk, int j0,
                                             const uint8_t* xw, uint32_t xw_s, uint32_t pitch, const uint8_t* xzero,
-                                            uint32_t xzero_s, const float4* xsum4, int lane, float (&acc)[2][MT][4]) {
+                                            uint32_t xzero_s, const float* xs, int lane, float (&acc)[2][MT][4]) {
     using F = Fmt3<FMT>;
     constexpr int NCH = MT == 1 ? 4 : 2;  // independent MMA chains
     const int tq = lane & 3, tg = lane >> 2;
     const int rkb = chain_row_kb_bytes(FMT);
     const uint32_t rs = uint32_t(op.kbc) * uint32_t(rkb);  // row stride of a row-major piece
-#pragma unroll 1
+#pragma unroll 2
     for (int i = 0; i < wk.cnt; ++i) {
         const int ic = wk.lo + i;  // block within the chunk
         uint32_t bfr[MT][16];
         chain_bfrag<FMT, MT>(xw, xw_s, pitch, op.M, j0 + i, lane, xzero, xzero_s, bfr);
         float sA[GPK][MT][2], sX[GPK][MT][2];
         if constexpr (F::kInt4) {
+            constexpr float kMagic = 128.f + float(F::kOfs);  // dequantized code = 128 + q
 #pragma unroll
             for (int sg = 0; sg < GPK; ++sg)
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt) {
-                    const float4 ax = xsum4[(((j0 + i) * GPK + sg) * MT + mt) * 4 + tq];
-                    sA[sg][mt][0] = ax.x;
-                    sX[sg][mt][0] = ax.y;
-                    sA[sg][mt][1] = ax.z;
-                    sX[sg][mt][1] = ax.w;
+                    const int m0 = 8 * mt + 2 * tq;
+                    const float2 xx = *reinterpret_cast<const float2*>(xs + ((j0 + i) * GPK + sg) * 16 + m0);
+                    sX[sg][mt][0] = m0 < op.M ? xx.x : 0.f;
+                    sX[sg][mt][1] = m0 + 1 < op.M ? xx.y : 0.f;
+                    sA[sg][mt][0] = kMagic * sX[sg][mt][0];
+                    sA[sg][mt][1] = kMagic * sX[sg][mt][1];
                 }
         }
 #pragma unroll
@@ -668,8 +683,8 @@ __device__ __forceinline__ void chain_chunk(const ChainOp& op, const uint8_t* sl
 // Reduction over the eight warps, norm factor, row scale, bias and the
 // epilogue of one tile, for the M tile `mt` (one warp per M tile).
 template <int FMT, int MT>
-__device__ __forceinline__ void chain_epilogue(const ChainOp& op, const float4* part, const ChainMisc& mc, int pbuf,
-                                               int t, int ti, int mt, int lane) {
+__device__ __forceinline__ void chain_epilogue(const ChainOp& op, const float4* part, const ChainMisc& mc, int t,
+                                               int ti, int mt, int lane) {
     using F = Fmt3<FMT>;
     const int tq = lane & 3, tg = lane >> 2;
     const int M = op.M;
@@ -705,7 +720,7 @@ __device__ __forceinline__ void chain_epilogue(const ChainOp& op, const float4* 
         for (int d = 0; d < 4; ++d) {
             const int r = tg + (d >> 1) * 8;
             float sc = 1.f;
-            if constexpr (FMT == BQ_W_FP8_E4M3 || FMT == BQ_W_INT8) sc = mc.rscale[(pbuf * 2 + p) * 16 + r];
+            if constexpr (FMT == BQ_W_FP8_E4M3 || FMT == BQ_W_INT8) sc = mc.rscale[(ti * 2 + p) * 16 + r];
             float o = v[p][d] * ((d & 1) ? inv1 : inv0) * sc;
             if (op.bias && p < op.pieces) o += load_act(op.bias, chain_piece_row(op, t, p) + r, op.out_dtype);
             v[p][d] = o;
@@ -725,64 +740,76 @@ __device__ __forceinline__ void chain_epilogue(const ChainOp& op, const float4* 
     }
 }
 
+// Ring position of the consumers: slot index and the parity of its current fill.
+struct ChainRing {
+    uint32_t slot, phase;
+    __device__ __forceinline__ void advance(int R) {
+        if (++slot == uint32_t(R)) {
+            slot = 0;
+            phase ^= 1u;
+        }
+    }
+};
+
 // One op's work on this CTA's tiles (consumer warps; the op's inputs are ready).
+// Every warp computes its k-blocks of every tile, chunk by chunk as they land,
+// and leaves each tile's partial sums in shared memory; after one barrier the
+// warps reduce and store the tiles in parallel, one (tile, M tile) each.
 template <int FMT, int MT, int GPK>
 __device__ __forceinline__ void chain_op_body(const ChainArgs& a, const ChainOp& op, uint8_t* smem, ChainCtl* ctl,
-                                           uint32_t& q, int& pbuf) {
+                                              ChainRing& ring) {
     using F = Fmt3<FMT>;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tq = lane & 3, tg = lane >> 2;
     const int grid = gridDim.x, M = op.M, R = a.ring_slots;
     const uint32_t bars = smem_u32(smem + a.smem_bar);
-    const ChainMisc mc = chain_misc(a, smem);
+    ChainMisc mc = chain_misc(a, smem);
     const ChainWarpK wk = chain_warp_k(op, warp);
     uint8_t* xw = smem + a.smem_x + warp * a.xw_bytes;
     const uint32_t xw_s = smem_u32(xw);
     const uint8_t* xzero = xw + M * a.xw_pitch;
     const uint32_t xzero_s = smem_u32(xzero);
-    float4* xsum4 = reinterpret_cast<float4*>(smem + a.smem_xsum + warp * a.xsum_w_bytes);
+    float* xs = reinterpret_cast<float*>(smem + a.smem_xsum + warp * a.xsum_w_bytes);
     const int t0 = chain_first_tile(op, blockIdx.x, grid);
     const int ntile = (op.tiles - t0 + grid - 1) / grid;
 
     // x (this warp's blocks) and the residual rows of the CTA's tiles: L2 only
-    {
+    if (wk.cnt > 0) {
         const char* xb = static_cast<const char*>(op.x);
         const int per_row = wk.nkw * 16;
         for (int sidx = lane; sidx < M * per_row; sidx += 32) {
             const int m = sidx / per_row, r = sidx - m * per_row;
-            cp_async16(xw_s + m * a.xw_pitch + (r >> 4) * 256 + (r & 15) * 16,
-                       xb + (int64_t(m) * op.ldx + wk.global_kb(op, r >> 4) * 128 + (r & 15) * 8) * 2);
+            const int jl = r >> 4, c = jl / wk.cnt, kb = c * op.kbc + wk.lo + (jl - c * wk.cnt);
+            cp_async16(xw_s + m * a.xw_pitch + jl * 256 + (r & 15) * 16,
+                       xb + (int64_t(m) * op.ldx + kb * 128 + (r & 15) * 8) * 2);
         }
-        if (op.epi == BQ_EPI_ADD_RESIDUAL) {
-            const char* rb = static_cast<const char*>(op.residual);
-            for (int c = threadIdx.x; c < ntile * M * 2; c += kChainWarps * 32) {
-                const int ti = c / (M * 2), r = c - ti * M * 2, m = r >> 1, h = r & 1;
-                const int n = 16 * (t0 + ti * grid) + 8 * h;
-                cp_async16(smem_u32(mc.res + (ti * 16 + m) * 16 + 8 * h), rb + (int64_t(m) * op.ldr + n) * 2);
-            }
-        }
-        cp_async_commit();
     }
+    if (op.epi == BQ_EPI_ADD_RESIDUAL) {
+        const char* rb = static_cast<const char*>(op.residual);
+        for (int c = threadIdx.x; c < ntile * M * 2; c += kChainWarps * 32) {
+            const int ti = c / (M * 2), r = c - ti * M * 2, m = r >> 1, h = r & 1;
+            const int n = 16 * (t0 + ti * grid) + 8 * h;
+            cp_async16(smem_u32(mc.res + (ti * 16 + m) * 16 + 8 * h), rb + (int64_t(m) * op.ldr + n) * 2);
+        }
+    }
+    cp_async_commit();
     // gamma arrives through the ring ahead of the weights
     uint32_t gslot = 0;
     const uint8_t* gam = nullptr;
     if (op.norm) {
-        gslot = q % uint32_t(R);
-        chain_mbar_wait(bars + 8u * gslot, (q / uint32_t(R)) & 1u, ctl);
-        ++q;
+        gslot = ring.slot;
+        chain_mbar_wait(bars + 8u * gslot, ring.phase, ctl, 0);
+        ring.advance(R);
         gam = smem + gslot * a.slot_bytes;
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncwarp();
-    ChainMisc mcs = mc;
-    chain_stage<FMT>(op, wk, xw, a.xw_pitch, gam, mcs, warp, lane);
+    chain_stage<FMT, GPK>(op, wk, xw, a.xw_pitch, gam, mc, xs, warp, lane);
     if (op.norm && lane == 0) mbar_arrive(bars + 8u * (R + gslot));
-    if constexpr (F::kInt4) chain_group_sums<FMT, MT, GPK>(xw, xw_s, a.xw_pitch, M, wk.nkw, lane, xzero, xzero_s, xsum4);
 
     const int nq = M >= 7 ? 4 : (M + 1) >> 1;
 #pragma unroll 1
     for (int ti = 0; ti < ntile; ++ti) {
-        const int t = t0 + ti * grid;
         float acc[2][MT][4];
 #pragma unroll
         for (int p = 0; p < 2; ++p)
@@ -792,23 +819,23 @@ __device__ __forceinline__ void chain_op_body(const ChainArgs& a, const ChainOp&
                 for (int d = 0; d < 4; ++d) acc[p][mt][d] = 0.f;
 #pragma unroll 1
         for (int c = 0; c < op.nchunk; ++c) {
-            const uint32_t sl = q % uint32_t(R);
-            chain_mbar_wait(bars + 8u * sl, (q / uint32_t(R)) & 1u, ctl);
-            ++q;
+            const uint32_t sl = ring.slot;
+            chain_mbar_wait(bars + 8u * sl, ring.phase, ctl, 0);
+            ring.advance(R);
             const uint8_t* slot = smem + sl * a.slot_bytes;
-            chain_chunk<FMT, MT, GPK>(op, slot, wk, c * wk.cnt, xw, xw_s, a.xw_pitch, xzero, xzero_s, xsum4, lane, acc);
+            chain_chunk<FMT, MT, GPK>(op, slot, wk, c * wk.cnt, xw, xw_s, a.xw_pitch, xzero, xzero_s, xs, lane, acc);
             if constexpr (FMT == BQ_W_FP8_E4M3 || FMT == BQ_W_INT8) {
                 if (c == op.nchunk - 1 && warp == 0 && lane < 16 * op.pieces) {
                     const int p = lane >> 4;
                     float sc = *reinterpret_cast<const float*>(slot + p * op.piece_bytes + op.wpiece + (lane & 15) * 4);
                     if (FMT == BQ_W_INT8 && (op.flags & BQ_FLAG_SCALE_ROUND_BF16)) sc = __bfloat162float(__float2bfloat16_rn(sc));
-                    mc.rscale[(pbuf * 2 + p) * 16 + (lane & 15)] = sc;
+                    mc.rscale[(ti * 2 + p) * 16 + (lane & 15)] = sc;
                 }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(bars + 8u * (R + sl));
         }
-        float4* part = reinterpret_cast<float4*>(smem + a.smem_part + pbuf * a.part_bytes);
+        float4* part = reinterpret_cast<float4*>(smem + a.smem_part + ti * a.part_bytes);
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
             const int m0 = 8 * mt + 2 * tq;
@@ -820,28 +847,39 @@ __device__ __forceinline__ void chain_op_body(const ChainArgs& a, const ChainOp&
                     part[(((warp * 2 + p) * MT + mt) * 8 + tg) * nq + tq] =
                         make_float4(acc[p][mt][0] * u0, acc[p][mt][1] * u1, acc[p][mt][2] * u0, acc[p][mt][3] * u1);
         }
-        consumer_sync();
-        if (warp < MT) chain_epilogue<FMT, MT>(op, part, mc, pbuf, t, ti, warp, lane);
-        pbuf ^= 1;
+    }
+    consumer_sync();
+    for (int task = warp; task < ntile * MT; task += kChainWarps) {
+        const int ti = task / MT, mt = task - ti * MT;
+        chain_epilogue<FMT, MT>(op, reinterpret_cast<const float4*>(smem + a.smem_part + ti * a.part_bytes), mc,
+                                t0 + ti * grid, ti, mt, lane);
     }
 }
 
-template <int MT>
+// FMT >= 0: every op of the chain has this format (and GPK): one body, a
+// small kernel whose code stays in the instruction caches from op to op (the
+// all-format kernel spent ~1 us per op refetching its code). FMT < 0: any
+// mix of formats, dispatched per op.
+template <int MT, int FMT, int GPK>
 __device__ __forceinline__ void chain_dispatch(const ChainArgs& a, const ChainOp& op, uint8_t* smem, ChainCtl* ctl,
-                                               uint32_t& q, int& pbuf) {
+                                               ChainRing& ring) {
+    if constexpr (FMT >= 0) {
+        chain_op_body<FMT, MT, GPK>(a, op, smem, ctl, ring);
+        return;
+    }
     switch (op.fmt) {
         case BQ_W_INT4_TINYGEMM:
             if (op.gpk == 4)
-                chain_op_body<BQ_W_INT4_TINYGEMM, MT, 4>(a, op, smem, ctl, q, pbuf);
+                chain_op_body<BQ_W_INT4_TINYGEMM, MT, 4>(a, op, smem, ctl, ring);
             else if (op.gpk == 2)
-                chain_op_body<BQ_W_INT4_TINYGEMM, MT, 2>(a, op, smem, ctl, q, pbuf);
+                chain_op_body<BQ_W_INT4_TINYGEMM, MT, 2>(a, op, smem, ctl, ring);
             else
-                chain_op_body<BQ_W_INT4_TINYGEMM, MT, 1>(a, op, smem, ctl, q, pbuf);
+                chain_op_body<BQ_W_INT4_TINYGEMM, MT, 1>(a, op, smem, ctl, ring);
             break;
-        case BQ_W_INT4_PLAIN: chain_op_body<BQ_W_INT4_PLAIN, MT, 1>(a, op, smem, ctl, q, pbuf); break;
-        case BQ_W_FP8_E4M3: chain_op_body<BQ_W_FP8_E4M3, MT, 1>(a, op, smem, ctl, q, pbuf); break;
-        case BQ_W_INT8: chain_op_body<BQ_W_INT8, MT, 1>(a, op, smem, ctl, q, pbuf); break;
-        default: chain_op_body<BQ_W_BF16, MT, 1>(a, op, smem, ctl, q, pbuf); break;
+        case BQ_W_INT4_PLAIN: chain_op_body<BQ_W_INT4_PLAIN, MT, 1>(a, op, smem, ctl, ring); break;
+        case BQ_W_FP8_E4M3: chain_op_body<BQ_W_FP8_E4M3, MT, 1>(a, op, smem, ctl, ring); break;
+        case BQ_W_INT8: chain_op_body<BQ_W_INT8, MT, 1>(a, op, smem, ctl, ring); break;
+        default: chain_op_body<BQ_W_BF16, MT, 1>(a, op, smem, ctl, ring); break;
     }
 }
 
@@ -849,15 +887,19 @@ __device__ __forceinline__ void chain_dispatch(const ChainArgs& a, const ChainOp
 // op j - 1 (or the start flag), works, and signals op j once all its stores
 // are issued and fenced; a CTA with no tiles in op j signals at once (it
 // reads and writes nothing for it).
-template <int MT>
+template <int MT, int FMT, int GPK>
 __device__ __forceinline__ void chain_consumer(const ChainArgs& a, const ChainHeader* hdr, uint8_t* smem,
                                                ChainCtl* ctl, unsigned int target) {
-    uint32_t q = 0;
-    int pbuf = 0;
+    ChainRing ring{0u, 0u};
+    // the waiting and signalling thread sits in warp 1: warp 0 shares its
+    // scheduler with the producer warp
+    constexpr int kLead = 32;
     for (int j = 0; j < a.n_ops; ++j) {
-        const ChainOp& op = a.ops[j];
+        // a private copy: the inline-PTX memory clobbers of the hot loops would
+        // otherwise make every field a fresh global load
+        const ChainOp op = a.ops[j];
         if (chain_first_tile(op, blockIdx.x, gridDim.x) < op.tiles) {
-            if (threadIdx.x == 0) {
+            if (threadIdx.x == kLead) {
                 if (j > 0)
                     chain_counter_wait(a.counters + (j - 1) * kCounterStride, target, ctl);
                 else if (hdr->start_flag)
@@ -865,17 +907,17 @@ __device__ __forceinline__ void chain_consumer(const ChainArgs& a, const ChainHe
                 __threadfence();
             }
             if (consumer_sync_or(ctl->abort != 0)) return;
-            chain_dispatch<MT>(a, op, smem, ctl, q, pbuf);
+            chain_dispatch<MT, FMT, GPK>(a, op, smem, ctl, ring);
             if (consumer_sync_or(ctl->abort != 0)) return;
         }
-        if (threadIdx.x == 0) {
+        if (threadIdx.x == kLead) {
             __threadfence();
             atomicAdd(a.counters + j * kCounterStride, 1u);
         }
     }
 }
 
-template <int MT>
+template <int MT, int FMT, int GPK>
 __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const ChainArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ ChainCtl ctl;
@@ -902,7 +944,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const Chai
     if (warp == kChainWarps)
         chain_producer(a, smem, &ctl);
     else
-        chain_consumer<MT>(a, hdr, smem, &ctl, (s_epoch + 1u) * gridDim.x);
+        chain_consumer<MT, FMT, GPK>(a, hdr, smem, &ctl, (s_epoch + 1u) * gridDim.x);
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();

@@ -10,8 +10,13 @@ the inputs it actually read, at max rel err 1e-2: QKV (RMSNorm fused), the
 attention output and the k / v it wrote, O (+ residual), gate+up (RMSNorm,
 SiLU*up), down (+ residual) and the fp32 head (RMSNorm fused).
 
+The same checks run through the one-launch decode chain (DecodeStack
+chain=True, the persistent kernel) at M = 1, 2, 4 and 8, the rows whose
+staged activations fit beside its weight ring at K = 8192.
+
 The whole 28-layer step the benchmark times is also run per format (M = 1
-and 16), and its last layer and head are checked the same way.
+and 16 launch by launch, M = 1 and 4 as one chain launch), and its last
+layer and head are checked the same way.
 """
 
 import pytest
@@ -52,12 +57,12 @@ def _check(name, got, x, w, gamma=None, epilogue=0, residual=None):
     assert err <= TOL, f"{name}: max rel err {err:.3e}"
 
 
-def _run_and_check(fmt, rows, n_layers, attention):
+def _run_and_check(fmt, rows, n_layers, attention, chain=False):
     from breeze_b200 import _lib
     from breeze_b200.fused.stack import DecodeStack
 
     layers, head, ln_f, deq = _stack_weights(fmt, n_layers)
-    st = DecodeStack(layers, head, ln_f, rows=rows, attention=attention)
+    st = DecodeStack(layers, head, ln_f, rows=rows, attention=attention, chain=chain)
     g = torch.Generator().manual_seed(100 + rows)
     st.x.copy_(torch.randn(rows, st.hidden, generator=g).to(torch.bfloat16))
     li = n_layers - 1
@@ -71,7 +76,7 @@ def _run_and_check(fmt, rows, n_layers, attention):
     last = layers[li]
     xin = st.x if n_layers == 1 else st.res[(li - 1) % 2]
     y = st.res[li % 2]
-    tag = f"{fmt} M={rows} layers={n_layers} attention={attention}"
+    tag = f"{fmt} M={rows} layers={n_layers} attention={attention} chain={chain}"
     _check(f"qkv [{tag}]", st.qkv, xin, deq["wqkv"], gamma=last.ln1)
     if attention:
         pos = int(st.pos.item())
@@ -99,7 +104,13 @@ def test_full_size_layer_stages_match_oracle(fmt, rows, attention):
     _run_and_check(fmt, rows, 1, attention)
 
 
-@pytest.mark.parametrize("rows", [1, 16])
+@pytest.mark.parametrize("rows", [1, 2, 4, 8])
 @pytest.mark.parametrize("fmt", ["int4", "fp8", "int8"])
-def test_full_28_layer_step_last_layer_matches_oracle(fmt, rows):
-    _run_and_check(fmt, rows, 28, False)
+def test_full_size_layer_stages_match_oracle_one_launch(fmt, rows):
+    _run_and_check(fmt, rows, 1, False, chain=True)
+
+
+@pytest.mark.parametrize("rows,chain", [(1, False), (16, False), (1, True), (4, True)])
+@pytest.mark.parametrize("fmt", ["int4", "fp8", "int8"])
+def test_full_28_layer_step_last_layer_matches_oracle(fmt, rows, chain):
+    _run_and_check(fmt, rows, 28, False, chain=chain)
