@@ -79,6 +79,11 @@ class Ranks:
     def failed(self) -> list[int]:
         return sorted(self.grp.failed) if self.grp is not None else []
 
+    def close(self) -> None:
+        """Leave the group (the rank hosting the store waits for the others)."""
+        if self.grp is not None:
+            self.grp.close()
+
 
 def measured_peak():
     p = ROOT / "MEASURED_PEAKS.json"
@@ -258,7 +263,7 @@ def run_ours(args, rank, local_rank, world):
         if world > 1:
             line["replicas_failed"] = ranks.failed
         print(json.dumps(line), flush=True)
-    ranks.meet()  # rank 0 hosts the store: the others finish before it exits
+    ranks.close()
 
 
 DECODE_FORMATS = ("int4", "fp8", "int8")
