@@ -260,6 +260,16 @@ def run_ours(args, rank, local_rank, world):
             line["decode_step"] = decode
         if depth is not None:
             line["depth_frame"] = depth
+        if world == 1 and not args.no_reference_gpu:
+            ours_ref = {"config1_us": per_launch_s * 1e6}
+            for e in (decode or {}).get("results", []):
+                step = e.get("per_op", {}).get("step_us")
+                if step is not None:
+                    ours_ref[f"{e['format']}_{e['rows']}"] = step
+            try:
+                line["reference_gpu"] = reference_gpu_bench(device, copies, x, gamma, ours_ref)
+            except Exception as ex:  # noqa: BLE001 - reported, never hidden
+                line["reference_gpu"] = {"unavailable": f"{type(ex).__name__}: {str(ex)[:200]}"}
         if world > 1:
             line["replicas_failed"] = ranks.failed
         print(json.dumps(line), flush=True)
@@ -419,6 +429,219 @@ def shape_bench(device, spec: str, steps: int, warmup: int):
             "algorithmic_bytes_per_call": algo}
 
 
+REF_DIR = ROOT / "baseline" / "_ref"
+# The reference's own rms_gemv autotune results on this pool's B200 (its
+# BREEZE_FUSED_TUNE file format, written by its unmodified tuner); the bench
+# hands the reference a copy so its first call does not re-tune for minutes.
+REF_TUNE = ROOT / "reference_tune_b200.json"
+
+
+def _reference_modules():
+    """The unmodified reference's fused kernels and Int4Linear from
+    baseline/_ref (None when the reference is not installed there)."""
+    if not (REF_DIR / "models" / "fused" / "kernels.py").exists():
+        return None
+    import shutil
+    import tempfile
+
+    tune = Path(tempfile.gettempdir()) / "bq_reference_fused_tune.json"
+    if REF_TUNE.exists():
+        shutil.copyfile(REF_TUNE, tune)
+    os.environ["BREEZE_FUSED_TUNE"] = str(tune)  # read when models.fused.kernels is imported
+    if str(REF_DIR) not in sys.path:
+        sys.path.insert(0, str(REF_DIR))
+    import models.fused.kernels as rk  # noqa: PLC0415 - the reference package
+    import models.int4_linear as ri4  # noqa: PLC0415
+
+    return rk, ri4
+
+
+def _graph_us_per_replay(fn, device, replays: int = 10, warmup: int = 3) -> float:
+    """fn recorded once into a CUDA graph; device time per replay (us)."""
+    fn()
+    torch.cuda.synchronize(device)
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side), torch.cuda.graph(graph, stream=side):
+        fn()
+    torch.cuda.current_stream(device).wait_stream(side)
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(replays):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize(device)
+    del graph
+    return e0.elapsed_time(e1) * 1e3 / replays
+
+
+def reference_gpu_bench(device, copies, x, gamma, ours: dict) -> dict:
+    """The reference's own GPU path on this B200, timed like ours (CUDA-graph
+    replays, cold rotated weight copies, CUDA events), next to ours:
+
+      config 1: Triton rms_gemv over FusedWeight(W, 4) (the same plain int4
+        codes, scales and mins as ours) and tinygemm Int4Linear alone (no
+        norm), models/fused/kernels.py:334-351, models/int4_linear.py:99-109;
+      config 3 int4 decode step (28 layers + head, M = 1, 2, 16): Int4Linear
+        (tinygemm) projections with the reference's Triton rmsnorm / silu_mul
+        around them, as its FusedDecoderLayer runs an int4 MLP
+        (models/fused/layer.py:92-96), the attention projections in int4 too;
+      config 3 fp8 decode step (M = 1, 2): Triton rms_gemv over FusedWeight(W,
+        8) for every projection (layer.py:87-98 with mlp_bits=8, attn_bits=8).
+    ``ours`` holds this build's figures for the same cases (us)."""
+    mods = _reference_modules()
+    if mods is None:
+        return {"unavailable": "the reference is not installed in baseline/_ref"}
+    if not REF_TUNE.exists():
+        return {"unavailable": "no B200 tune file for the reference's Triton kernels (reference_tune_b200.json)"}
+    rk, ri4 = mods
+    out = {"source": "unmodified reference modules from baseline/_ref, same box and run", "cases": []}
+    for case in (_ref_config1_triton, _ref_config1_tinygemm, _ref_int4_stack, _ref_fp8_stack):
+        try:
+            case(rk, ri4, device, copies, x, gamma, ours, out)
+        except Exception as ex:  # noqa: BLE001 - reported per case, never hidden
+            out["cases"].append({"case": case.__name__, "unavailable": f"{type(ex).__name__}: {str(ex)[:200]}"})
+        torch.cuda.empty_cache()
+    return out
+
+
+def _ref_add(out, case, ref_us, ours_us, weight_bytes):
+    e = {"case": case, "reference_us": round(ref_us, 2), "ours_us": None if ours_us is None else round(ours_us, 2),
+         "reference_weight_GBps": round(weight_bytes / ref_us / 1e3, 1)}
+    if ours_us:
+        e["ours_over_reference_speedup"] = round(ref_us / ours_us, 3)
+    out["cases"].append(e)
+
+
+def _ref_config1_triton(rk, ri4, device, copies, x, gamma, ours, out):
+    """config 1: Triton rms_gemv (plain int4) over the same rotated copies."""
+    rf = []
+    for c in copies:
+        f = rk.FusedWeight.__new__(rk.FusedWeight)
+        f.bits, f.N, f.K = 4, c.N, c.K
+        f.w, f.s, f.z = c.w, c.s.contiguous(), c.z.contiguous()
+        rf.append(f)
+    y = torch.empty(M, N, device=device, dtype=torch.bfloat16)
+
+    def triton_calls():
+        for f in rf:
+            rk.rms_gemv(x, f, gamma, EPS, out=y)
+
+    us = _graph_us_per_replay(triton_calls, device) / len(rf)
+    _ref_add(out, "config 1: fused RMSNorm -> int4 GEMV (Triton rms_gemv, bits=4), per call", us, ours.get("config1_us"),
+             ALGO_BYTES)
+
+
+def _ref_config1_tinygemm(rk, ri4, device, copies, x, gamma, ours, out):
+    """config 1 shape: tinygemm Int4Linear alone (no norm), same rotation."""
+    lin = torch.nn.Linear(K, N, bias=False, device=device, dtype=torch.bfloat16)
+    base = ri4.Int4Linear(lin, group_size=GROUP)
+    del lin
+    mods4 = [base]
+    for _ in range(len(copies) - 1):
+        m = ri4.Int4Linear.__new__(ri4.Int4Linear)
+        torch.nn.Module.__init__(m)
+        m.in_features, m.out_features, m.group_size = base.in_features, base.out_features, base.group_size
+        m.register_buffer("weight_int4", base.weight_int4.clone())
+        m.register_buffer("scales_zeros", base.scales_zeros.clone())
+        mods4.append(m)
+    xs = x.clone()
+
+    def tinygemm_calls():
+        for m in mods4:
+            m(xs)
+
+    us = _graph_us_per_replay(tinygemm_calls, device) / len(mods4)
+    wb = base.weight_int4.numel() * 4 + base.scales_zeros.numel() * 2
+    _ref_add(out, "config 1 shape 2048->6144: tinygemm Int4Linear alone (no norm), per call", us, None, wb)
+
+
+_REF_H, _REF_QKV, _REF_INTER, _REF_HEAD = 2048, 6144, 8192, 8192
+
+
+def _ref_int4_stack(rk, ri4, device, copies, x, gamma, ours, out):
+    """config 3 int4 step: Int4Linear (tinygemm) projections, Triton rmsnorm /
+    silu_mul around them; O reads a static attention-output buffer (attention
+    is not part of config 3; the reference's O input is always contiguous)."""
+    H, QKV, INTER, HEAD, L = _REF_H, _REF_QKV, _REF_INTER, _REF_HEAD, DECODE_LAYERS
+    gen = torch.Generator(device=device).manual_seed(5)
+
+    def rand_linear(n, k):
+        lin = torch.nn.Linear(k, n, bias=False, device=device, dtype=torch.bfloat16)
+        with torch.no_grad():
+            lin.weight.copy_(torch.randn(n, k, device=device, generator=gen) * 0.02)
+        return lin
+
+    def norm_w(n=H):
+        return (1 + 0.1 * torch.randn(n, device=device, generator=gen)).to(torch.bfloat16)
+
+    layers = []
+    for _ in range(L):
+        layers.append({name: ri4.Int4Linear(rand_linear(n, k), group_size=GROUP) for name, n, k in
+                       (("qkv", QKV, H), ("o", H, H), ("gate", INTER, H), ("up", INTER, H), ("down", H, INTER))})
+        layers[-1]["ln1"], layers[-1]["ln2"] = norm_w(), norm_w()
+    head = ri4.Int4Linear(rand_linear(HEAD, H), group_size=GROUP)
+    ln_f = norm_w()
+    wb4 = sum(m.weight_int4.numel() * 4 + m.scales_zeros.numel() * 2 for l in layers for m in l.values()
+              if isinstance(m, ri4.Int4Linear)) + head.weight_int4.numel() * 4 + head.scales_zeros.numel() * 2
+    for rows in (1, 2, 16):
+        x0 = torch.randn(rows, H, device=device, generator=gen).to(torch.bfloat16)
+        attn = torch.randn(rows, H, device=device, generator=gen).to(torch.bfloat16)
+
+        def step4():
+            h = x0
+            for l in layers:
+                l["qkv"](rk.rmsnorm(h, l["ln1"], EPS))
+                hh = l["o"](attn) + h
+                n2 = rk.rmsnorm(hh, l["ln2"], EPS)
+                h = l["down"](rk.silu_mul(l["gate"](n2), l["up"](n2))) + hh
+            return head(rk.rmsnorm(h, ln_f, EPS)).float()
+
+        us = _graph_us_per_replay(step4, device)
+        _ref_add(out, f"config 3 int4 decode step M={rows} (tinygemm + Triton rmsnorm/silu_mul)", us,
+                 ours.get(f"int4_{rows}"), wb4)
+
+
+def _ref_fp8_stack(rk, ri4, device, copies, x, gamma, ours, out):
+    """config 3 fp8 step: Triton rms_gemv over FusedWeight(W, 8) everywhere."""
+    H, QKV, INTER, HEAD, L = _REF_H, _REF_QKV, _REF_INTER, _REF_HEAD, DECODE_LAYERS
+    gen = torch.Generator(device=device).manual_seed(6)
+
+    def norm_w(n=H):
+        return (1 + 0.1 * torch.randn(n, device=device, generator=gen)).to(torch.bfloat16)
+
+    layers8 = []
+    for _ in range(L):
+        wq = torch.randn(QKV, H, device=device, generator=gen) * 0.02
+        wo = torch.randn(H, H, device=device, generator=gen) * 0.02
+        wgu = torch.randn(2 * INTER, H, device=device, generator=gen) * 0.02
+        wd = torch.randn(H, INTER, device=device, generator=gen) * 0.02
+        layers8.append({"qkv": rk.FusedWeight(wq, 8), "o": rk.FusedWeight(wo, 8), "gu": rk.FusedWeight(wgu, 8),
+                        "down": rk.FusedWeight(wd, 8), "ln1": norm_w(), "ln2": norm_w()})
+    head8 = rk.FusedWeight(torch.randn(HEAD, H, device=device, generator=gen) * 0.02, 8)
+    ln_f = norm_w()
+    wb8 = sum(f.w.numel() + f.s.numel() * 4 for l in layers8 for f in l.values() if isinstance(f, rk.FusedWeight))
+    wb8 += head8.w.numel() + head8.s.numel() * 4
+    for rows in (1, 2):
+        x0 = torch.randn(rows, H, device=device, generator=gen).to(torch.bfloat16)
+
+        def step8():
+            h = x0
+            for l in layers8:
+                qkv = rk.rms_gemv(h, l["qkv"], l["ln1"], EPS)
+                hh = rk.rms_gemv(qkv[:, :H], l["o"], None, EPS, epilogue=2, residual=h)
+                act = rk.rms_gemv(hh, l["gu"], l["ln2"], EPS, epilogue=1)
+                h = rk.rms_gemv(act, l["down"], None, EPS, epilogue=2, residual=hh)
+            return rk.rms_gemv(h, head8, ln_f, EPS).float()
+
+        us = _graph_us_per_replay(step8, device)
+        _ref_add(out, f"config 3 fp8 decode step M={rows} (Triton rms_gemv bits=8)", us, ours.get(f"fp8_{rows}"), wb8)
+
+
 def _cpu_inputs():
     g = torch.Generator().manual_seed(1234)
     codes = torch.randint(0, 16, (N, K), generator=g, dtype=torch.int32).to(torch.uint8)
@@ -492,6 +715,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode-step", action="store_true", help="skip the 28-layer decode-step leg")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip timing the reference's own GPU kernels (baseline/_ref) on the same device")
     ap.add_argument("--shape", default=None, metavar="FMT:N:K:M:EPI",
                     help="time one GEMV shape (fmt int4|fp8|int8|bf16, epilogue 0 none / 1 SiLU*up / 2 residual; "
                          "RMSNorm unless EPI is 2) over rotated weight copies > 4x L2 and print its JSON")
