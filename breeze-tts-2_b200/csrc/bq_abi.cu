@@ -163,6 +163,11 @@ int32_t bq_gemv_workspace_bytes(const bq_gemv_desc* desc, size_t* bytes) {
     if (!bytes) return set_error(BQ_ERR_INVALID_ARG, "bytes is NULL");
     int rc = validate_gemv(desc);
     if (rc) return rc;
+    TcPlan tp;
+    if (plan_tc(desc, &tp)) {
+        *bytes = size_t(tp.ws_bytes);
+        return BQ_OK;
+    }
     const int step = gemv3_rows_per_launch(desc);
     int64_t need = 0;
     for (int row0 = 0; row0 < desc->M; row0 += step) {
@@ -183,6 +188,15 @@ int32_t bq_gemv(const bq_gemv_desc* desc, void* workspace, size_t workspace_byte
     const DeviceInfo* di = device_info();
     if (!di) return BQ_ERR_CUDA;
     if (di->major != 10) return set_error(BQ_ERR_DEVICE, "sm_%d%d device: this library is built for sm_100a", di->major, di->minor);
+    TcPlan tp;
+    if (plan_tc(desc, &tp)) {
+        if (!workspace || int64_t(workspace_bytes) < tp.ws_bytes)
+            return set_error(BQ_ERR_WORKSPACE, "workspace of %zu bytes given, %lld needed", workspace_bytes,
+                             (long long)tp.ws_bytes);
+        if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+            return set_error(BQ_ERR_ALIGN, "workspace must be 256-byte aligned");
+        return launch_tc(desc, tp, workspace, static_cast<cudaStream_t>(stream));
+    }
     const int step = gemv3_rows_per_launch(desc);
     for (int row0 = 0; row0 < desc->M; row0 += step) {
         Gemv3Plan pl;

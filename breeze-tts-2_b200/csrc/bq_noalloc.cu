@@ -82,6 +82,15 @@ extern "C" int32_t bq_gemv_noalloc(const bq_gemv_desc* desc, void* stream) {
     size_t need = 0;
     int rc = bq_gemv_workspace_bytes(desc, &need);  // validates the descriptor, plans every row block
     if (rc) return rc;
+    bq_gemv_desc rows16;
+    if (int64_t(need) > kNoAllocScratchBytes && !(desc->flags & BQ_FLAG_NO_TC)) {
+        // the tensor-core kernel's per-CTA pieces do not fit: the row-block kernel needs less
+        rows16 = *desc;
+        rows16.flags |= BQ_FLAG_NO_TC;
+        rc = bq_gemv_workspace_bytes(&rows16, &need);
+        if (rc) return rc;
+        desc = &rows16;
+    }
     if (int64_t(need) > kNoAllocScratchBytes)
         return set_error(BQ_ERR_WORKSPACE,
                          "bq_gemv_noalloc: this shape needs %zu bytes of scratch, the fixed array holds %lld "

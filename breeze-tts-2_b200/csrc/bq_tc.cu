@@ -1,0 +1,828 @@
+// Tensor-core GEMV for 17..128 activation rows: every weight byte is read once
+// whatever the row count (the mma.sync kernel re-streams the weights once per
+// 16 rows). Same contract as bq_gemv (models/fused/kernels.py:334-351,
+// models/int4_linear.py:99-109 -- tinygemm's single pass over the weights at
+// any M --, models/fp8_linear.py:68-83, models/int8_linear.py:50-53).
+//
+// One CTA per SM, 14 warps:
+//   warps 0-7  dequantizers, two groups of four. Group g takes the CTA's
+//              k-blocks g, g+2, ...; thread r of a group owns weight row r of
+//              the 128-row unit. It streams its own row's bytes with cp.async
+//              into a private ring (no cross-thread hand-off of raw data),
+//              dequantizes 128 k at a time to bf16 in registers and writes
+//              them with tcgen05.st into its tensor-memory (TMEM) lane: the
+//              MMA's A operand lives in TMEM, so dequantized weights never
+//              touch shared memory.
+//   warp 8     activation loader: cp.async of the k-block's X tile (bf16
+//              rows, K-major core matrices) into a shared-memory stage,
+//              completion through cp.async.mbarrier.arrive.
+//   warp 9     allocates TMEM; one thread issues tcgen05.mma kind::f16
+//              (M = 128 weight rows, N = rows rounded up to 16, K = 16; A from
+//              TMEM, B from shared memory, fp32 accumulators in TMEM) and
+//              tcgen05.commit to free stages / publish accumulators.
+//   warps 10-13 epilogue, one per TMEM lane quadrant: tcgen05.ld of the
+//              accumulator, per-row scale, bias, SiLU*up or + residual, cast.
+// TMEM: 2 accumulators (columns 0 and 128) so a segment's epilogue overlaps
+// the next segment's MMAs; 4 A stages of 64 columns at 256..511.
+//
+// Work split (stream-K): a unit is 128 weight rows (SiLU*up: 64 gate rows and
+// the matching 64 up rows), an item is (unit, 128-k block); CTA c takes the
+// contiguous item range [c*T/G, (c+1)*T/G) in unit-major order. A unit covered
+// by one CTA is finished from TMEM; otherwise every covering CTA writes its
+// fp32 piece to the workspace and the last to arrive sums the pieces in
+// piece order (deterministic) and finishes the unit.
+//
+// With an RMSNorm the rows are normalized first by a short kernel into the
+// workspace (bf16 x * rstd * gamma, as models/fused/kernels.py:541
+// rmsnorm_kernel computes it); programmatic dependent launch lets the weight
+// stream of the GEMV start while it runs.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+
+#include "bq_device.cuh"
+#include "bq_host.h"
+
+namespace bq {
+namespace {
+
+constexpr int kTcWarps = 14;
+constexpr int kTcThreads = kTcWarps * 32;
+constexpr int kTcXWarp = 8;
+constexpr int kTcMmaWarp = 9;
+constexpr int kTcStages = 4;       // A (TMEM) and X (shared) stages, indexed by block % 4
+constexpr int kTcTmemCols = 512;
+constexpr int kTcAccCols = 128;    // columns per accumulator (N <= 128)
+constexpr int kTcACol0 = 256;      // A stage a at columns 256 + 64 a
+constexpr int kTcACols = 64;       // 128 bf16 k-values of one row = 64 32-bit columns
+constexpr int kTcXGroup = 2048;    // 8 activation rows x 16 k-chunks of 16 B (core matrices)
+constexpr int kTcRawChunk = 2048;  // one 16-byte chunk for each of the 128 rows
+constexpr int kTcScSlot = 2048;    // int4: up to 4 (scale, zero) words for each of the 128 rows
+constexpr int kTcMinRows = 17;
+constexpr int kTcMaxRows = 128;
+
+struct TcParams {
+    const void* w;
+    const void* scale;
+    const void* bias;
+    const void* residual;
+    void* out;
+    const __nv_bfloat16* x;
+    long long ldx, ldr, ldo;
+    int M, N, K, KB, group, epi, out_dtype, res_dtype;
+    unsigned flags;
+    int units, items, n_mma, max_pieces, raw_depth;
+    unsigned idesc;
+    long long wait_cycles;
+    float* part;
+    unsigned* counters;
+    unsigned sm_x, sm_raw, sm_sc, sm_xch, sm_bar, sm_total;
+    unsigned raw_slot, sc_slot;  // bytes per ring slot
+};
+
+// Bytes of one weight row per 128-k block, by format.
+__host__ __device__ constexpr int tc_row_bytes(int fmt) {
+    return (fmt == BQ_W_INT4_TINYGEMM || fmt == BQ_W_INT4_PLAIN) ? 64 : fmt == BQ_W_BF16 ? 256 : 128;
+}
+
+// ------------------------------------------------------------- tcgen05 / TMEM
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t slot_smem, uint32_t cols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot_smem), "r"(cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// D[tmem] (+)= A[tmem] . B[smem]^T, one 128 x N x 16 step.
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// The mbarrier completes one phase once every tcgen05 op issued so far by this thread is done.
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major bf16 operand without swizzle:
+// core matrices of 8 rows x 16 bytes; the two 8-k halves of a k16 step are
+// 128 B apart (leading offset), consecutive 8-row groups 2048 B apart (stride
+// offset); bit 46 is the sm_100 descriptor version.
+__device__ __forceinline__ uint64_t tc_bdesc(uint32_t saddr) {
+    return uint64_t((saddr >> 4) & 0x3FFFu) | (uint64_t(128 >> 4) << 16) | (uint64_t(kTcXGroup >> 4) << 32) |
+           (1ull << 46);
+}
+
+// ------------------------------------------------------------- small helpers
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_depth(int pending) {
+    // cp.async.wait_group takes an immediate
+    switch (pending) {
+        case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
+        case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
+        case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
+        case 3: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
+        case 4: asm volatile("cp.async.wait_group 4;" ::: "memory"); break;
+        default: asm volatile("cp.async.wait_group 5;" ::: "memory"); break;
+    }
+}
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t bf16x2_fma(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Barrier of the 128 epilogue threads that also returns whether any of them passed `pred`.
+__device__ __forceinline__ bool epi_any(bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, 1, 128, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(uint32_t(pred))
+        : "memory");
+    return r != 0;
+}
+
+// f16 pair -> bf16 pair (exact for the e4m3 values it is used on).
+__device__ __forceinline__ uint32_t f16x2_to_bf16x2(uint32_t h) {
+    __half2 hh;
+    memcpy(&hh, &h, 4);
+    const float2 f = __half22float2(hh);
+    return pack_bf162(f.x, f.y);
+}
+
+constexpr uint32_t kOne2 = 0x3F803F80u;   // bf16 (1, 1)
+constexpr uint32_t kM136x2 = 0xC308C308u; // bf16 (-136, -136)
+constexpr uint32_t kM128x2 = 0xC300C300u; // bf16 (-128, -128)
+
+// Waits for a phase of `bar` with a bound; gives up when another role has
+// already given up (abort flag) or after p.wait_cycles, recording the timeout.
+__device__ __forceinline__ bool tc_wait(uint32_t bar, uint32_t parity, volatile int* abort, long long limit) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (int it = 0;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 15) == 15) {
+            if (abort && *abort) return false;
+            if (clock64() - t0 > limit) {
+                atomicOr(&g_device_error, BQ_DEVERR_WAIT_TIMEOUT_BIT);
+                if (abort) *abort = 1;
+                return false;
+            }
+        }
+    }
+}
+
+// Weight row of lane r of unit u.
+__device__ __forceinline__ int tc_row(const TcParams& p, int u, int r) {
+    if (p.epi == BQ_EPI_SILU_MUL) return r < 64 ? u * 64 + r : (p.N >> 1) + u * 64 + (r - 64);
+    return u * 128 + r;
+}
+
+// CTA holding item i under the balanced split [c*T/G, (c+1)*T/G).
+__host__ __device__ __forceinline__ int tc_cta_of(long long i, int T, int G) {
+    return int(((i + 1) * G - 1) / T);
+}
+
+// ------------------------------------------------------------- weight stream
+// Issues the cp.async copies of row n's bytes of k-block kb into ring slot
+// `raw` (chunk c of every row at raw + c * 2048 + r * 16) and, for int4, its
+// (scale, zero) words into `sc` (group gi at sc + gi * 512 + r * 4).
+template <int FMT>
+__device__ __forceinline__ void tc_issue(const TcParams& p, int n, int kb, int r, uint32_t raw, uint32_t sc) {
+    const char* w = static_cast<const char*>(p.w);
+    if constexpr (FMT == BQ_W_INT4_TINYGEMM) {
+        // [N/8, K/128, 32 lanes, 4 words]: lanes 4(n%8) .. 4(n%8)+3 hold row n's 128 k of the block
+        const char* src = w + ((size_t(n >> 3) * p.KB + kb) * 32 + (n & 7) * 4) * 16;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) cp_async16(raw + c * kTcRawChunk + r * 16, src + c * 16);
+        const int g = p.group;
+        const int ngr = g < 128 ? 128 / g : 1;
+        const int g0 = g <= 128 ? kb * (128 / g) : kb / (g / 128);
+        const char* s = static_cast<const char*>(p.scale);
+        for (int gi = 0; gi < ngr; ++gi) cp_async4(sc + gi * 512 + r * 4, s + (size_t(g0 + gi) * p.N + n) * 4);
+    } else if constexpr (FMT == BQ_W_INT4_PLAIN) {
+        const char* src = w + size_t(n) * (p.K >> 1) + kb * 64;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) cp_async16(raw + c * kTcRawChunk + r * 16, src + c * 16);
+        cp_async4(sc + r * 4, static_cast<const char*>(p.scale) + (size_t(kb) * p.N + n) * 4);
+    } else if constexpr (FMT == BQ_W_BF16) {
+        const char* src = w + (size_t(n) * p.K + size_t(kb) * 128) * 2;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) cp_async16(raw + c * kTcRawChunk + r * 16, src + c * 16);
+    } else {  // fp8 / int8: one byte per weight
+        const char* src = w + size_t(n) * p.K + size_t(kb) * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) cp_async16(raw + c * kTcRawChunk + r * 16, src + c * 16);
+    }
+}
+
+// Dequantizes row r's block from the ring slot into bf16 pairs (low half =
+// even k) and stores them to TMEM columns col .. col+63 of the warp's lane.
+template <int FMT>
+__device__ __forceinline__ void tc_dequant(const TcParams& p, int r, uint32_t raw, uint32_t sc, uint32_t taddr) {
+    if constexpr (FMT == BQ_W_INT4_TINYGEMM) {
+        // word j of lane c, nibble pair i (bits 4i and 16 + 4i) holds the codes of
+        // k = 32 j + 8 i + 2 c and k + 1 (even k in the low nibble of the pair)
+        uint4 l[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) l[c] = lds128(raw + c * kTcRawChunk + r * 16);
+        const int g = p.group;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int gi = g == 32 ? j : g == 64 ? (j >> 1) : 0;
+            const uint32_t sz = lds32(sc + gi * 512 + r * 4);
+            const uint32_t s2 = prmt(sz, sz, 0x1010u), z2 = prmt(sz, sz, 0x3232u);
+            uint32_t o[16];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const uint32_t wj = j == 0 ? l[c].x : j == 1 ? l[c].y : j == 2 ? l[c].z : l[c].w;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const uint32_t q = bf16x2_fma(i4_bf16(wj >> (4 * i)), kOne2, kM136x2);  // q - 8, exact
+                    o[4 * i + c] = bf16x2_fma(q, s2, z2);  // (q - 8) * scale + zero, one rounding
+                }
+            }
+            tmem_st16(taddr + 16 * j, o);
+        }
+    } else if constexpr (FMT == BQ_W_INT4_PLAIN) {
+        // byte b of the row holds k = 2b (low nibble) and 2b + 1 (high nibble)
+        const uint32_t sz = lds32(sc + r * 4);
+        const uint32_t s2 = prmt(sz, sz, 0x1010u), m2 = prmt(sz, sz, 0x3232u);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint4 l = lds128(raw + c * kTcRawChunk + r * 16);
+            uint32_t o[16];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const uint32_t wt = t == 0 ? l.x : t == 1 ? l.y : t == 2 ? l.z : l.w;
+                const uint32_t lo = wt & 0x0F0F0F0Fu, hi = (wt >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    // bytes (lo.b, 0, hi.b, 0): a selector nibble with bit 3 set copies the sign of a byte < 16
+                    const uint32_t sel = b | ((8 | b) << 4) | ((4 + b) << 8) | ((12 + b) << 12);
+                    const uint32_t q = bf16x2_fma(prmt(lo, hi, sel) | 0x43004300u, kOne2, kM128x2);  // q, exact
+                    o[4 * t + b] = bf16x2_fma(q, s2, m2);  // q * scale + min, one rounding
+                }
+            }
+            tmem_st16(taddr + 16 * c, o);
+        }
+    } else if constexpr (FMT == BQ_W_BF16) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            uint32_t o[16];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const uint4 l = lds128(raw + (4 * j + c) * kTcRawChunk + r * 16);
+                o[4 * c] = l.x;
+                o[4 * c + 1] = l.y;
+                o[4 * c + 2] = l.z;
+                o[4 * c + 3] = l.w;
+            }
+            tmem_st16(taddr + 16 * j, o);
+        }
+    } else {
+        // fp8 / int8: chunk c holds k = 16 c .. 16 c + 15; bf16 represents both exactly
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            uint32_t o[16];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint4 l = lds128(raw + (2 * j + h) * kTcRawChunk + r * 16);
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const uint32_t wt = t == 0 ? l.x : t == 1 ? l.y : t == 2 ? l.z : l.w;
+                    if constexpr (FMT == BQ_W_FP8_E4M3) {
+                        o[8 * h + 2 * t] = f16x2_to_bf16x2(e4m3x2_to_f16x2(uint16_t(wt & 0xFFFFu)));
+                        o[8 * h + 2 * t + 1] = f16x2_to_bf16x2(e4m3x2_to_f16x2(uint16_t(wt >> 16)));
+                    } else {
+                        const int v = int(wt);
+                        o[8 * h + 2 * t] = pack_bf162(float((v << 24) >> 24), float((v << 16) >> 24));
+                        o[8 * h + 2 * t + 1] = pack_bf162(float((v << 8) >> 24), float(v >> 24));
+                    }
+                }
+            }
+            tmem_st16(taddr + 16 * j, o);
+        }
+    }
+}
+
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void sts_zero16(uint32_t a) {
+    asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0u) : "memory");
+}
+
+// Segment s of a CTA: the run of its items inside one unit.
+struct TcSeg {
+    int unit, kb0, kb1;  // k-blocks [kb0, kb1) of `unit`
+};
+__device__ __forceinline__ TcSeg tc_seg_at(const TcParams& p, int item, int i1) {
+    const int u = item / p.KB, kb0 = item % p.KB;
+    const int end = min(i1, (u + 1) * p.KB);
+    return TcSeg{u, kb0, kb0 + (end - item)};
+}
+
+// Final value of one output element of lane r (weight row n) for activation row m.
+__device__ __forceinline__ void tc_store(const TcParams& p, int m, int n, float v) {
+    if (p.epi == BQ_EPI_ADD_RESIDUAL) v += load_act(p.residual, m * p.ldr + n, p.res_dtype);
+    store_act(p.out, m * p.ldo + n, p.out_dtype, v);
+}
+
+// Finishes 16 activation rows (16 mc .. 16 mc + 15) of lane r's values v.
+// Called by all 128 epilogue threads together (SiLU*up exchanges through xch).
+__device__ __forceinline__ void tc_finish16(const TcParams& p, int u, int r, int n, int mc, float rs, float bi,
+                                            float (&v)[16], float* xch) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = fmaf(v[i], rs, bi);
+    if (p.epi == BQ_EPI_SILU_MUL) {
+        if (r >= 64) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) xch[i * 64 + (r - 64)] = v[i];
+        }
+        epi_sync();
+        if (r < 64) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const int m = 16 * mc + i;
+                if (m < p.M) store_act(p.out, m * p.ldo + u * 64 + r, p.out_dtype, silu(v[i]) * xch[i * 64 + r]);
+            }
+        }
+        epi_sync();
+    } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int m = 16 * mc + i;
+            if (m < p.M) tc_store(p, m, n, v[i]);
+        }
+    }
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(const __grid_constant__ TcParams p) {
+    extern __shared__ __align__(1024) unsigned char smem[];
+    const uint32_t sbase = smem_u32(smem);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = gridDim.x, cta = blockIdx.x;
+    const int i0 = int((long long)cta * p.items / G), i1 = int((long long)(cta + 1) * p.items / G);
+    const int nb = i1 - i0;
+
+    // barriers: full[4] (A stage dequantized), empty[4] (stage consumed by the MMAs),
+    // xfull[4] (X stage loaded), accf[2] (accumulator ready), acce[2] (accumulator read), done
+    const uint32_t bars = sbase + p.sm_bar;
+    const uint32_t bar_full = bars, bar_empty = bars + 32, bar_xfull = bars + 64, bar_accf = bars + 96,
+                   bar_acce = bars + 112, bar_done = bars + 128;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + p.sm_bar + 136);
+    volatile int* abort = reinterpret_cast<volatile int*>(smem + p.sm_bar + 140);
+    volatile int* last_flag = reinterpret_cast<volatile int*>(smem + p.sm_bar + 144);
+    const long long lim = p.wait_cycles;
+
+    if (threadIdx.x == 0) {
+        for (int a = 0; a < kTcStages; ++a) {
+            mbar_init(bar_full + 8 * a, 128);
+            mbar_init(bar_empty + 8 * a, 1);
+            mbar_init(bar_xfull + 8 * a, 32);
+        }
+        for (int d = 0; d < 2; ++d) {
+            mbar_init(bar_accf + 8 * d, 1);
+            mbar_init(bar_acce + 8 * d, 128);
+        }
+        mbar_init(bar_done, 1);
+        *abort = 0;
+        fence_barrier_init();
+    }
+    // dequantizers: start the weight stream first (static data, before the PDL wait)
+    const int grp = warp >> 2, r = ((warp & 3) << 5) | lane;
+    const int RD = p.raw_depth;
+    const uint32_t raw_g = sbase + p.sm_raw + grp * RD * p.raw_slot;
+    const uint32_t sc_g = sbase + p.sm_sc + grp * RD * p.sc_slot;
+    if (warp < 8) {
+        for (int jj = 0; jj < RD - 1; ++jj) {
+            const int b = grp + 2 * jj;
+            if (b < nb) {
+                const int item = i0 + b;
+                tc_issue<FMT>(p, tc_row(p, item / p.KB, r), item % p.KB, r, raw_g + jj * p.raw_slot,
+                              sc_g + jj * p.sc_slot);
+            }
+            cp_async_commit();
+        }
+    }
+    // activation rows M .. n_mma of every X stage stay zero (the loader never writes them)
+    {
+        const int pad = (p.n_mma - p.M) * 16;
+        for (int idx = threadIdx.x; idx < kTcStages * pad; idx += kTcThreads) {
+            const int st = idx / pad, rem = idx - st * pad;
+            const int m = p.M + (rem >> 4), c = rem & 15;
+            sts_zero16(sbase + p.sm_x + st * (p.n_mma * 256) + (m >> 3) * kTcXGroup + c * 128 + (m & 7) * 16);
+        }
+        fence_proxy_async();
+    }
+    if (warp == kTcMmaWarp) tmem_alloc(smem_u32(tmem_slot), kTcTmemCols);
+    pdl_launch_dependents();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp < 8) {
+        // ---------------------------------------------------------- dequantizers
+        const uint32_t lane_base = tmem + (uint32_t((warp & 3) * 32) << 16);
+        int j = 0;
+        for (int b = grp; b < nb; b += 2, ++j) {
+            {  // keep RD - 1 blocks of this group in flight
+                const int bn = b + 2 * (RD - 1);
+                if (bn < nb) {
+                    const int item = i0 + bn, jn = (j + RD - 1) % RD;
+                    tc_issue<FMT>(p, tc_row(p, item / p.KB, r), item % p.KB, r, raw_g + jn * p.raw_slot,
+                                  sc_g + jn * p.sc_slot);
+                }
+                cp_async_commit();
+            }
+            cp_async_wait_depth(RD - 1);  // this thread's copies of block b have landed
+            const int a = b & 3;
+            if (b >= kTcStages) {  // the decision is warp-uniform: tcgen05.st is a warp-wide instruction
+                const bool ok = tc_wait(bar_empty + 8 * a, ((b >> 2) + 1) & 1, abort, lim);
+                if (!__all_sync(0xffffffffu, ok)) break;
+            }
+            tc_fence_after();
+            const int slot = j % RD;
+            tc_dequant<FMT>(p, r, raw_g + slot * p.raw_slot, sc_g + slot * p.sc_slot,
+                            lane_base + kTcACol0 + kTcACols * a);
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(bar_full + 8 * a);
+        }
+        cp_async_wait_depth(0);
+    } else if (warp == kTcXWarp) {
+        // ---------------------------------------------------------- activation loader
+        pdl_wait();  // x is written by the previous kernel
+        const int rows8 = p.n_mma >> 3;
+        for (int b = 0; b <= nb; ++b) {
+            if (b < nb) {
+                const int a = b & 3;
+                if (b >= kTcStages && !tc_wait(bar_empty + 8 * a, ((b >> 2) + 1) & 1, abort, lim)) break;
+                const int kb = (i0 + b) % p.KB;
+                const uint32_t xs = sbase + p.sm_x + a * (p.n_mma * 256);
+                // lane -> (row m = 8 g + lane % 8, k-chunk 4 q + lane / 8): 4 x 128 contiguous bytes per store
+                for (int t = 0; t < rows8 * 4; ++t) {
+                    const int g8 = t >> 2, q = t & 3;
+                    const int m = 8 * g8 + (lane & 7), c = 4 * q + (lane >> 3);
+                    if (m < p.M)
+                        cp_async16(xs + g8 * kTcXGroup + c * 128 + (lane & 7) * 16,
+                                   p.x + m * p.ldx + kb * 128 + c * 8);
+                }
+            }
+            cp_async_commit();
+            if (b > 0) {  // block b - 1 has landed: publish it to the tensor cores (async proxy)
+                cp_async_wait_depth(b < nb ? 1 : 0);
+                fence_proxy_async();
+                mbar_arrive(bar_xfull + 8 * ((b - 1) & 3));
+            }
+        }
+        cp_async_wait_depth(0);
+    } else if (warp == kTcMmaWarp) {
+        // ---------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            int s = 0;
+            for (int b = 0; b < nb;) {
+                const TcSeg sg = tc_seg_at(p, i0 + b, i1);
+                const int d = s & 1;
+                bool ok = true;
+                if (s >= 2) ok = tc_wait(bar_acce + 8 * d, ((s >> 1) + 1) & 1, abort, lim);
+                for (int kb = sg.kb0; ok && kb < sg.kb1; ++kb, ++b) {
+                    const int a = b & 3;
+                    ok = tc_wait(bar_full + 8 * a, (b >> 2) & 1, abort, lim) &&
+                         tc_wait(bar_xfull + 8 * a, (b >> 2) & 1, abort, lim);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t xs = sbase + p.sm_x + a * (p.n_mma * 256);
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        tc_mma(tmem + d * kTcAccCols, tmem + kTcACol0 + kTcACols * a + 8 * k, tc_bdesc(xs + 256 * k),
+                               p.idesc, (kb > sg.kb0 || k > 0) ? 1u : 0u);
+                    tc_commit(bar_empty + 8 * a);
+                }
+                if (!ok) break;
+                tc_commit(bar_accf + 8 * d);
+                ++s;
+            }
+            tc_commit(bar_done);  // every MMA issued above has finished once this completes
+            tc_wait(bar_done, 0, nullptr, lim);  // also after an abort: TMEM is freed only when they are done
+        }
+        __syncwarp();
+    } else {
+        // ---------------------------------------------------------- epilogue
+        const int q = warp & 3;
+        const int re = (q << 5) | lane;  // TMEM lane = weight row within the unit
+        const uint32_t lane_base = tmem + (uint32_t(q * 32) << 16);
+        float* xch = reinterpret_cast<float*>(smem + p.sm_xch);
+        const int n_chunks = p.n_mma >> 4;
+        pdl_wait();  // outputs, residual rows and the workspace are shared with the previous kernel
+        int s = 0;
+        for (int b = 0; b < nb; ++s) {
+            const TcSeg sg = tc_seg_at(p, i0 + b, i1);
+            b += sg.kb1 - sg.kb0;
+            const int d = s & 1;
+            const int n = tc_row(p, sg.unit, re);
+            float rs = 1.f;
+            if (FMT == BQ_W_FP8_E4M3 || FMT == BQ_W_INT8) {
+                rs = static_cast<const float*>(p.scale)[n];
+                if (p.flags & BQ_FLAG_SCALE_ROUND_BF16) rs = __bfloat162float(__float2bfloat16_rn(rs));
+            }
+            const float bi = p.bias ? load_act(p.bias, n, p.out_dtype) : 0.f;
+            const bool owned = sg.kb0 == 0 && sg.kb1 == p.KB;
+            // uniform over the 128 epilogue threads (warp-wide tcgen05.ld, named barriers below)
+            if (epi_any(!tc_wait(bar_accf + 8 * d, (s >> 1) & 1, abort, lim))) break;
+            tc_fence_after();
+            if (owned) {
+                for (int mc = 0; mc < n_chunks; ++mc) {
+                    float v[16];
+                    tmem_ld16(lane_base + d * kTcAccCols + 16 * mc, v);
+                    tc_finish16(p, sg.unit, re, n, mc, rs, bi, v, xch);
+                }
+                tc_fence_before();
+                mbar_arrive(bar_acce + 8 * d);
+                continue;
+            }
+            // one piece of a shared unit: publish it, the last of the unit's CTAs finishes
+            const long long first = (long long)sg.unit * p.KB;
+            const int c_lo = tc_cta_of(first, p.items, G), c_hi = tc_cta_of(first + p.KB - 1, p.items, G);
+            const int pieces = c_hi - c_lo + 1, piece = cta - c_lo;
+            float* part = p.part + size_t(sg.unit) * p.max_pieces * p.n_mma * 128;
+            for (int mc = 0; mc < n_chunks; ++mc) {
+                float v[16];
+                tmem_ld16(lane_base + d * kTcAccCols + 16 * mc, v);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) part[(size_t(piece) * p.n_mma + 16 * mc + i) * 128 + re] = v[i];
+            }
+            tc_fence_before();
+            mbar_arrive(bar_acce + 8 * d);
+            __threadfence();
+            epi_sync();
+            if (re == 0) *last_flag = atomicAdd(&p.counters[sg.unit], 1u) == unsigned(pieces - 1);
+            epi_sync();
+            if (*last_flag) {
+                __threadfence();
+                for (int mc = 0; mc < n_chunks; ++mc) {
+                    float v[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) v[i] = 0.f;
+                    for (int pc = 0; pc < pieces; ++pc) {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) v[i] += __ldcg(&part[(size_t(pc) * p.n_mma + 16 * mc + i) * 128 + re]);
+                    }
+                    tc_finish16(p, sg.unit, re, n, mc, rs, bi, v, xch);
+                }
+                if (re == 0) p.counters[sg.unit] = 0u;  // ready for the next call
+            }
+            epi_sync();  // last_flag is rewritten by the next segment
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == kTcMmaWarp) tmem_dealloc(tmem, kTcTmemCols);
+}
+
+// RMSNorm of the activation rows into the workspace: one block per row,
+// out = bf16(x * rsqrt(mean(x^2) + eps) * gamma) with fp32 math (the
+// reference's rmsnorm_kernel, models/fused/kernels.py:541-557). Launched as a
+// programmatic dependent: the GEMV after it starts its weight stream early.
+__global__ void __launch_bounds__(256) tc_rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
+                                                         const __nv_bfloat16* __restrict__ g,
+                                                         __nv_bfloat16* __restrict__ out, int K, float eps) {
+    __shared__ float red[8];
+    pdl_launch_dependents();
+    pdl_wait();
+    const __nv_bfloat16* xr = x + blockIdx.x * ldx;
+    float ss = 0.f;
+    for (int k = threadIdx.x; k < K; k += 256) {
+        const float v = __bfloat162float(xr[k]);
+        ss = fmaf(v, v, ss);
+    }
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tot += red[i];
+    const float inv = 1.0f / sqrtf(tot / float(K) + eps);
+    __nv_bfloat16* orow = out + size_t(blockIdx.x) * K;
+    for (int k = threadIdx.x; k < K; k += 256)
+        orow[k] = __float2bfloat16_rn(__bfloat162float(xr[k]) * inv * __bfloat162float(g[k]));
+}
+
+const void* tc_kernel_for(int fmt) {
+    switch (fmt) {
+        case BQ_W_INT4_TINYGEMM: return reinterpret_cast<const void*>(gemv_tc_kernel<BQ_W_INT4_TINYGEMM>);
+        case BQ_W_INT4_PLAIN: return reinterpret_cast<const void*>(gemv_tc_kernel<BQ_W_INT4_PLAIN>);
+        case BQ_W_FP8_E4M3: return reinterpret_cast<const void*>(gemv_tc_kernel<BQ_W_FP8_E4M3>);
+        case BQ_W_INT8: return reinterpret_cast<const void*>(gemv_tc_kernel<BQ_W_INT8>);
+        case BQ_W_BF16: return reinterpret_cast<const void*>(gemv_tc_kernel<BQ_W_BF16>);
+        default: return nullptr;
+    }
+}
+
+}  // namespace
+
+// Plans the tensor-core path for `d`; returns false when it does not apply
+// (row count, activation dtype, N, group or shared memory).
+bool plan_tc(const bq_gemv_desc* d, TcPlan* pl) {
+    if (d->flags & BQ_FLAG_NO_TC) return false;
+    if (d->M < kTcMinRows || d->M > kTcMaxRows || d->x_dtype != BQ_DT_BF16 || d->N % 128 != 0) return false;
+    if (d->wfmt == BQ_W_INT4_PLAIN && d->group != 128) return false;
+    if (d->wfmt == BQ_W_INT4_TINYGEMM && d->group != 32 && d->group != 64 && d->group != 128 && d->group != 256)
+        return false;
+    if (!tc_kernel_for(d->wfmt)) return false;
+    const DeviceInfo* di = device_info();
+    if (!di) return false;
+    TcPlan p{};
+    p.n_mma = (d->M + 15) & ~15;
+    p.KB = d->K / 128;
+    p.units = d->N / 128;
+    p.items = p.units * p.KB;
+    p.grid = std::min(di->sm_count, p.items);
+    const bool int4 = d->wfmt == BQ_W_INT4_TINYGEMM || d->wfmt == BQ_W_INT4_PLAIN;
+    p.raw_slot = 128u * uint32_t(tc_row_bytes(d->wfmt));
+    p.sc_slot = int4 ? uint32_t(kTcScSlot) : 0u;
+    p.sm_x = 0;
+    const uint32_t x_bytes = uint32_t(kTcStages) * uint32_t(p.n_mma) * 256u;
+    const uint32_t xch = d->epilogue == BQ_EPI_SILU_MUL ? 16u * 64u * 4u : 0u;
+    const uint32_t fixed = x_bytes + xch + 256u;
+    int rd = 0;
+    for (int c = 6; c >= 2; --c)
+        if (fixed + 2u * uint32_t(c) * (p.raw_slot + p.sc_slot) <= uint32_t(di->smem_optin)) {
+            rd = c;
+            break;
+        }
+    if (!rd) return false;
+    p.raw_depth = rd;
+    p.sm_raw = x_bytes;
+    p.sm_sc = p.sm_raw + 2u * rd * p.raw_slot;
+    p.sm_xch = p.sm_sc + 2u * rd * p.sc_slot;
+    p.sm_bar = p.sm_xch + xch;
+    p.sm_total = p.sm_bar + 256u;
+    // pieces of the units that several CTAs share
+    p.max_pieces = 1;
+    for (int u = 0; u < p.units; ++u) {
+        const long long first = (long long)u * p.KB;
+        const int pcs = tc_cta_of(first + p.KB - 1, p.items, p.grid) - tc_cta_of(first, p.items, p.grid) + 1;
+        p.max_pieces = std::max(p.max_pieces, pcs);
+    }
+    int64_t off = kCounterBytes;
+    p.part_off = off;
+    if (p.max_pieces > 1) off += int64_t(p.units) * p.max_pieces * p.n_mma * 128 * 4;
+    off = (off + 255) & ~int64_t(255);
+    p.xn_off = off;
+    if (d->gamma) off += int64_t(d->M) * d->K * 2;
+    p.ws_bytes = off;
+    *pl = p;
+    return true;
+}
+
+int launch_tc(const bq_gemv_desc* d, const TcPlan& pl, void* workspace, cudaStream_t stream) {
+    const void* fn = tc_kernel_for(d->wfmt);
+    if (!fn) return set_error(BQ_ERR_FORMAT, "no tensor-core GEMV for format %d", d->wfmt);
+    if (!workspace) return set_error(BQ_ERR_WORKSPACE, "the tensor-core GEMV needs a workspace");
+    char* ws = static_cast<char*>(workspace);
+    const __nv_bfloat16* x = static_cast<const __nv_bfloat16*>(d->x);
+    long long ldx = d->ldx;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    const bool pdl = (d->flags & BQ_FLAG_PDL) != 0;
+    if (d->gamma) {
+        __nv_bfloat16* xn = reinterpret_cast<__nv_bfloat16*>(ws + pl.xn_off);
+        cudaLaunchConfig_t cfg;
+        std::memset(&cfg, 0, sizeof(cfg));
+        cfg.gridDim = dim3(d->M);
+        cfg.blockDim = dim3(256);
+        cfg.stream = stream;
+        if (pdl) {
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+        }
+        const __nv_bfloat16* g = static_cast<const __nv_bfloat16*>(d->gamma);
+        const int K = d->K;
+        const float eps = d->eps;
+        void* args[] = {&x, &ldx, &g, &xn, const_cast<int*>(&K), const_cast<float*>(&eps)};
+        cudaError_t e = cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(tc_rmsnorm_kernel), args);
+        if (e != cudaSuccess) return set_error(BQ_ERR_CUDA, "RMSNorm launch failed: %s", cudaGetErrorString(e));
+        x = xn;
+        ldx = d->K;
+    } else if ((reinterpret_cast<uintptr_t>(x) & 15) || (ldx * 2) % 16) {
+        return set_error(BQ_ERR_ALIGN, "the tensor-core GEMV needs 16-byte aligned activation rows");
+    }
+    TcParams p;
+    std::memset(&p, 0, sizeof(p));
+    p.w = d->w;
+    p.scale = d->scale;
+    p.bias = d->bias;
+    p.residual = d->residual;
+    p.out = d->out;
+    p.x = x;
+    p.ldx = ldx;
+    p.ldr = d->ldr;
+    p.ldo = d->ldo;
+    p.M = d->M;
+    p.N = d->N;
+    p.K = d->K;
+    p.KB = pl.KB;
+    p.group = d->group;
+    p.epi = d->epilogue;
+    p.out_dtype = d->out_dtype;
+    p.res_dtype = d->res_dtype;
+    p.flags = d->flags;
+    p.units = pl.units;
+    p.items = pl.items;
+    p.n_mma = pl.n_mma;
+    p.max_pieces = pl.max_pieces;
+    p.raw_depth = pl.raw_depth;
+    // kind::f16, fp32 accumulate, bf16 A and B, both K-major, N = n_mma, M = 128
+    p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(pl.n_mma >> 3) << 17) | (uint32_t(128 >> 4) << 24);
+    p.wait_cycles = kWaitCycles;
+    p.part = reinterpret_cast<float*>(ws + pl.part_off);
+    p.counters = reinterpret_cast<unsigned*>(ws);
+    p.sm_x = pl.sm_x;
+    p.sm_raw = pl.sm_raw;
+    p.sm_sc = pl.sm_sc;
+    p.sm_xch = pl.sm_xch;
+    p.sm_bar = pl.sm_bar;
+    p.sm_total = pl.sm_total;
+    p.raw_slot = pl.raw_slot;
+    p.sc_slot = pl.sc_slot;
+    int rc = ensure_smem_attr(fn, pl.sm_total);
+    if (rc) return rc;
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(pl.grid);
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = pl.sm_total;
+    cfg.stream = stream;
+    if (pdl || d->gamma) {  // after the norm kernel always: its rows are waited for in the kernel
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    void* args[] = {&p};
+    cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
+    if (e != cudaSuccess) return set_error(BQ_ERR_CUDA, "tensor-core GEMV launch failed: %s", cudaGetErrorString(e));
+    return BQ_OK;
+}
+
+}  // namespace bq

@@ -80,6 +80,8 @@ extern "C" {
                                        streaming starts before the previous kernel ends  */
 #define BQ_FLAG_SCALE_ROUND_BF16 2u /* int8: round the per-row scale to bf16 first, as
                                        Int8Linear does for bf16 activations              */
+#define BQ_FLAG_NO_TC 4u            /* keep 17..128-row calls on the mma.sync kernel (row
+                                       blocks of 16) instead of the tcgen05 kernel        */
 
 typedef struct bq_gemv_desc {
     int32_t M;         /* activation rows (decode batch), >= 1 */
@@ -122,7 +124,13 @@ int32_t bq_gemv_workspace_bytes(const bq_gemv_desc* desc, size_t* bytes);
 /* out = epilogue( rmsnorm(x) @ dequant(w)^T ), fp32 accumulation.
  * Replaces models/fused/kernels.py:334-351 (rms_gemv + both kernels),
  * models/int4_linear.py:99-109, models/fp8_linear.py:68-83 (weight-only),
- * models/int8_linear.py:50-53. */
+ * models/int8_linear.py:50-53.
+ * Two kernels: up to 16 rows per pass on mma.sync tiles with in-register
+ * dequantization (more rows: passes of 16, each streaming the weights again);
+ * 17..128 bf16 rows with N % 128 == 0 on tcgen05 tiles (dequantized weights
+ * in tensor memory, the rows in shared memory, weights read once; with an
+ * RMSNorm the normalized rows go through the workspace first) unless
+ * BQ_FLAG_NO_TC is set. */
 int32_t bq_gemv(const bq_gemv_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
 
 /* bq_gemv with host-side input and output: x_host (M rows of K values, dense,
