@@ -94,7 +94,8 @@ def measured_peak():
 
 
 # DRAM bytes (read + write) of one gemv3_kernel launch on this workload (mean of
-# two launches), from the ncu capture summarised in profiles/gemv3_int4_plain_config1.md.
+# two launches), from an ncu capture of this workload (dram__bytes_read.sum +
+# dram__bytes_write.sum); re-captured whenever the kernel changes.
 NCU_TRAFFIC_BYTES = 6_769_920
 
 

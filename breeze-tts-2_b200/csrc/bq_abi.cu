@@ -156,6 +156,7 @@ int32_t bq_device_status_clear(int32_t device) {
     if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(uint32_t));
     cudaSetDevice(prev);
     if (e != cudaSuccess) return set_error(BQ_ERR_CUDA, "clearing device status: %s", cudaGetErrorString(e));
+    noalloc_forget(device);  // a timed-out kernel may have left the built-in scratch's counters set
     return BQ_OK;
 }
 
@@ -190,7 +191,7 @@ int32_t bq_gemv(const bq_gemv_desc* desc, void* workspace, size_t workspace_byte
     if (di->major != 10) return set_error(BQ_ERR_DEVICE, "sm_%d%d device: this library is built for sm_100a", di->major, di->minor);
     TcPlan tp;
     if (plan_tc(desc, &tp)) {
-        if (!workspace || int64_t(workspace_bytes) < tp.ws_bytes)
+        if (tp.ws_bytes > 0 && (!workspace || int64_t(workspace_bytes) < tp.ws_bytes))
             return set_error(BQ_ERR_WORKSPACE, "workspace of %zu bytes given, %lld needed", workspace_bytes,
                              (long long)tp.ws_bytes);
         if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)

@@ -19,13 +19,15 @@
 //    the activation fragments of a k-block are loaded once for all its units;
 //    items outside the CTA's range are zero-filled and computed branch-free.
 //  * Staging is row-parallel: lanes are split into row groups (32 / rows per
-//    row, rounded to a power of two) that reduce sum-of-squares and max|x*g|
-//    with a few shuffles, then rewrite the row as f16 scaled by a per-(warp,
-//    row) power of two. RMSNorm's 1/rms is applied to the accumulator.
-//  * int4 magic offsets (1024 + q, 1024 + 16 q) are removed once per group:
-//    an MMA with a 0/1 indicator operand gives the low- and high-nibble
-//    activation sums of each column; they are computed once per k-block
-//    after staging and kept in shared memory.
+//    row, rounded to a power of two). int4 and bf16 weights take bf16
+//    activations: one pass rewrites x*gamma as bf16 in place and accumulates
+//    each lane's sum of squares. fp8 and int8 weights take f16 activations
+//    scaled by a per-(warp, row) power of two from max|x*gamma|. RMSNorm's
+//    1/rms is applied to the accumulator after the main loop.
+//  * int4 nibbles become bf16 128 + q in registers (magic exponent 0x4300);
+//    the offset is removed once per group: an MMA with an all-ones operand
+//    gives each column's activation sum over the group, computed once per
+//    k-block after staging and kept in shared memory.
 #pragma once
 
 #include <cuda_runtime.h>

@@ -45,11 +45,14 @@ int launch_gemv3(const bq_gemv_desc* d, const Gemv3Plan& pl, int row0, void* wor
 
 // Tensor-core GEMV (tcgen05, weights read once for 17..128 rows).
 struct TcPlan {
-    int n_mma, KB, units, items, grid, max_pieces, raw_depth;
-    uint32_t raw_slot, sc_slot, sm_x, sm_raw, sm_sc, sm_xch, sm_bar, sm_total;
-    int64_t part_off, xn_off, ws_bytes;
+    int n_mma, KB, units, C, grid, raw_depth;
+    uint32_t raw_slot, sc_slot, sm_x, sm_raw, sm_sc, sm_bar, sm_total, red_pitch;
+    int64_t xn_off, ws_bytes;
 };
 bool plan_tc(const bq_gemv_desc* d, TcPlan* pl);
 int launch_tc(const bq_gemv_desc* d, const TcPlan& pl, void* workspace, cudaStream_t stream);
+
+// The no-alloc GEMV's built-in scratch: clear its counters again on the next call on `dev`.
+void noalloc_forget(int dev);
 
 }  // namespace bq

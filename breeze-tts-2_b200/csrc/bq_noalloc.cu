@@ -29,6 +29,10 @@
 //    after the library's device image was reloaded (a cudaDeviceReset),
 //    clears the counters with a blocking memset: make that call before any
 //    stream capture.
+//  * A kernel whose bounded wait ran out (BQ_DEVERR_WAIT_TIMEOUT) may leave
+//    counters non-zero. bq_device_status_clear on that device marks the
+//    array for clearing again, so the next call here starts from zeroed
+//    counters (the same blocking memset: outside stream capture).
 //  * No cudaMalloc, cudaFree or allocating library routine is called.
 #include <cuda_runtime.h>
 
@@ -72,6 +76,14 @@ static int noalloc_scratch(void** out) {
     }
     *out = p;
     return BQ_OK;
+}
+
+// Called by bq_device_status_clear: the next call on `dev` clears the
+// counters again (after a timeout they may not have returned to zero).
+void noalloc_forget(int dev) {
+    if (dev < 0 || dev >= kMaxDevices) return;
+    std::lock_guard<std::mutex> lk(g_na_mu);
+    g_na_cleared[dev] = nullptr;
 }
 
 }  // namespace bq

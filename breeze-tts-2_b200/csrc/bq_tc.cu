@@ -14,23 +14,27 @@
 //              MMA's A operand lives in TMEM, so dequantized weights never
 //              touch shared memory.
 //   warp 8     activation loader: cp.async of the k-block's X tile (bf16
-//              rows, K-major core matrices) into a shared-memory stage,
-//              completion through cp.async.mbarrier.arrive.
+//              rows, K-major core matrices) into one of four shared-memory
+//              stages; each lane's copies complete on the stage's mbarrier
+//              (cp.async.mbarrier.arrive.noinc), so the loader runs up to
+//              four k-blocks ahead of the tensor cores.
 //   warp 9     allocates TMEM; one thread issues tcgen05.mma kind::f16
 //              (M = 128 weight rows, N = rows rounded up to 16, K = 16; A from
 //              TMEM, B from shared memory, fp32 accumulators in TMEM) and
-//              tcgen05.commit to free stages / publish accumulators.
-//   warps 10-13 epilogue, one per TMEM lane quadrant: tcgen05.ld of the
-//              accumulator, per-row scale, bias, SiLU*up or + residual, cast.
-// TMEM: 2 accumulators (columns 0 and 128) so a segment's epilogue overlaps
-// the next segment's MMAs; 4 A stages of 64 columns at 256..511.
+//              tcgen05.commit to free stages / publish the accumulator.
+//   warps 10-13 copy the accumulator (tcgen05.ld, one TMEM lane quadrant per
+//              warp) into shared memory once the last MMA is done.
 //
-// Work split (stream-K): a unit is 128 weight rows (SiLU*up: 64 gate rows and
-// the matching 64 up rows), an item is (unit, 128-k block); CTA c takes the
-// contiguous item range [c*T/G, (c+1)*T/G) in unit-major order. A unit covered
-// by one CTA is finished from TMEM; otherwise every covering CTA writes its
-// fp32 piece to the workspace and the last to arrive sums the pieces in
-// piece order (deterministic) and finishes the unit.
+// Work split: a unit is 128 weight rows (SiLU*up: 64 gate rows and the
+// matching 64 up rows). The C CTAs of unit u form a thread-block cluster;
+// cluster rank r takes the k-blocks [r KB / C, (r + 1) KB / C). C is chosen so
+// that units x C fills the SMs in one wave (O and down projections: 16 units
+// x 8 slices; gate+up: 128 units x 1). After a cluster barrier every CTA sums
+// its share of the unit's rows over the C partial accumulators in rank order
+// (distributed shared memory; deterministic), applies the per-row scale,
+// bias, SiLU*up or residual, and stores; a second barrier keeps each CTA's
+// shared memory alive until the others have read it. No global scratch and
+// no cross-CTA counters.
 //
 // With an RMSNorm the rows are normalized first by a short kernel into the
 // workspace (bf16 x * rstd * gamma, as models/fused/kernels.py:541
@@ -41,7 +45,11 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <array>
 #include <cstring>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "bq_device.cuh"
 #include "bq_host.h"
@@ -55,8 +63,7 @@ constexpr int kTcXWarp = 8;
 constexpr int kTcMmaWarp = 9;
 constexpr int kTcStages = 4;       // A (TMEM) and X (shared) stages, indexed by block % 4
 constexpr int kTcTmemCols = 512;
-constexpr int kTcAccCols = 128;    // columns per accumulator (N <= 128)
-constexpr int kTcACol0 = 256;      // A stage a at columns 256 + 64 a
+constexpr int kTcACol0 = 256;      // A stage a at columns 256 + 64 a (accumulator at columns 0..N-1)
 constexpr int kTcACols = 64;       // 128 bf16 k-values of one row = 64 32-bit columns
 constexpr int kTcXGroup = 2048;    // 8 activation rows x 16 k-chunks of 16 B (core matrices)
 constexpr int kTcRawChunk = 2048;  // one 16-byte chunk for each of the 128 rows
@@ -74,12 +81,10 @@ struct TcParams {
     long long ldx, ldr, ldo;
     int M, N, K, KB, group, epi, out_dtype, res_dtype;
     unsigned flags;
-    int units, items, n_mma, max_pieces, raw_depth;
+    int C, n_mma, raw_depth;
     unsigned idesc;
     long long wait_cycles;
-    float* part;
-    unsigned* counters;
-    unsigned sm_x, sm_raw, sm_sc, sm_xch, sm_bar, sm_total;
+    unsigned sm_x, sm_raw, sm_sc, sm_bar, sm_total, red_pitch;
     unsigned raw_slot, sc_slot;  // bytes per ring slot
 };
 
@@ -184,7 +189,6 @@ __device__ __forceinline__ uint32_t bf16x2_fma(uint32_t a, uint32_t b, uint32_t 
     asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
     return d;
 }
-__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 // Barrier of the 128 epilogue threads that also returns whether any of them passed `pred`.
 __device__ __forceinline__ bool epi_any(bool pred) {
     uint32_t r;
@@ -233,11 +237,6 @@ __device__ __forceinline__ bool tc_wait(uint32_t bar, uint32_t parity, volatile 
 __device__ __forceinline__ int tc_row(const TcParams& p, int u, int r) {
     if (p.epi == BQ_EPI_SILU_MUL) return r < 64 ? u * 64 + r : (p.N >> 1) + u * 64 + (r - 64);
     return u * 128 + r;
-}
-
-// CTA holding item i under the balanced split [c*T/G, (c+1)*T/G).
-__host__ __device__ __forceinline__ int tc_cta_of(long long i, int T, int G) {
-    return int(((i + 1) * G - 1) / T);
 }
 
 // ------------------------------------------------------------- weight stream
@@ -368,49 +367,38 @@ __device__ __forceinline__ void sts_zero16(uint32_t a) {
     asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0u) : "memory");
 }
 
-// Segment s of a CTA: the run of its items inside one unit.
-struct TcSeg {
-    int unit, kb0, kb1;  // k-blocks [kb0, kb1) of `unit`
-};
-__device__ __forceinline__ TcSeg tc_seg_at(const TcParams& p, int item, int i1) {
-    const int u = item / p.KB, kb0 = item % p.KB;
-    const int end = min(i1, (u + 1) * p.KB);
-    return TcSeg{u, kb0, kb0 + (end - item)};
+// Cluster barrier of every thread of every CTA of the cluster: writes to
+// shared memory before the arrive are visible to all after the wait.
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t dsmem_addr(uint32_t a, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float4 dsmem_ld4(uint32_t a) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ int dsmem_ld_s32(uint32_t a) {
+    int v;
+    asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+    return v;
+}
+// This thread's cp.async copies issued so far complete one arrival on `bar`.
+__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
 }
 
-// Final value of one output element of lane r (weight row n) for activation row m.
+// Output of activation row m for weight row n (unit-relative row r), value v.
 __device__ __forceinline__ void tc_store(const TcParams& p, int m, int n, float v) {
     if (p.epi == BQ_EPI_ADD_RESIDUAL) v += load_act(p.residual, m * p.ldr + n, p.res_dtype);
     store_act(p.out, m * p.ldo + n, p.out_dtype, v);
-}
-
-// Finishes 16 activation rows (16 mc .. 16 mc + 15) of lane r's values v.
-// Called by all 128 epilogue threads together (SiLU*up exchanges through xch).
-__device__ __forceinline__ void tc_finish16(const TcParams& p, int u, int r, int n, int mc, float rs, float bi,
-                                            float (&v)[16], float* xch) {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = fmaf(v[i], rs, bi);
-    if (p.epi == BQ_EPI_SILU_MUL) {
-        if (r >= 64) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) xch[i * 64 + (r - 64)] = v[i];
-        }
-        epi_sync();
-        if (r < 64) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const int m = 16 * mc + i;
-                if (m < p.M) store_act(p.out, m * p.ldo + u * 64 + r, p.out_dtype, silu(v[i]) * xch[i * 64 + r]);
-            }
-        }
-        epi_sync();
-    } else {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            const int m = 16 * mc + i;
-            if (m < p.M) tc_store(p, m, n, v[i]);
-        }
-    }
 }
 
 template <int FMT>
@@ -418,18 +406,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(const __grid_con
     extern __shared__ __align__(1024) unsigned char smem[];
     const uint32_t sbase = smem_u32(smem);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int G = gridDim.x, cta = blockIdx.x;
-    const int i0 = int((long long)cta * p.items / G), i1 = int((long long)(cta + 1) * p.items / G);
-    const int nb = i1 - i0;
+    const int C = p.C;
+    const int u = int(blockIdx.x) / C, rank = int(blockIdx.x) - u * C;  // cluster dims (C, 1, 1)
+    const int kb0 = rank * p.KB / C, nb = (rank + 1) * p.KB / C - kb0;
 
     // barriers: full[4] (A stage dequantized), empty[4] (stage consumed by the MMAs),
-    // xfull[4] (X stage loaded), accf[2] (accumulator ready), acce[2] (accumulator read), done
+    // xfull[4] (X stage landed), acc (accumulator complete), done (every MMA finished)
     const uint32_t bars = sbase + p.sm_bar;
-    const uint32_t bar_full = bars, bar_empty = bars + 32, bar_xfull = bars + 64, bar_accf = bars + 96,
-                   bar_acce = bars + 112, bar_done = bars + 128;
+    const uint32_t bar_full = bars, bar_empty = bars + 32, bar_xfull = bars + 64, bar_acc = bars + 96,
+                   bar_done = bars + 104;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + p.sm_bar + 136);
     volatile int* abort = reinterpret_cast<volatile int*>(smem + p.sm_bar + 140);
-    volatile int* last_flag = reinterpret_cast<volatile int*>(smem + p.sm_bar + 144);
     const long long lim = p.wait_cycles;
 
     if (threadIdx.x == 0) {
@@ -438,10 +425,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(const __grid_con
             mbar_init(bar_empty + 8 * a, 1);
             mbar_init(bar_xfull + 8 * a, 32);
         }
-        for (int d = 0; d < 2; ++d) {
-            mbar_init(bar_accf + 8 * d, 1);
-            mbar_init(bar_acce + 8 * d, 128);
-        }
+        mbar_init(bar_acc, 1);
         mbar_init(bar_done, 1);
         *abort = 0;
         fence_barrier_init();
@@ -451,14 +435,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(const __grid_con
     const int RD = p.raw_depth;
     const uint32_t raw_g = sbase + p.sm_raw + grp * RD * p.raw_slot;
     const uint32_t sc_g = sbase + p.sm_sc + grp * RD * p.sc_slot;
+    const int wrow = tc_row(p, u, r);
     if (warp < 8) {
         for (int jj = 0; jj < RD - 1; ++jj) {
             const int b = grp + 2 * jj;
-            if (b < nb) {
-                const int item = i0 + b;
-                tc_issue<FMT>(p, tc_row(p, item / p.KB, r), item % p.KB, r, raw_g + jj * p.raw_slot,
-                              sc_g + jj * p.sc_slot);
-            }
+            if (b < nb) tc_issue<FMT>(p, wrow, kb0 + b, r, raw_g + jj * p.raw_slot, sc_g + jj * p.sc_slot);
             cp_async_commit();
         }
     }
@@ -487,9 +468,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(const __grid_con
             {  // keep RD - 1 blocks of this group in flight
                 const int bn = b + 2 * (RD - 1);
                 if (bn < nb) {
-                    const int item = i0 + bn, jn = (j + RD - 1) % RD;
-                    tc_issue<FMT>(p, tc_row(p, item / p.KB, r), item % p.KB, r, raw_g + jn * p.raw_slot,
-                                  sc_g + jn * p.sc_slot);
+                    const int jn = (j + RD - 1) % RD;
+                    tc_issue<FMT>(p, wrow, kb0 + bn, r, raw_g + jn * p.raw_slot, sc_g + jn * p.sc_slot);
                 }
                 cp_async_commit();
             }
@@ -501,8 +481,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(const __grid_con
             }
             tc_fence_after();
             const int slot = j % RD;
-            tc_dequant<FMT>(p, r, raw_g + slot * p.raw_slot, sc_g + slot * p.sc_slot,
-                            lane_base + kTcACol0 + kTcACols * a);
+            tc_dequant<FMT>(p, r, raw_g + slot * p.raw_slot, sc_g + slot * p.sc_slot, lane_base + kTcACol0 + kTcACols * a);
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(bar_full + 8 * a);
@@ -512,131 +491,118 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(const __grid_con
         // ---------------------------------------------------------- activation loader
         pdl_wait();  // x is written by the previous kernel
         const int rows8 = p.n_mma >> 3;
-        for (int b = 0; b <= nb; ++b) {
-            if (b < nb) {
-                const int a = b & 3;
-                if (b >= kTcStages && !tc_wait(bar_empty + 8 * a, ((b >> 2) + 1) & 1, abort, lim)) break;
-                const int kb = (i0 + b) % p.KB;
-                const uint32_t xs = sbase + p.sm_x + a * (p.n_mma * 256);
-                // lane -> (row m = 8 g + lane % 8, k-chunk 4 q + lane / 8): 4 x 128 contiguous bytes per store
-                for (int t = 0; t < rows8 * 4; ++t) {
-                    const int g8 = t >> 2, q = t & 3;
-                    const int m = 8 * g8 + (lane & 7), c = 4 * q + (lane >> 3);
-                    if (m < p.M)
-                        cp_async16(xs + g8 * kTcXGroup + c * 128 + (lane & 7) * 16,
-                                   p.x + m * p.ldx + kb * 128 + c * 8);
-                }
+        for (int b = 0; b < nb; ++b) {
+            const int a = b & 3;
+            if (b >= kTcStages) {
+                const bool ok = tc_wait(bar_empty + 8 * a, ((b >> 2) + 1) & 1, abort, lim);
+                if (!__all_sync(0xffffffffu, ok)) break;
             }
-            cp_async_commit();
-            if (b > 0) {  // block b - 1 has landed: publish it to the tensor cores (async proxy)
-                cp_async_wait_depth(b < nb ? 1 : 0);
-                fence_proxy_async();
-                mbar_arrive(bar_xfull + 8 * ((b - 1) & 3));
+            const int kb = kb0 + b;
+            const uint32_t xs = sbase + p.sm_x + a * (p.n_mma * 256);
+            // lane -> (row m = 8 g + lane % 8, k-chunk 4 q + lane / 8): 4 x 128 contiguous bytes per store
+            for (int t = 0; t < rows8 * 4; ++t) {
+                const int g8 = t >> 2, q = t & 3;
+                const int m = 8 * g8 + (lane & 7), c = 4 * q + (lane >> 3);
+                if (m < p.M)
+                    cp_async16(xs + g8 * kTcXGroup + c * 128 + (lane & 7) * 16, p.x + m * p.ldx + kb * 128 + c * 8);
             }
+            cp_async_arrive_noinc(bar_xfull + 8 * a);  // one arrival per lane once its copies have landed
         }
-        cp_async_wait_depth(0);
+        cp_async_commit();
+        cp_async_wait_depth(0);  // every copy of this thread (none is left in flight at exit)
     } else if (warp == kTcMmaWarp) {
         // ---------------------------------------------------------- MMA issuer
         if (lane == 0) {
-            int s = 0;
-            for (int b = 0; b < nb;) {
-                const TcSeg sg = tc_seg_at(p, i0 + b, i1);
-                const int d = s & 1;
-                bool ok = true;
-                if (s >= 2) ok = tc_wait(bar_acce + 8 * d, ((s >> 1) + 1) & 1, abort, lim);
-                for (int kb = sg.kb0; ok && kb < sg.kb1; ++kb, ++b) {
-                    const int a = b & 3;
-                    ok = tc_wait(bar_full + 8 * a, (b >> 2) & 1, abort, lim) &&
-                         tc_wait(bar_xfull + 8 * a, (b >> 2) & 1, abort, lim);
-                    if (!ok) break;
-                    tc_fence_after();
-                    const uint32_t xs = sbase + p.sm_x + a * (p.n_mma * 256);
-#pragma unroll
-                    for (int k = 0; k < 8; ++k)
-                        tc_mma(tmem + d * kTcAccCols, tmem + kTcACol0 + kTcACols * a + 8 * k, tc_bdesc(xs + 256 * k),
-                               p.idesc, (kb > sg.kb0 || k > 0) ? 1u : 0u);
-                    tc_commit(bar_empty + 8 * a);
-                }
+            bool ok = true;
+            for (int b = 0; ok && b < nb; ++b) {
+                const int a = b & 3;
+                ok = tc_wait(bar_full + 8 * a, (b >> 2) & 1, abort, lim) &&
+                     tc_wait(bar_xfull + 8 * a, (b >> 2) & 1, abort, lim);
                 if (!ok) break;
-                tc_commit(bar_accf + 8 * d);
-                ++s;
+                tc_fence_after();
+                const uint32_t xs = sbase + p.sm_x + a * (p.n_mma * 256);
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    tc_mma(tmem, tmem + kTcACol0 + kTcACols * a + 8 * k, tc_bdesc(xs + 256 * k), p.idesc,
+                           (b > 0 || k > 0) ? 1u : 0u);
+                tc_commit(bar_empty + 8 * a);
             }
+            if (ok) tc_commit(bar_acc);
             tc_commit(bar_done);  // every MMA issued above has finished once this completes
             tc_wait(bar_done, 0, nullptr, lim);  // also after an abort: TMEM is freed only when they are done
         }
         __syncwarp();
     } else {
-        // ---------------------------------------------------------- epilogue
+        // ---------------------------------------------------------- accumulator -> shared memory
+        // The X stages are free once the last MMA is done: the partial sums go there.
         const int q = warp & 3;
         const int re = (q << 5) | lane;  // TMEM lane = weight row within the unit
         const uint32_t lane_base = tmem + (uint32_t(q * 32) << 16);
-        float* xch = reinterpret_cast<float*>(smem + p.sm_xch);
-        const int n_chunks = p.n_mma >> 4;
-        pdl_wait();  // outputs, residual rows and the workspace are shared with the previous kernel
-        int s = 0;
-        for (int b = 0; b < nb; ++s) {
-            const TcSeg sg = tc_seg_at(p, i0 + b, i1);
-            b += sg.kb1 - sg.kb0;
-            const int d = s & 1;
-            const int n = tc_row(p, sg.unit, re);
-            float rs = 1.f;
-            if (FMT == BQ_W_FP8_E4M3 || FMT == BQ_W_INT8) {
-                rs = static_cast<const float*>(p.scale)[n];
-                if (p.flags & BQ_FLAG_SCALE_ROUND_BF16) rs = __bfloat162float(__float2bfloat16_rn(rs));
-            }
-            const float bi = p.bias ? load_act(p.bias, n, p.out_dtype) : 0.f;
-            const bool owned = sg.kb0 == 0 && sg.kb1 == p.KB;
-            // uniform over the 128 epilogue threads (warp-wide tcgen05.ld, named barriers below)
-            if (epi_any(!tc_wait(bar_accf + 8 * d, (s >> 1) & 1, abort, lim))) break;
+        if (!epi_any(!tc_wait(bar_acc, 0, abort, lim))) {
             tc_fence_after();
-            if (owned) {
-                for (int mc = 0; mc < n_chunks; ++mc) {
-                    float v[16];
-                    tmem_ld16(lane_base + d * kTcAccCols + 16 * mc, v);
-                    tc_finish16(p, sg.unit, re, n, mc, rs, bi, v, xch);
-                }
-                tc_fence_before();
-                mbar_arrive(bar_acce + 8 * d);
-                continue;
-            }
-            // one piece of a shared unit: publish it, the last of the unit's CTAs finishes
-            const long long first = (long long)sg.unit * p.KB;
-            const int c_lo = tc_cta_of(first, p.items, G), c_hi = tc_cta_of(first + p.KB - 1, p.items, G);
-            const int pieces = c_hi - c_lo + 1, piece = cta - c_lo;
-            float* part = p.part + size_t(sg.unit) * p.max_pieces * p.n_mma * 128;
-            for (int mc = 0; mc < n_chunks; ++mc) {
+            float* red = reinterpret_cast<float*>(smem + p.sm_x) + re * p.red_pitch;
+            for (int mc = 0; mc < (p.n_mma >> 4); ++mc) {
                 float v[16];
-                tmem_ld16(lane_base + d * kTcAccCols + 16 * mc, v);
+                tmem_ld16(lane_base + 16 * mc, v);
 #pragma unroll
-                for (int i = 0; i < 16; ++i) part[(size_t(piece) * p.n_mma + 16 * mc + i) * 128 + re] = v[i];
+                for (int i = 0; i < 16; i += 4) *reinterpret_cast<float4*>(red + 16 * mc + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
             }
-            tc_fence_before();
-            mbar_arrive(bar_acce + 8 * d);
-            __threadfence();
-            epi_sync();
-            if (re == 0) *last_flag = atomicAdd(&p.counters[sg.unit], 1u) == unsigned(pieces - 1);
-            epi_sync();
-            if (*last_flag) {
-                __threadfence();
-                for (int mc = 0; mc < n_chunks; ++mc) {
-                    float v[16];
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) v[i] = 0.f;
-                    for (int pc = 0; pc < pieces; ++pc) {
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) v[i] += __ldcg(&part[(size_t(pc) * p.n_mma + 16 * mc + i) * 128 + re]);
-                    }
-                    tc_finish16(p, sg.unit, re, n, mc, rs, bi, v, xch);
-                }
-                if (re == 0) p.counters[sg.unit] = 0u;  // ready for the next call
-            }
-            epi_sync();  // last_flag is rewritten by the next segment
         }
     }
 
+    // ---------------------------------------------------------- cluster reduction
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    pdl_wait();  // the residual and the output are shared with the previous kernel
+    cluster_sync_all();  // every CTA of the unit has its partial rows in shared memory
+    int bad = 0;
+    for (int c = 0; c < C; ++c) bad |= dsmem_ld_s32(dsmem_addr(smem_u32(const_cast<int*>(abort)), uint32_t(c)));
+    if (!bad) {
+        const bool is_silu = p.epi == BQ_EPI_SILU_MUL;
+        const int half = is_silu ? 64 : 128;               // rows summed per output row: one, or the gate/up pair
+        const int r0 = rank * half / C, nr = (rank + 1) * half / C - r0;
+        const int mq_n = (p.M + 3) >> 2;                // groups of four activation rows
+        const uint32_t red0 = sbase + p.sm_x;
+        for (int t = threadIdx.x; t < nr * mq_n; t += kTcThreads) {
+            const int rl = r0 + t % nr, mq = t / nr;
+            float4 g = make_float4(0.f, 0.f, 0.f, 0.f), v = g;
+            const uint32_t ag = red0 + uint32_t(rl * p.red_pitch + 4 * mq) * 4u;
+            const uint32_t av = red0 + uint32_t((rl + 64) * p.red_pitch + 4 * mq) * 4u;
+            for (int c = 0; c < C; ++c) {  // rank order: deterministic
+                const float4 x = dsmem_ld4(dsmem_addr(ag, uint32_t(c)));
+                g.x += x.x; g.y += x.y; g.z += x.z; g.w += x.w;
+                if (is_silu) {
+                    const float4 y = dsmem_ld4(dsmem_addr(av, uint32_t(c)));
+                    v.x += y.x; v.y += y.y; v.z += y.z; v.w += y.w;
+                }
+            }
+            const int n = tc_row(p, u, rl);
+            float rs = 1.f, rsu = 1.f;
+            if (FMT == BQ_W_FP8_E4M3 || FMT == BQ_W_INT8) {
+                rs = static_cast<const float*>(p.scale)[n];
+                if (p.flags & BQ_FLAG_SCALE_ROUND_BF16) rs = __bfloat162float(__float2bfloat16_rn(rs));
+                if (is_silu) {
+                    rsu = static_cast<const float*>(p.scale)[n + (p.N >> 1)];
+                    if (p.flags & BQ_FLAG_SCALE_ROUND_BF16) rsu = __bfloat162float(__float2bfloat16_rn(rsu));
+                }
+            }
+            const float bi = p.bias ? load_act(p.bias, n, p.out_dtype) : 0.f;
+            const float biu = (p.bias && is_silu) ? load_act(p.bias, n + (p.N >> 1), p.out_dtype) : 0.f;
+            const float gs[4] = {g.x, g.y, g.z, g.w}, us[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int m = 4 * mq + i;
+                if (m >= p.M) break;
+                const float a = fmaf(gs[i], rs, bi);
+                if (is_silu)
+                    store_act(p.out, m * p.ldo + n, p.out_dtype, silu(a) * fmaf(us[i], rsu, biu));
+                else
+                    tc_store(p, m, n, a);
+            }
+        }
+    }
+    cluster_sync_all();  // no CTA leaves while another may still read its shared memory
     if (warp == kTcMmaWarp) tmem_dealloc(tmem, kTcTmemCols);
 }
 
@@ -681,30 +647,30 @@ const void* tc_kernel_for(int fmt) {
 
 }  // namespace
 
-// Plans the tensor-core path for `d`; returns false when it does not apply
-// (row count, activation dtype, N, group or shared memory).
-bool plan_tc(const bq_gemv_desc* d, TcPlan* pl) {
-    if (d->flags & BQ_FLAG_NO_TC) return false;
+namespace {
+// Plans depend on the shape, format, group, epilogue, norm and device only.
+std::mutex g_tc_mu;
+std::map<std::array<int, 9>, std::pair<bool, TcPlan>> g_tc_plans;
+
+bool plan_tc_uncached(const bq_gemv_desc* d, TcPlan* pl) {
     if (d->M < kTcMinRows || d->M > kTcMaxRows || d->x_dtype != BQ_DT_BF16 || d->N % 128 != 0) return false;
     if (d->wfmt == BQ_W_INT4_PLAIN && d->group != 128) return false;
     if (d->wfmt == BQ_W_INT4_TINYGEMM && d->group != 32 && d->group != 64 && d->group != 128 && d->group != 256)
         return false;
-    if (!tc_kernel_for(d->wfmt)) return false;
+    const void* fn = tc_kernel_for(d->wfmt);
+    if (!fn) return false;
     const DeviceInfo* di = device_info();
     if (!di) return false;
     TcPlan p{};
     p.n_mma = (d->M + 15) & ~15;
     p.KB = d->K / 128;
     p.units = d->N / 128;
-    p.items = p.units * p.KB;
-    p.grid = std::min(di->sm_count, p.items);
     const bool int4 = d->wfmt == BQ_W_INT4_TINYGEMM || d->wfmt == BQ_W_INT4_PLAIN;
     p.raw_slot = 128u * uint32_t(tc_row_bytes(d->wfmt));
     p.sc_slot = int4 ? uint32_t(kTcScSlot) : 0u;
     p.sm_x = 0;
     const uint32_t x_bytes = uint32_t(kTcStages) * uint32_t(p.n_mma) * 256u;
-    const uint32_t xch = d->epilogue == BQ_EPI_SILU_MUL ? 16u * 64u * 4u : 0u;
-    const uint32_t fixed = x_bytes + xch + 256u;
+    const uint32_t fixed = x_bytes + 256u;
     int rd = 0;
     for (int c = 6; c >= 2; --c)
         if (fixed + 2u * uint32_t(c) * (p.raw_slot + p.sc_slot) <= uint32_t(di->smem_optin)) {
@@ -715,35 +681,75 @@ bool plan_tc(const bq_gemv_desc* d, TcPlan* pl) {
     p.raw_depth = rd;
     p.sm_raw = x_bytes;
     p.sm_sc = p.sm_raw + 2u * rd * p.raw_slot;
-    p.sm_xch = p.sm_sc + 2u * rd * p.sc_slot;
-    p.sm_bar = p.sm_xch + xch;
+    p.sm_bar = p.sm_sc + 2u * rd * p.sc_slot;
     p.sm_total = p.sm_bar + 256u;
-    // pieces of the units that several CTAs share
-    p.max_pieces = 1;
-    for (int u = 0; u < p.units; ++u) {
-        const long long first = (long long)u * p.KB;
-        const int pcs = tc_cta_of(first + p.KB - 1, p.items, p.grid) - tc_cta_of(first, p.items, p.grid) + 1;
-        p.max_pieces = std::max(p.max_pieces, pcs);
+    p.red_pitch = uint32_t(p.n_mma) + 4u;
+    if (ensure_smem_attr(fn, p.sm_total)) return false;
+    // K slices per unit: fill the SMs in one wave with clusters of at most 8
+    // CTAs (the portable cluster size) that can all be resident at once
+    int C = std::max(1, std::min({8, p.KB, di->sm_count / std::max(1, p.units)}));
+    for (; C > 1; --C) {
+        cudaLaunchConfig_t cfg;
+        std::memset(&cfg, 0, sizeof(cfg));
+        cfg.gridDim = dim3(p.units * C);
+        cfg.blockDim = dim3(kTcThreads);
+        cfg.dynamicSmemBytes = p.sm_total;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = C;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, fn, &cfg) == cudaSuccess && clusters >= p.units) break;
+        cudaGetLastError();  // clear a refused query
     }
-    int64_t off = kCounterBytes;
-    p.part_off = off;
-    if (p.max_pieces > 1) off += int64_t(p.units) * p.max_pieces * p.n_mma * 128 * 4;
-    off = (off + 255) & ~int64_t(255);
-    p.xn_off = off;
-    if (d->gamma) off += int64_t(d->M) * d->K * 2;
-    p.ws_bytes = off;
+    p.C = C;
+    p.grid = p.units * C;
+    // the normalized rows go after the arrival-counter region that every
+    // workspace starts with: the row-block kernel's counters must stay zero
+    p.xn_off = kCounterBytes;
+    p.ws_bytes = d->gamma ? kCounterBytes + ((int64_t(d->M) * d->K * 2 + 255) & ~int64_t(255)) : 0;
     *pl = p;
     return true;
+}
+}  // namespace
+
+// Plans the tensor-core path for `d`; returns false when it does not apply
+// (row count, activation dtype, N, group or shared memory).
+bool plan_tc(const bq_gemv_desc* d, TcPlan* pl) {
+    if (d->flags & BQ_FLAG_NO_TC) return false;
+    if (d->M < kTcMinRows || d->M > kTcMaxRows) return false;
+    const DeviceInfo* di = device_info();
+    if (!di) return false;
+    const std::array<int, 9> key{di->device, d->M, d->N, d->K, d->wfmt, d->group, d->epilogue, d->x_dtype,
+                                 d->gamma != nullptr ? 1 : 0};
+    {
+        std::lock_guard<std::mutex> lk(g_tc_mu);
+        auto it = g_tc_plans.find(key);
+        if (it != g_tc_plans.end()) {
+            if (it->second.first) *pl = it->second.second;
+            return it->second.first;
+        }
+    }
+    TcPlan p{};
+    const bool ok = plan_tc_uncached(d, &p);
+    std::lock_guard<std::mutex> lk(g_tc_mu);
+    if (g_tc_plans.size() > 4096) g_tc_plans.clear();
+    g_tc_plans.emplace(key, std::make_pair(ok, p));
+    if (ok) *pl = p;
+    return ok;
 }
 
 int launch_tc(const bq_gemv_desc* d, const TcPlan& pl, void* workspace, cudaStream_t stream) {
     const void* fn = tc_kernel_for(d->wfmt);
     if (!fn) return set_error(BQ_ERR_FORMAT, "no tensor-core GEMV for format %d", d->wfmt);
-    if (!workspace) return set_error(BQ_ERR_WORKSPACE, "the tensor-core GEMV needs a workspace");
+    if (pl.ws_bytes > 0 && !workspace) return set_error(BQ_ERR_WORKSPACE, "the tensor-core GEMV needs a workspace");
     char* ws = static_cast<char*>(workspace);
     const __nv_bfloat16* x = static_cast<const __nv_bfloat16*>(d->x);
     long long ldx = d->ldx;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     const bool pdl = (d->flags & BQ_FLAG_PDL) != 0;
@@ -789,22 +795,18 @@ int launch_tc(const bq_gemv_desc* d, const TcPlan& pl, void* workspace, cudaStre
     p.out_dtype = d->out_dtype;
     p.res_dtype = d->res_dtype;
     p.flags = d->flags;
-    p.units = pl.units;
-    p.items = pl.items;
+    p.C = pl.C;
     p.n_mma = pl.n_mma;
-    p.max_pieces = pl.max_pieces;
     p.raw_depth = pl.raw_depth;
     // kind::f16, fp32 accumulate, bf16 A and B, both K-major, N = n_mma, M = 128
     p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(pl.n_mma >> 3) << 17) | (uint32_t(128 >> 4) << 24);
     p.wait_cycles = kWaitCycles;
-    p.part = reinterpret_cast<float*>(ws + pl.part_off);
-    p.counters = reinterpret_cast<unsigned*>(ws);
     p.sm_x = pl.sm_x;
     p.sm_raw = pl.sm_raw;
     p.sm_sc = pl.sm_sc;
-    p.sm_xch = pl.sm_xch;
     p.sm_bar = pl.sm_bar;
     p.sm_total = pl.sm_total;
+    p.red_pitch = pl.red_pitch;
     p.raw_slot = pl.raw_slot;
     p.sc_slot = pl.sc_slot;
     int rc = ensure_smem_attr(fn, pl.sm_total);
@@ -815,10 +817,14 @@ int launch_tc(const bq_gemv_desc* d, const TcPlan& pl, void* workspace, cudaStre
     cfg.blockDim = dim3(kTcThreads);
     cfg.dynamicSmemBytes = pl.sm_total;
     cfg.stream = stream;
-    if (pdl || d->gamma) {  // after the norm kernel always: its rows are waited for in the kernel
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-    }
+    int na = 0;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = pl.C;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    if (pdl || d->gamma) ++na;  // after the norm kernel always: its rows are waited for in the kernel
+    cfg.attrs = (pdl || d->gamma) ? attr : attr + 1;
+    cfg.numAttrs = na + 1;
     void* args[] = {&p};
     cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
     if (e != cudaSuccess) return set_error(BQ_ERR_CUDA, "tensor-core GEMV launch failed: %s", cudaGetErrorString(e));

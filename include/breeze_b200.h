@@ -153,7 +153,14 @@ int32_t bq_gemv_host_io(const bq_gemv_desc* desc, const void* x_host, void* out_
  * first after a cudaDeviceReset) clears the array's counters with a blocking
  * memset: make it before any stream capture. All calls on a device share the
  * array: calls whose kernels can overlap on the GPU race and must be
- * serialized on one stream. */
+ * serialized on one stream. For more than 16 rows, when the tensor-core
+ * kernel's split-K pieces would not fit the array, the call runs the 16-row
+ * block kernel instead, whose summation order differs from the tensor-core
+ * kernel that bq_gemv then uses (results agree within rounding, not bit for
+ * bit). After a device wait timeout, bq_device_status_clear on that device
+ * makes the next call clear the counters again (blocking, outside capture).
+ * The array's address is looked up on every call, so after a
+ * cudaDeviceReset the next call finds the reloaded array and clears it. */
 int32_t bq_gemv_noalloc(const bq_gemv_desc* desc, void* stream);
 
 /* ---- decode chain: a list of GEMVs in one launch ------------------------ */

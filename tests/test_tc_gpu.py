@@ -5,8 +5,8 @@ bq_gemv takes this path by itself for 17..128 bf16 rows when N is a multiple
 of 128; BQ_FLAG_NO_TC keeps a call on the mma.sync kernel, which re-streams
 the weights per 16 rows. Bar: max |err| / max |ref| <= 1e-2 against the
 oracle's fp32 dequant-then-linear (TOL), every weight format and epilogue, with
-and without the RMSNorm; bit-identical reruns (the last CTA of a unit sums
-the pieces in piece order).
+and without the RMSNorm; bit-identical reruns (the K slices of a unit are
+summed in cluster-rank order).
 """
 
 import functools
@@ -47,8 +47,8 @@ def _case(fmt, n, k):
     return make_weight(fmt, n, k, seed=n + 3 * k)
 
 
-# (N, K): units owned by one CTA (256x1024: 16 items on 16 CTAs), units split over
-# many CTAs (1024x2048: 128 items, one per CTA), uneven splits (6144x2048: 768 items)
+# (N, K): two units of 128 rows, each split into up to 8 K slices (256x1024), eight
+# units (1024x2048), 48 units in uneven K slices (6144x2048: 3 slices of 16 k-blocks)
 SHAPES = [(256, 1024), (1024, 2048), (6144, 2048)]
 
 

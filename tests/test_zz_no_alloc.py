@@ -104,3 +104,26 @@ def test_noalloc_rejects_shapes_beyond_its_scratch():
     assert "scratch" in L.last_error()
     torch.cuda.synchronize()
     assert bool((out == 7.0).all())
+
+
+def test_noalloc_after_status_clear():
+    """bq_device_status_clear (the recovery step after a device wait ran out)
+    makes the next call clear the built-in array's counters again; the calls
+    around it stay correct."""
+    L = _lib()
+    case = make_weight("int4_tinygemm", 2048, 2048, seed=3)
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(1, 2048, generator=g).to(torch.bfloat16)
+    ref = gemv.fused_reference(x, case["deq"], None, 1e-6, 0)
+    dx, w, scale = x.to(DEV), case["w"].to(DEV), case["scale"].to(DEV)
+    for clear in (False, True, False):
+        if clear:
+            torch.cuda.synchronize()
+            L.device_status(0, clear=True)
+        out = torch.full((1, 2048), float("nan"), device=DEV, dtype=torch.bfloat16)
+        d = L.make_desc(dx, w, wfmt_code("int4_tinygemm"), 2048, scale=scale, group=128, out=out,
+                        flags=L.default_flags())
+        _noalloc(L, d)
+        torch.cuda.synchronize()
+        assert gemv.max_rel_err(out.cpu().float(), ref) < TOL
+    assert L.device_status() == 0
