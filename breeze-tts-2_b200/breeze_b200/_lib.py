@@ -26,7 +26,7 @@ BQ_DEVERR_WAIT_TIMEOUT = 1
 W_BF16, W_INT4_TINYGEMM, W_INT4_PLAIN, W_FP8_E4M3, W_INT8 = 0, 1, 2, 3, 4
 EPI_NONE, EPI_SILU_MUL, EPI_ADD_RESIDUAL = 0, 1, 2
 DT_BF16, DT_F16, DT_F32 = 0, 1, 2
-FLAG_PDL, FLAG_SCALE_ROUND_BF16, FLAG_NO_TC = 1, 2, 4
+FLAG_PDL, FLAG_SCALE_ROUND_BF16, FLAG_NO_TC, FLAG_RING_KERNEL = 1, 2, 4, 8
 
 _DT = {torch.bfloat16: DT_BF16, torch.float16: DT_F16, torch.float32: DT_F32}
 

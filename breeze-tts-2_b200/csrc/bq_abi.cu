@@ -169,6 +169,11 @@ int32_t bq_gemv_workspace_bytes(const bq_gemv_desc* desc, size_t* bytes) {
         *bytes = size_t(tp.ws_bytes);
         return BQ_OK;
     }
+    LeanPlan lp;
+    if (plan_lean(desc, &lp)) {
+        *bytes = 0;
+        return BQ_OK;
+    }
     const int step = gemv3_rows_per_launch(desc);
     int64_t need = 0;
     for (int row0 = 0; row0 < desc->M; row0 += step) {
@@ -198,6 +203,8 @@ int32_t bq_gemv(const bq_gemv_desc* desc, void* workspace, size_t workspace_byte
             return set_error(BQ_ERR_ALIGN, "workspace must be 256-byte aligned");
         return launch_tc(desc, tp, workspace, static_cast<cudaStream_t>(stream));
     }
+    LeanPlan lp;
+    if (plan_lean(desc, &lp)) return launch_lean(desc, lp, static_cast<cudaStream_t>(stream));
     const int step = gemv3_rows_per_launch(desc);
     for (int row0 = 0; row0 < desc->M; row0 += step) {
         Gemv3Plan pl;

@@ -52,6 +52,15 @@ struct TcPlan {
 bool plan_tc(const bq_gemv_desc* d, TcPlan* pl);
 int launch_tc(const bq_gemv_desc* d, const TcPlan& pl, void* workspace, cudaStream_t stream);
 
+// Resident-slice GEMV (1..8 rows, whole weight slice in shared memory before the
+// dependent-launch wait, no workspace).
+struct LeanPlan {
+    int units, grid, upc, tpu, nkw, pitch, rbk;
+    uint32_t sm_w, sm_sc, sm_x, sm_xs, sm_part, sm_misc, sm_bar, sm_total;
+};
+bool plan_lean(const bq_gemv_desc* d, LeanPlan* pl);
+int launch_lean(const bq_gemv_desc* d, const LeanPlan& pl, cudaStream_t stream);
+
 // The no-alloc GEMV's built-in scratch: clear its counters again on the next call on `dev`.
 void noalloc_forget(int dev);
 

@@ -566,15 +566,27 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(const __grid_con
         const uint32_t red0 = sbase + p.sm_x;
         for (int t = threadIdx.x; t < nr * mq_n; t += kTcThreads) {
             const int rl = r0 + t % nr, mq = t / nr;
-            float4 g = make_float4(0.f, 0.f, 0.f, 0.f), v = g;
             const uint32_t ag = red0 + uint32_t(rl * p.red_pitch + 4 * mq) * 4u;
-            const uint32_t av = red0 + uint32_t((rl + 64) * p.red_pitch + 4 * mq) * 4u;
-            for (int c = 0; c < C; ++c) {  // rank order: deterministic
-                const float4 x = dsmem_ld4(dsmem_addr(ag, uint32_t(c)));
-                g.x += x.x; g.y += x.y; g.z += x.z; g.w += x.w;
-                if (is_silu) {
-                    const float4 y = dsmem_ld4(dsmem_addr(av, uint32_t(c)));
-                    v.x += y.x; v.y += y.y; v.z += y.z; v.w += y.w;
+            const uint32_t av = red0 + uint32_t((rl + (is_silu ? 64 : 0)) * p.red_pitch + 4 * mq) * 4u;
+            // every slice's partial in flight at once, then summed in rank order (deterministic)
+            float4 pg[8], pu[8];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                if (c < C) {
+                    pg[c] = c == rank ? *reinterpret_cast<const float4*>(smem + (ag - sbase)) : dsmem_ld4(dsmem_addr(ag, uint32_t(c)));
+                    if (is_silu)
+                        pu[c] = c == rank ? *reinterpret_cast<const float4*>(smem + (av - sbase))
+                                          : dsmem_ld4(dsmem_addr(av, uint32_t(c)));
+                }
+            }
+            float4 g = make_float4(0.f, 0.f, 0.f, 0.f), v = g;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                if (c < C) {
+                    g.x += pg[c].x; g.y += pg[c].y; g.z += pg[c].z; g.w += pg[c].w;
+                    if (is_silu) {
+                        v.x += pu[c].x; v.y += pu[c].y; v.z += pu[c].z; v.w += pu[c].w;
+                    }
                 }
             }
             const int n = tc_row(p, u, rl);

@@ -82,6 +82,9 @@ extern "C" {
                                        Int8Linear does for bf16 activations              */
 #define BQ_FLAG_NO_TC 4u            /* keep 17..128-row calls on the mma.sync kernel (row
                                        blocks of 16) instead of the tcgen05 kernel        */
+#define BQ_FLAG_RING_KERNEL 8u      /* keep 1..8-row calls on the ring-streaming kernel
+                                       instead of the resident-slice kernel (for
+                                       comparisons; results agree within rounding)       */
 
 typedef struct bq_gemv_desc {
     int32_t M;         /* activation rows (decode batch), >= 1 */
