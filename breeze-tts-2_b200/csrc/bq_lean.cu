@@ -9,17 +9,17 @@
 
 namespace bq {
 
-const void* lean_kernel_int4(int fmt, int tpu, int upc);
-const void* lean_kernel_f8(int fmt, int tpu, int upc);
-const void* lean_kernel_bf16(int tpu, int upc);
+const void* lean_kernel_int4(int fmt, int tpu, int upc, int rows);
+const void* lean_kernel_f8(int fmt, int tpu, int upc, int rows);
+const void* lean_kernel_bf16(int tpu, int upc, int rows);
 
 namespace {
 inline uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
-const void* lean_kernel(int fmt, int tpu, int upc) {
-    if (fmt == BQ_W_INT4_TINYGEMM || fmt == BQ_W_INT4_PLAIN) return lean_kernel_int4(fmt, tpu, upc);
-    if (fmt == BQ_W_FP8_E4M3 || fmt == BQ_W_INT8) return lean_kernel_f8(fmt, tpu, upc);
-    if (fmt == BQ_W_BF16) return lean_kernel_bf16(tpu, upc);
+const void* lean_kernel(int fmt, int tpu, int upc, int rows) {
+    if (fmt == BQ_W_INT4_TINYGEMM || fmt == BQ_W_INT4_PLAIN) return lean_kernel_int4(fmt, tpu, upc, rows);
+    if (fmt == BQ_W_FP8_E4M3 || fmt == BQ_W_INT8) return lean_kernel_f8(fmt, tpu, upc, rows);
+    if (fmt == BQ_W_BF16) return lean_kernel_bf16(tpu, upc, rows);
     return nullptr;
 }
 }  // namespace
@@ -79,13 +79,13 @@ bool plan_lean(const bq_gemv_desc* d, LeanPlan* pl) {
     o += 16;
     P.sm_total = o;
     if (int64_t(P.sm_total) > int64_t(di->smem_optin)) return false;
-    if (!lean_kernel(fmt, P.tpu, P.upc)) return false;
+    if (!lean_kernel(fmt, P.tpu, P.upc, d->M)) return false;
     *pl = P;
     return true;
 }
 
 int launch_lean(const bq_gemv_desc* d, const LeanPlan& pl, cudaStream_t stream) {
-    const void* fn = lean_kernel(d->wfmt, pl.tpu, pl.upc);
+    const void* fn = lean_kernel(d->wfmt, pl.tpu, pl.upc, d->M);
     if (!fn) return set_error(BQ_ERR_FORMAT, "no resident-slice GEMV for format %d", d->wfmt);
     LeanParams p;
     std::memset(&p, 0, sizeof(p));

@@ -87,13 +87,16 @@ __device__ __forceinline__ int lean_row(const LeanParams& p, int u, int tile) {
     return tile == 0 ? 16 * u : (p.N >> 1) + 16 * u;
 }
 
-template <int FMT, int TPU, int UPC>
+// MR: activation rows (1 or 2), a compile-time count so the staging and its
+// row reductions are straight-line code.
+template <int FMT, int TPU, int UPC, int MR>
 __global__ void __launch_bounds__(kLeanThreads, 2) gemv_lean_kernel(const __grid_constant__ LeanParams p) {
     using F = Fmt3<FMT>;
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tq = lane & 3, tg = lane >> 2;
-    const int M = p.M, KB = p.KB;
+    constexpr int M = MR;
+    const int KB = p.KB;
     const int u0 = int(int64_t(blockIdx.x) * p.units / gridDim.x);
     const int nu = int(int64_t(blockIdx.x + 1) * p.units / gridDim.x) - u0;  // 1 .. UPC
     const int kw0 = (warp * KB) >> 3, nkw = (((warp + 1) * KB) >> 3) - kw0;  // this warp's k-blocks
@@ -169,6 +172,7 @@ __global__ void __launch_bounds__(kLeanThreads, 2) gemv_lean_kernel(const __grid
     }
     const int per_row = nkw * 16;  // 16-byte chunks of one activation row in this warp's K range
     const int nch = M * per_row;
+    const int nci = (nch + 31) >> 5;  // chunk rounds of the warp (uniform)
     uint4 gv[kLeanMaxChunks];
 #pragma unroll
     for (int i = 0; i < kLeanMaxChunks; ++i) {
@@ -194,6 +198,7 @@ __global__ void __launch_bounds__(kLeanThreads, 2) gemv_lean_kernel(const __grid
     for (int i = 0; i < kLeanMaxChunks; ++i) {
         const int t = lane + 32 * i;
         xv[i] = make_uint4(0u, 0u, 0u, 0u);
+        if (i >= nci) continue;
         if (t < nch) {
             const int m = t / per_row, jc = t - m * per_row;
             xv[i] = __ldcg(reinterpret_cast<const uint4*>(p.x + m * p.ldx + int64_t(kw0) * 128 + jc * 8));
@@ -212,11 +217,12 @@ __global__ void __launch_bounds__(kLeanThreads, 2) gemv_lean_kernel(const __grid
     // staging: x * gamma per chunk; sum(x^2) per chunk (x itself, as RMSNorm uses it)
     float ssc[kLeanMaxChunks], xsc[kLeanMaxChunks], amc[kLeanMaxChunks];
     int mrow[kLeanMaxChunks];
-    const int nci = (nch + 31) >> 5;  // chunk rounds of the warp (uniform)
 #pragma unroll
     for (int i = 0; i < kLeanMaxChunks; ++i) {
         const int t = lane + 32 * i;
         mrow[i] = t < nch ? t / per_row : -1;
+        ssc[i] = amc[i] = xsc[i] = 0.f;
+        if (i >= nci) continue;
         const uint32_t xr[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
         const uint32_t gr[4] = {gv[i].x, gv[i].y, gv[i].z, gv[i].w};
         float ss = 0.f, am = 0.f;
@@ -229,14 +235,13 @@ __global__ void __launch_bounds__(kLeanThreads, 2) gemv_lean_kernel(const __grid
         }
         ssc[i] = ss;
         amc[i] = am;
-        xsc[i] = 0.f;
     }
     // per-row reductions over the warp (every lane gets each row's value)
-    float row_down[8];
+    float row_down[MR];
 #pragma unroll
-    for (int m = 0; m < 8; ++m) {
+    for (int m = 0; m < MR; ++m) {
         row_down[m] = 1.f;
-        if (m < M) {
+        {
             float s = 0.f, a = 0.f;
 #pragma unroll
             for (int i = 0; i < kLeanMaxChunks; ++i) {
@@ -248,7 +253,7 @@ __global__ void __launch_bounds__(kLeanThreads, 2) gemv_lean_kernel(const __grid
 #pragma unroll
             for (int o = 16; o; o >>= 1) {
                 s += __shfl_xor_sync(0xffffffffu, s, o);
-                a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+                if constexpr (F::kF16) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
             }
             if (lane == 0) s_ss[warp * 8 + m] = s;
             if constexpr (F::kF16) {
@@ -267,6 +272,7 @@ __global__ void __launch_bounds__(kLeanThreads, 2) gemv_lean_kernel(const __grid
     // rewrite as the MMA's B operand: bf16 (plain int4: pairs {0,4},{1,5},{2,6},{3,7}) or scaled f16
 #pragma unroll
     for (int i = 0; i < kLeanMaxChunks; ++i) {
+        if (i >= nci) break;
         const int t = lane + 32 * i;
         if (t < nch) {
             const int m = mrow[i], jc = t - m * per_row;
@@ -282,7 +288,7 @@ __global__ void __launch_bounds__(kLeanThreads, 2) gemv_lean_kernel(const __grid
             if constexpr (F::kF16) {
                 float dn = 1.f;
 #pragma unroll
-                for (int mm = 0; mm < 8; ++mm)
+                for (int mm = 0; mm < MR; ++mm)
                     if (mm == m) dn = row_down[mm];
                 o.x = pack_half2(v[0] * dn, v[1] * dn);
                 o.y = pack_half2(v[2] * dn, v[3] * dn);

@@ -2,5 +2,5 @@
 #include "bq_lean_kinst.h"
 
 namespace bq {
-const void* lean_kernel_bf16(int tpu, int upc) { return lean_select<BQ_W_BF16>(tpu, upc); }
+const void* lean_kernel_bf16(int tpu, int upc, int rows) { return lean_select<BQ_W_BF16>(tpu, upc, rows); }
 }  // namespace bq

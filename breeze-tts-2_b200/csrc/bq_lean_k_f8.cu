@@ -2,7 +2,7 @@
 #include "bq_lean_kinst.h"
 
 namespace bq {
-const void* lean_kernel_f8(int fmt, int tpu, int upc) {
-    return fmt == BQ_W_FP8_E4M3 ? lean_select<BQ_W_FP8_E4M3>(tpu, upc) : lean_select<BQ_W_INT8>(tpu, upc);
+const void* lean_kernel_f8(int fmt, int tpu, int upc, int rows) {
+    return fmt == BQ_W_FP8_E4M3 ? lean_select<BQ_W_FP8_E4M3>(tpu, upc, rows) : lean_select<BQ_W_INT8>(tpu, upc, rows);
 }
 }  // namespace bq

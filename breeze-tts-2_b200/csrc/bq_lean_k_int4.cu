@@ -2,7 +2,8 @@
 #include "bq_lean_kinst.h"
 
 namespace bq {
-const void* lean_kernel_int4(int fmt, int tpu, int upc) {
-    return fmt == BQ_W_INT4_TINYGEMM ? lean_select<BQ_W_INT4_TINYGEMM>(tpu, upc) : lean_select<BQ_W_INT4_PLAIN>(tpu, upc);
+const void* lean_kernel_int4(int fmt, int tpu, int upc, int rows) {
+    return fmt == BQ_W_INT4_TINYGEMM ? lean_select<BQ_W_INT4_TINYGEMM>(tpu, upc, rows)
+                                     : lean_select<BQ_W_INT4_PLAIN>(tpu, upc, rows);
 }
 }  // namespace bq

@@ -6,16 +6,24 @@
 
 namespace bq {
 
-template <int FMT>
-const void* lean_select(int tpu, int upc) {
+template <int FMT, int MR>
+const void* lean_select_m(int tpu, int upc) {
     if (tpu == 2) {
-        if (upc <= 1) return reinterpret_cast<const void*>(&gemv_lean_kernel<FMT, 2, 1>);
-        if (upc <= 2) return reinterpret_cast<const void*>(&gemv_lean_kernel<FMT, 2, 2>);
-        return reinterpret_cast<const void*>(&gemv_lean_kernel<FMT, 2, 4>);
+        if (upc <= 1) return reinterpret_cast<const void*>(&gemv_lean_kernel<FMT, 2, 1, MR>);
+        if (upc <= 2) return reinterpret_cast<const void*>(&gemv_lean_kernel<FMT, 2, 2, MR>);
+        return reinterpret_cast<const void*>(&gemv_lean_kernel<FMT, 2, 4, MR>);
     }
-    if (upc <= 1) return reinterpret_cast<const void*>(&gemv_lean_kernel<FMT, 1, 1>);
-    if (upc <= 2) return reinterpret_cast<const void*>(&gemv_lean_kernel<FMT, 1, 2>);
-    return reinterpret_cast<const void*>(&gemv_lean_kernel<FMT, 1, 4>);
+    if (upc <= 1) return reinterpret_cast<const void*>(&gemv_lean_kernel<FMT, 1, 1, MR>);
+    if (upc <= 2) return reinterpret_cast<const void*>(&gemv_lean_kernel<FMT, 1, 2, MR>);
+    return reinterpret_cast<const void*>(&gemv_lean_kernel<FMT, 1, 4, MR>);
+}
+
+// rows: 1 or 2 (int4 weights take this kernel for one row only)
+template <int FMT>
+const void* lean_select(int tpu, int upc, int rows) {
+    if (rows == 1) return lean_select_m<FMT, 1>(tpu, upc);
+    if constexpr (FMT == BQ_W_INT4_TINYGEMM || FMT == BQ_W_INT4_PLAIN) return nullptr;
+    else return rows == 2 ? lean_select_m<FMT, 2>(tpu, upc) : nullptr;
 }
 
 }  // namespace bq
