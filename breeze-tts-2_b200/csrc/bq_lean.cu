@@ -24,18 +24,18 @@ const void* lean_kernel(int fmt, int tpu, int upc, int rows) {
 }
 }  // namespace
 
-// The resident-slice kernel applies to bf16 rows (16-byte aligned) whose
-// per-warp activation slice fits eight 16-byte chunks per lane, int4 groups of
-// 128 or 256, at most four units per CTA, and a CTA share that fits shared
-// memory. It takes one row, and two rows of fp8 / int8 / bf16 weights: the
-// 28-layer decode step measured int4 M=1 883 -> 855 us, fp8 M=2 982 -> 923,
-// int8 M=1 / 2 952 / 1048 -> 907 / 960, but int4 M=2 922 -> 948 and every
-// format slower at M = 4 and 8 (its staging and row reductions grow with M),
-// so those keep the ring-streaming kernel. BQ_FLAG_RING_KERNEL forces the latter.
+// The resident-slice kernel applies to one or two bf16 rows (16-byte aligned)
+// whose per-warp activation slice fits eight 16-byte chunks per lane, int4
+// groups of 128 or 256, at most four units per CTA, and a CTA share that fits
+// shared memory. Measured on the 28-layer decode step (per-launch graph, us):
+// int4 M = 1 / 2 883 / 922 -> 764 / 901, fp8 877 / 982 -> 760 / 893, int8
+// 952 / 1048 -> 807 / 927. At M = 4 and 8 (the row count a compile-time
+// parameter there too) it was level or up to 10 % slower than the
+// ring-streaming kernel -- its staging and row reductions grow with M -- so
+// those keep the ring kernel. BQ_FLAG_RING_KERNEL forces the ring kernel.
 bool plan_lean(const bq_gemv_desc* d, LeanPlan* pl) {
     if (d->flags & BQ_FLAG_RING_KERNEL) return false;
-    const bool int4fmt = d->wfmt == BQ_W_INT4_TINYGEMM || d->wfmt == BQ_W_INT4_PLAIN;
-    if (!(d->M == 1 || (d->M == 2 && !int4fmt)) || d->x_dtype != BQ_DT_BF16) return false;
+    if (d->M < 1 || d->M > 2 || d->x_dtype != BQ_DT_BF16) return false;
     if ((reinterpret_cast<uintptr_t>(d->x) & 15) || (d->ldx % 8) != 0) return false;
     const int fmt = d->wfmt;
     const bool int4 = fmt == BQ_W_INT4_TINYGEMM || fmt == BQ_W_INT4_PLAIN;

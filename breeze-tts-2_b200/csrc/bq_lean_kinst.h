@@ -18,12 +18,11 @@ const void* lean_select_m(int tpu, int upc) {
     return reinterpret_cast<const void*>(&gemv_lean_kernel<FMT, 1, 4, MR>);
 }
 
-// rows: 1 or 2 (int4 weights take this kernel for one row only)
+// rows: 1 or 2
 template <int FMT>
 const void* lean_select(int tpu, int upc, int rows) {
     if (rows == 1) return lean_select_m<FMT, 1>(tpu, upc);
-    if constexpr (FMT == BQ_W_INT4_TINYGEMM || FMT == BQ_W_INT4_PLAIN) return nullptr;
-    else return rows == 2 ? lean_select_m<FMT, 2>(tpu, upc) : nullptr;
+    return rows == 2 ? lean_select_m<FMT, 2>(tpu, upc) : nullptr;
 }
 
 }  // namespace bq
