@@ -93,10 +93,10 @@ def measured_peak():
     return 6650.0, "fallback"
 
 
-# DRAM bytes (read + write) of one gemv3_kernel launch on this workload (mean of
-# two launches), from an ncu capture of this workload (dram__bytes_read.sum +
-# dram__bytes_write.sum); re-captured whenever the kernel changes.
-NCU_TRAFFIC_BYTES = 6_769_920
+# DRAM bytes (read + write) of one GEMV launch on this workload (the resident-slice
+# kernel, gemv_lean_kernel), from an ncu capture of this workload
+# (dram__bytes_read.sum + dram__bytes_write.sum); re-captured whenever the kernel changes.
+NCU_TRAFFIC_BYTES = 6_749_184
 
 
 class ClockSampler:
