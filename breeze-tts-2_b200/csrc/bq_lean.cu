@@ -49,6 +49,10 @@ bool plan_lean(const bq_gemv_desc* d, LeanPlan* pl) {
     P.tpu = d->epilogue == BQ_EPI_SILU_MUL ? 2 : 1;
     const int n_out = P.tpu == 2 ? d->N / 2 : d->N;
     P.units = (n_out + 15) / 16;
+    // Fewer units than half the SMs (the depth decoder's down projection, 64 units
+    // over K = 8192) would leave most SMs idle with one long K chain each: the ring
+    // kernel splits K across CTAs there.
+    if (2 * P.units < di->sm_count) return false;
     P.grid = std::min(di->sm_count, P.units);
     P.upc = (P.units + P.grid - 1) / P.grid;
     if (P.upc > 4) return false;
