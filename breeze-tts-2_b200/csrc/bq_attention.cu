@@ -422,6 +422,10 @@ __global__ void __launch_bounds__(kAttnThreads) attention_o_kernel(const AttnOPa
     const int kv_len = int(pos) + 1;
     const float* red = &s_red[0][0][0];
     constexpr int HS = kMaxG * (D + 2);  // stride between warps
+    // the residual of the first output row this thread finishes, in flight during the attention
+    const int r_first = CLUSTER ? j + a.HKV * int(threadIdx.x) : int(threadIdx.x);
+    const float res_first =
+        r_first < R ? __bfloat162float(p.res[int64_t(b) * p.ldr + int64_t(c) * R + r_first]) : 0.f;
     {
         attn_core<DPL>(a, j, b, pos, 0, kv_len, c == 0, s_q, s_k, s_v, s_red);
         for (int t = threadIdx.x; t < GD; t += kAttnThreads) {
@@ -445,20 +449,28 @@ __global__ void __launch_bounds__(kAttnThreads) attention_o_kernel(const AttnOPa
     // partial rows: warp w takes rows w, w + 4, ...; lanes split the G D columns
     const int64_t cb = int64_t(c) * a.B + b;  // (chunk, row)
     float* part = CLUSTER ? s_part : p.partials + (cb * a.HKV + j) * R;
-    for (int r = warp; r < R; r += 4) {
-        const __nv_bfloat16* wr = s_w + r * GD;
-        float acc = 0.f;
+    // four rows at a time with independent accumulators and reductions (R is a multiple of 16)
+    for (int r0 = warp; r0 < R; r0 += 16) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
         for (int t = lane * 2; t < GD; t += 64) {
-            const uint32_t w2 = *reinterpret_cast<const uint32_t*>(wr + t);
-            acc = fmaf(__uint_as_float(w2 << 16), s_o[t], acc);
-            acc = fmaf(__uint_as_float(w2 & 0xFFFF0000u), s_o[t + 1], acc);
+            const float o0 = s_o[t], o1 = s_o[t + 1];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint32_t w2 = *reinterpret_cast<const uint32_t*>(s_w + (r0 + 4 * q) * GD + t);
+                acc[q] = fmaf(__uint_as_float(w2 << 16), o0, acc[q]);
+                acc[q] = fmaf(__uint_as_float(w2 & 0xFFFF0000u), o1, acc[q]);
+            }
         }
-        acc = warp_sum(acc);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[q] = warp_sum(acc[q]);
         if (lane == 0) {
-            if constexpr (CLUSTER)
-                part[r] = acc;
-            else
-                __stcg(part + r, acc);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                if constexpr (CLUSTER)
+                    part[r0 + 4 * q] = acc[q];
+                else
+                    __stcg(part + r0 + 4 * q, acc[q]);
+            }
         }
     }
     if constexpr (CLUSTER) {
@@ -470,7 +482,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_o_kernel(const AttnOPa
             float v = 0.f;
             for (int h = 0; h < a.HKV; ++h) v += cluster.map_shared_rank(s_part, h)[r];
             const int64_t n = int64_t(c) * R + r;
-            v += __bfloat162float(p.res[int64_t(b) * p.ldr + n]);
+            v += r == r_first ? res_first : __bfloat162float(p.res[int64_t(b) * p.ldr + n]);
             p.out[int64_t(b) * p.ldo + n] = __float2bfloat16_rn(v);
         }
         cluster.sync();  // no CTA leaves while another may still read its partials
@@ -487,7 +499,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_o_kernel(const AttnOPa
         float v = 0.f;
         for (int h = 0; h < a.HKV; ++h) v += __ldcg(base + int64_t(h) * R + r);
         const int64_t n = int64_t(c) * R + r;
-        v += __bfloat162float(p.res[int64_t(b) * p.ldr + n]);
+        v += r == r_first ? res_first : __bfloat162float(p.res[int64_t(b) * p.ldr + n]);
         p.out[int64_t(b) * p.ldo + n] = __float2bfloat16_rn(v);
     }
     if (threadIdx.x == 0) atomicExch(p.counters + cb, 0u);
