@@ -114,6 +114,7 @@ int launch_lean(const bq_gemv_desc* d, const LeanPlan& pl, cudaStream_t stream) 
     while ((1 << p.group_shift) < d->group) ++p.group_shift;
     p.flags = d->flags;
     p.eps = d->eps;
+    p.inv_k = 1.0f / float(d->K);
     p.n_out = pl.tpu == 2 ? d->N / 2 : d->N;
     p.units = pl.units;
     p.nkw = pl.nkw;

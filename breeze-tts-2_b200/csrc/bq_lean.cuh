@@ -64,6 +64,7 @@ struct LeanParams {
     int32_t M, N, K, KB, epi, out_dtype, res_dtype, group_shift;
     uint32_t flags;
     float eps;
+    float inv_k;     // 1 / K
     int32_t n_out;   // output columns: N, or N / 2 with SiLU*up
     int32_t units;   // 16-row units
     int32_t nkw;     // k-blocks of the widest warp: ceil(KB / 8)
@@ -148,13 +149,15 @@ __global__ void __launch_bounds__(kLeanThreads, 2) gemv_lean_kernel(const __grid
     }
     __syncthreads();  // the weight barrier is initialized before anyone waits on it
 
-    // ---- 2. static data: the epilogue's row scales and bias, gamma, zero blocks
+    // ---- 2. static data: the epilogue's row scales and bias, gamma, zero blocks.
+    // Epilogue task t = (unit ul, row r, activation row m), m fastest: m = t % M,
+    // r = (t / M) % 16, ul = t / (16 M) -- compile-time divisors only.
     const int n_tasks = nu * 16 * M;
     float t_rs[2][TPU], t_rb[2][TPU];
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
         const int t = threadIdx.x + kLeanThreads * i;
-        const int r = t & 15, ul = (t >> 4) % nu;
+        const int r = (t / M) & 15, ul = t / (16 * M);
 #pragma unroll
         for (int tile = 0; tile < TPU; ++tile) {
             t_rs[i][tile] = 1.f;
@@ -209,7 +212,7 @@ __global__ void __launch_bounds__(kLeanThreads, 2) gemv_lean_kernel(const __grid
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
             const int t = threadIdx.x + kLeanThreads * i;
-            const int r = t & 15, ul = (t >> 4) % nu, m = (t >> 4) / nu;
+            const int m = t % M, r = (t / M) & 15, ul = t / (16 * M);
             const int n = 16 * (u0 + ul) + r;
             if (t < n_tasks && n < p.n_out) t_res[i] = load_act(p.residual, m * p.ldr + n, p.res_dtype);
         }
@@ -517,14 +520,14 @@ __global__ void __launch_bounds__(kLeanThreads, 2) gemv_lean_kernel(const __grid
     for (int i = 0; i < 2; ++i) {
         const int t = threadIdx.x + kLeanThreads * i;
         if (t >= n_tasks) break;
-        const int r = t & 15, ul = (t >> 4) % nu, m = (t >> 4) / nu;
+        const int m = t % M, r = (t / M) & 15, ul = t / (16 * M);
         const int n = 16 * (u0 + ul) + r;
         float inv = 1.f;
         if (norm) {
             float a = 0.f;
 #pragma unroll
             for (int w = 0; w < 8; ++w) a += s_ss[w * 8 + m];
-            inv = rsqrtf(a / float(p.K) + p.eps);
+            inv = rsqrtf(a * p.inv_k + p.eps);
         }
         float v[TPU];
 #pragma unroll
