@@ -303,7 +303,8 @@ DECODE_ROWS_INT4 = (1, 2, 4, 8, 16, 32, 64)  # config 4 adds 32 and 64 concurren
 DECODE_LAYERS = 28
 
 
-def decode_step_bench(device, ranks: Ranks, replays: int = 10, warmup: int = 3):
+def decode_step_bench(device, ranks: Ranks, replays: int = 10, warmup: int = 3, formats=DECODE_FORMATS,
+                      rows_list=None, modes=("per_op", "chain", "attn")):
     """Decode-step leg (the 28-layer projection stack + head as one CUDA graph,
     breeze_b200.fused.stack.DecodeStack) for each weight format and row count.
     The stack's weights (1.0 GB int4, 1.9 GB fp8/int8) exceed L2 by far, so
@@ -312,11 +313,11 @@ def decode_step_bench(device, ranks: Ranks, replays: int = 10, warmup: int = 3):
 
     results = []
     cur = torch.cuda.current_stream(device)
-    for fmt in DECODE_FORMATS:
+    for fmt in formats:
         layers, head, ln_f = synthetic_stack(fmt, DECODE_LAYERS, device, seed=7)
-        for rows in (DECODE_ROWS_INT4 if fmt == "int4" else DECODE_ROWS):
+        for rows in rows_list or (DECODE_ROWS_INT4 if fmt == "int4" else DECODE_ROWS):
             entry = {"format": fmt, "rows": rows}
-            for mode in ("per_op", "chain", "attn"):
+            for mode in modes:
                 if mode == "chain" and rows > 16:
                     entry[mode] = {"unavailable": "the chain takes at most 16 rows"}
                     continue
@@ -743,6 +744,8 @@ def main():
                          "RMSNorm unless EPI is 2) over rotated weight copies > 4x L2 and print its JSON")
     ap.add_argument("--depth-only", action="store_true",
                     help="run only the depth-decoder frame leg (one GPU; for profiling) and print its JSON")
+    ap.add_argument("--decode-only", default=None, metavar="FMT:ROWS",
+                    help="run only one decode-step configuration launch by launch (one GPU; for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -754,6 +757,13 @@ def main():
         device = torch.device("cuda", local_rank)
         torch.cuda.set_device(device)
         print(json.dumps(shape_bench(device, args.shape, args.steps, args.warmup)), flush=True)
+        return
+    if args.decode_only:
+        device = torch.device("cuda", local_rank)
+        torch.cuda.set_device(device)
+        fmt, rows = args.decode_only.split(":")
+        print(json.dumps({"decode_step": decode_step_bench(device, Ranks(0, 1), formats=(fmt,), rows_list=(int(rows),),
+                                                           modes=("per_op",))}), flush=True)
         return
     if args.depth_only:
         device = torch.device("cuda", local_rank)
