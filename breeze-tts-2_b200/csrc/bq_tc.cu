@@ -65,13 +65,13 @@ constexpr int kTcStages = 4;       // A (TMEM) and X (shared) stages, indexed by
 constexpr int kTcTmemCols = 512;
 constexpr int kTcACol0 = 256;      // A stage a at columns 256 + 64 a (accumulator at columns 0..N-1)
 constexpr int kTcACols = 64;       // 128 bf16 k-values of one row = 64 32-bit columns
-constexpr int kTcXGroup = 2048;    // 8 activation rows x 16 k-chunks of 16 B (core matrices)
 constexpr int kTcRawChunk = 2048;  // one 16-byte chunk for each of the 128 rows
 constexpr int kTcScSlot = 2048;    // int4: up to 4 (scale, zero) words for each of the 128 rows
 constexpr int kTcMinRows = 17;
 constexpr int kTcMaxRows = 128;
 
 struct TcParams {
+    CUtensorMap xmap;  // activation rows [M][K] bf16, boxes of 64 k x n_mma rows, 128-byte swizzle
     const void* w;
     const void* scale;
     const void* bias;
@@ -146,13 +146,22 @@ __device__ __forceinline__ void tc_commit(uint32_t bar) {
                  : "memory");
 }
 
-// Shared-memory matrix descriptor of a K-major bf16 operand without swizzle:
-// core matrices of 8 rows x 16 bytes; the two 8-k halves of a k16 step are
-// 128 B apart (leading offset), consecutive 8-row groups 2048 B apart (stride
-// offset); bit 46 is the sm_100 descriptor version.
+// Shared-memory matrix descriptor of the K-major bf16 activation tile as the
+// tensor map writes it: rows of 64 k (128 B) in 128-byte swizzle atoms of 8
+// rows; a k16 step inside the atom starts 32 B further (the swizzle is applied
+// to the final address); bit 46 is the sm_100 descriptor version.
 __device__ __forceinline__ uint64_t tc_bdesc(uint32_t saddr) {
-    return uint64_t((saddr >> 4) & 0x3FFFu) | (uint64_t(128 >> 4) << 16) | (uint64_t(kTcXGroup >> 4) << 32) |
-           (1ull << 46);
+    // K-major, 128-byte swizzle: 8-row groups 1024 B apart (stride offset); the
+    // leading offset is unused for swizzled K-major layouts; layout type 2 = 128B
+    return uint64_t((saddr >> 4) & 0x3FFFu) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) | (1ull << 46) |
+           (uint64_t(2) << 61);
+}
+
+// Tiled TMA load of a 2-D box (no multicast), completion on an mbarrier.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+                 ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
+                 : "memory");
 }
 
 // ------------------------------------------------------------- small helpers
@@ -362,10 +371,6 @@ __device__ __forceinline__ void tc_dequant(const TcParams& p, int r, uint32_t ra
     }
 }
 
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void sts_zero16(uint32_t a) {
-    asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0u) : "memory");
-}
 
 // Cluster barrier of every thread of every CTA of the cluster: writes to
 // shared memory before the arrive are visible to all after the wait.
@@ -390,10 +395,6 @@ __device__ __forceinline__ int dsmem_ld_s32(uint32_t a) {
     asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
     return v;
 }
-// This thread's cp.async copies issued so far complete one arrival on `bar`.
-__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
-}
 
 // Output of activation row m for weight row n (unit-relative row r), value v.
 __device__ __forceinline__ void tc_store(const TcParams& p, int m, int n, float v) {
@@ -403,8 +404,11 @@ __device__ __forceinline__ void tc_store(const TcParams& p, int m, int n, float 
 
 template <int FMT>
 __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(const __grid_constant__ TcParams p) {
-    extern __shared__ __align__(1024) unsigned char smem[];
-    const uint32_t sbase = smem_u32(smem);
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // the swizzled activation tiles need 1024-byte aligned stages (1 KB slack is allocated)
+    const uint32_t sraw = smem_u32(smem_raw);
+    const uint32_t sbase = (sraw + 1023u) & ~1023u;
+    unsigned char* smem = smem_raw + (sbase - sraw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int C = p.C;
     const int u = int(blockIdx.x) / C, rank = int(blockIdx.x) - u * C;  // cluster dims (C, 1, 1)
@@ -423,7 +427,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(const __grid_con
         for (int a = 0; a < kTcStages; ++a) {
             mbar_init(bar_full + 8 * a, 128);
             mbar_init(bar_empty + 8 * a, 1);
-            mbar_init(bar_xfull + 8 * a, 32);
+            mbar_init(bar_xfull + 8 * a, 1);
         }
         mbar_init(bar_acc, 1);
         mbar_init(bar_done, 1);
@@ -443,16 +447,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(const __grid_con
             cp_async_commit();
         }
     }
-    // activation rows M .. n_mma of every X stage stay zero (the loader never writes them)
-    {
-        const int pad = (p.n_mma - p.M) * 16;
-        for (int idx = threadIdx.x; idx < kTcStages * pad; idx += kTcThreads) {
-            const int st = idx / pad, rem = idx - st * pad;
-            const int m = p.M + (rem >> 4), c = rem & 15;
-            sts_zero16(sbase + p.sm_x + st * (p.n_mma * 256) + (m >> 3) * kTcXGroup + c * 128 + (m & 7) * 16);
-        }
-        fence_proxy_async();
-    }
+    // activation rows M .. n_mma are outside the tensor map: the TMA fills them with zeros
     if (warp == kTcMmaWarp) tmem_alloc(smem_u32(tmem_slot), kTcTmemCols);
     pdl_launch_dependents();
     tc_fence_before();
@@ -488,28 +483,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(const __grid_con
         }
         cp_async_wait_depth(0);
     } else if (warp == kTcXWarp) {
-        // ---------------------------------------------------------- activation loader
+        // ---------------------------------------------------------- activation loader (TMA)
         pdl_wait();  // x is written by the previous kernel
-        const int rows8 = p.n_mma >> 3;
-        for (int b = 0; b < nb; ++b) {
-            const int a = b & 3;
-            if (b >= kTcStages) {
-                const bool ok = tc_wait(bar_empty + 8 * a, ((b >> 2) + 1) & 1, abort, lim);
-                if (!__all_sync(0xffffffffu, ok)) break;
+        if (lane == 0) {
+            const uint32_t half = uint32_t(p.n_mma) * 128u;  // one box: 64 k of every row
+            int issued = 0;
+            for (int b = 0; b < nb; ++b, ++issued) {
+                const int a = b & 3;
+                if (b >= kTcStages && !tc_wait(bar_empty + 8 * a, ((b >> 2) + 1) & 1, abort, lim)) break;
+                const uint32_t xs = sbase + p.sm_x + a * (p.n_mma * 256), bar = bar_xfull + 8 * a;
+                mbar_arrive_expect_tx(bar, 2u * half);
+                tma_load_2d(xs, &p.xmap, (kb0 + b) * 128, 0, bar);
+                tma_load_2d(xs + half, &p.xmap, (kb0 + b) * 128 + 64, 0, bar);
             }
-            const int kb = kb0 + b;
-            const uint32_t xs = sbase + p.sm_x + a * (p.n_mma * 256);
-            // lane -> (row m = 8 g + lane % 8, k-chunk 4 q + lane / 8): 4 x 128 contiguous bytes per store
-            for (int t = 0; t < rows8 * 4; ++t) {
-                const int g8 = t >> 2, q = t & 3;
-                const int m = 8 * g8 + (lane & 7), c = 4 * q + (lane >> 3);
-                if (m < p.M)
-                    cp_async16(xs + g8 * kTcXGroup + c * 128 + (lane & 7) * 16, p.x + m * p.ldx + kb * 128 + c * 8);
-            }
-            cp_async_arrive_noinc(bar_xfull + 8 * a);  // one arrival per lane once its copies have landed
+            // no tile may still be landing when the CTA leaves (an abort skips the MMAs)
+            for (int b = issued > kTcStages ? issued - kTcStages : 0; b < issued; ++b)
+                tc_wait(bar_xfull + 8 * (b & 3), (b >> 2) & 1, nullptr, lim);
         }
-        cp_async_commit();
-        cp_async_wait_depth(0);  // every copy of this thread (none is left in flight at exit)
+        __syncwarp();
     } else if (warp == kTcMmaWarp) {
         // ---------------------------------------------------------- MMA issuer
         if (lane == 0) {
@@ -522,8 +513,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(const __grid_con
                 tc_fence_after();
                 const uint32_t xs = sbase + p.sm_x + a * (p.n_mma * 256);
 #pragma unroll
-                for (int k = 0; k < 8; ++k)
-                    tc_mma(tmem, tmem + kTcACol0 + kTcACols * a + 8 * k, tc_bdesc(xs + 256 * k), p.idesc,
+                for (int k = 0; k < 8; ++k)  // k16 step k: box k / 4, 32 B per step inside the swizzle atom
+                    tc_mma(tmem, tmem + kTcACol0 + kTcACols * a + 8 * k,
+                           tc_bdesc(xs + uint32_t(k >> 2) * uint32_t(p.n_mma) * 128u + 32u * uint32_t(k & 3)), p.idesc,
                            (b > 0 || k > 0) ? 1u : 0u);
                 tc_commit(bar_empty + 8 * a);
             }
@@ -660,6 +652,40 @@ const void* tc_kernel_for(int fmt) {
 }  // namespace
 
 namespace {
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(f);
+    });
+    return fn;
+}
+
+// Tensor map of the activation rows: [M][K] bf16 with row stride ldx, boxes of
+// 64 k x n_mma rows (rows past M read as zeros), 128-byte swizzle -- the K-major
+// layout the MMA's B descriptor (tc_bdesc) describes.
+int tc_encode_x(const void* x, int64_t ldx, int M, int K, int n_mma, CUtensorMap* map) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return set_error(BQ_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+    const cuuint64_t dims[2] = {cuuint64_t(K), cuuint64_t(M)};
+    const cuuint64_t strides[1] = {cuuint64_t(ldx) * 2};
+    const cuuint32_t box[2] = {64, cuuint32_t(n_mma)};
+    const cuuint32_t es[2] = {1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(BQ_ERR_CUDA, "cuTensorMapEncodeTiled (activations) failed (%d)", int(r));
+    return BQ_OK;
+}
+
 // Plans depend on the shape, format, group, epilogue, norm and device only.
 std::mutex g_tc_mu;
 std::map<std::array<int, 9>, std::pair<bool, TcPlan>> g_tc_plans;
@@ -682,7 +708,7 @@ bool plan_tc_uncached(const bq_gemv_desc* d, TcPlan* pl) {
     p.sc_slot = int4 ? uint32_t(kTcScSlot) : 0u;
     p.sm_x = 0;
     const uint32_t x_bytes = uint32_t(kTcStages) * uint32_t(p.n_mma) * 256u;
-    const uint32_t fixed = x_bytes + 256u;
+    const uint32_t fixed = x_bytes + 256u + 1024u;  // + slack to align the layout to 1024 bytes
     int rd = 0;
     for (int c = 6; c >= 2; --c)
         if (fixed + 2u * uint32_t(c) * (p.raw_slot + p.sc_slot) <= uint32_t(di->smem_optin)) {
@@ -694,7 +720,7 @@ bool plan_tc_uncached(const bq_gemv_desc* d, TcPlan* pl) {
     p.sm_raw = x_bytes;
     p.sm_sc = p.sm_raw + 2u * rd * p.raw_slot;
     p.sm_bar = p.sm_sc + 2u * rd * p.sc_slot;
-    p.sm_total = p.sm_bar + 256u;
+    p.sm_total = p.sm_bar + 256u + 1024u;
     p.red_pitch = uint32_t(p.n_mma) + 4u;
     if (ensure_smem_attr(fn, p.sm_total)) return false;
     // K slices per unit: fill the SMs in one wave with clusters of at most 8
@@ -789,6 +815,10 @@ int launch_tc(const bq_gemv_desc* d, const TcPlan& pl, void* workspace, cudaStre
     }
     TcParams p;
     std::memset(&p, 0, sizeof(p));
+    {
+        const int rc = tc_encode_x(x, ldx, d->M, d->K, pl.n_mma, &p.xmap);
+        if (rc) return rc;
+    }
     p.w = d->w;
     p.scale = d->scale;
     p.bias = d->bias;
