@@ -45,8 +45,8 @@ int launch_gemv3(const bq_gemv_desc* d, const Gemv3Plan& pl, int row0, void* wor
 
 // Tensor-core GEMV (tcgen05, weights read once for 17..128 rows).
 struct TcPlan {
-    int n_mma, KB, units, C, grid, raw_depth;
-    uint32_t raw_slot, sc_slot, sm_x, sm_raw, sm_sc, sm_bar, sm_total, red_pitch;
+    int n_mma, KB, units, C, grid, wst;
+    uint32_t w_stage, w_bytes, tx_bytes, sm_x, sm_w, sm_bar, sm_total, red_pitch;
     int64_t xn_off, ws_bytes;
 };
 bool plan_tc(const bq_gemv_desc* d, TcPlan* pl);

@@ -57,7 +57,7 @@
 namespace bq {
 namespace {
 
-constexpr int kTcWarps = 14;
+constexpr int kTcWarps = 15;
 constexpr int kTcThreads = kTcWarps * 32;
 constexpr int kTcXWarp = 8;
 constexpr int kTcMmaWarp = 9;
@@ -65,13 +65,14 @@ constexpr int kTcStages = 4;       // A (TMEM) and X (shared) stages, indexed by
 constexpr int kTcTmemCols = 512;
 constexpr int kTcACol0 = 256;      // A stage a at columns 256 + 64 a (accumulator at columns 0..N-1)
 constexpr int kTcACols = 64;       // 128 bf16 k-values of one row = 64 32-bit columns
-constexpr int kTcRawChunk = 2048;  // one 16-byte chunk for each of the 128 rows
-constexpr int kTcScSlot = 2048;    // int4: up to 4 (scale, zero) words for each of the 128 rows
+constexpr int kTcProdWarp = 14;   // weight producer (TMA)
+constexpr int kTcMaxWStages = 8;   // weight ring stages at most
 constexpr int kTcMinRows = 17;
 constexpr int kTcMaxRows = 128;
 
 struct TcParams {
     CUtensorMap xmap;  // activation rows [M][K] bf16, boxes of 64 k x n_mma rows, 128-byte swizzle
+    CUtensorMap wmap;  // weights: int4 plain / 8-bit / bf16 2-D, tinygemm 3-D (see tc_encode_weights)
     const void* w;
     const void* scale;
     const void* bias;
@@ -81,11 +82,13 @@ struct TcParams {
     long long ldx, ldr, ldo;
     int M, N, K, KB, group, epi, out_dtype, res_dtype;
     unsigned flags;
-    int C, n_mma, raw_depth;
+    int C, n_mma, wst;  // cluster size, MMA N, weight ring stages
     unsigned idesc;
     long long wait_cycles;
-    unsigned sm_x, sm_raw, sm_sc, sm_bar, sm_total, red_pitch;
-    unsigned raw_slot, sc_slot;  // bytes per ring slot
+    unsigned sm_x, sm_w, sm_bar, sm_total, red_pitch;
+    unsigned w_stage;   // bytes per weight stage: 128 rows of weights, then int4 scales
+    unsigned w_bytes;   // weight bytes per stage (the scales follow)
+    unsigned tx_bytes;  // bytes a stage receives per k-block (weights + scales)
 };
 
 // Bytes of one weight row per 128-k block, by format.
@@ -168,21 +171,6 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
-__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_depth(int pending) {
-    // cp.async.wait_group takes an immediate
-    switch (pending) {
-        case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
-        case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
-        case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
-        case 3: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
-        case 4: asm volatile("cp.async.wait_group 4;" ::: "memory"); break;
-        default: asm volatile("cp.async.wait_group 5;" ::: "memory"); break;
-    }
-}
 __device__ __forceinline__ uint4 lds128(uint32_t a) {
     uint4 v;
     asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
@@ -249,48 +237,85 @@ __device__ __forceinline__ int tc_row(const TcParams& p, int u, int r) {
 }
 
 // ------------------------------------------------------------- weight stream
-// Issues the cp.async copies of row n's bytes of k-block kb into ring slot
-// `raw` (chunk c of every row at raw + c * 2048 + r * 16) and, for int4, its
-// (scale, zero) words into `sc` (group gi at sc + gi * 512 + r * 4).
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, uint32_t bar) {
+    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+                 ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
+                 : "memory");
+}
+// 1-D bulk copy global -> shared (16-byte aligned, size a multiple of 16).
+__device__ __forceinline__ void tc_bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
+// One k-block of unit u into weight stage `st` (one thread): the 128 rows (two
+// 64-row boxes for SiLU*up: gate rows, then the matching up rows), then for
+// int4 the (scale, zero) words of the block's groups, [group][128 rows].
 template <int FMT>
-__device__ __forceinline__ void tc_issue(const TcParams& p, int n, int kb, int r, uint32_t raw, uint32_t sc) {
-    const char* w = static_cast<const char*>(p.w);
-    if constexpr (FMT == BQ_W_INT4_TINYGEMM) {
-        // [N/8, K/128, 32 lanes, 4 words]: lanes 4(n%8) .. 4(n%8)+3 hold row n's 128 k of the block
-        const char* src = w + ((size_t(n >> 3) * p.KB + kb) * 32 + (n & 7) * 4) * 16;
+__device__ __forceinline__ void tc_produce(const TcParams& p, int u, int kb, uint32_t st, uint32_t bar) {
+    const bool silu = p.epi == BQ_EPI_SILU_MUL;
+    const int nbox = silu ? 2 : 1, brows = silu ? 64 : 128;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) cp_async16(raw + c * kTcRawChunk + r * 16, src + c * 16);
+    for (int h = 0; h < 2; ++h) {
+        if (h >= nbox) break;
+        const int row0 = silu ? (h == 0 ? u * 64 : (p.N >> 1) + u * 64) : u * 128;
+        constexpr int line = FMT == BQ_W_BF16 ? 128 : tc_row_bytes(FMT);  // bytes of a row in one box
+        const uint32_t dst = st + uint32_t(h * brows * line);
+        if constexpr (FMT == BQ_W_INT4_TINYGEMM) {
+            tma_load_3d(dst, &p.wmap, 0, kb, row0 >> 3, bar);  // [n8][512 B]: the 8-row tiles of k-block kb
+        } else if constexpr (FMT == BQ_W_INT4_PLAIN) {
+            tma_load_2d(dst, &p.wmap, kb * 64, row0, bar);
+        } else if constexpr (FMT == BQ_W_BF16) {
+            tma_load_2d(dst, &p.wmap, kb * 128, row0, bar);                      // k 0-63 of the block
+            tma_load_2d(dst + 128u * 128u, &p.wmap, kb * 128 + 64, row0, bar);   // k 64-127
+        } else {
+            tma_load_2d(dst, &p.wmap, kb * 128, row0, bar);
+        }
+    }
+    if constexpr (FMT == BQ_W_INT4_TINYGEMM || FMT == BQ_W_INT4_PLAIN) {
         const int g = p.group;
         const int ngr = g < 128 ? 128 / g : 1;
         const int g0 = g <= 128 ? kb * (128 / g) : kb / (g / 128);
         const char* s = static_cast<const char*>(p.scale);
-        for (int gi = 0; gi < ngr; ++gi) cp_async4(sc + gi * 512 + r * 4, s + (size_t(g0 + gi) * p.N + n) * 4);
-    } else if constexpr (FMT == BQ_W_INT4_PLAIN) {
-        const char* src = w + size_t(n) * (p.K >> 1) + kb * 64;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) cp_async16(raw + c * kTcRawChunk + r * 16, src + c * 16);
-        cp_async4(sc + r * 4, static_cast<const char*>(p.scale) + (size_t(kb) * p.N + n) * 4);
-    } else if constexpr (FMT == BQ_W_BF16) {
-        const char* src = w + (size_t(n) * p.K + size_t(kb) * 128) * 2;
-#pragma unroll
-        for (int c = 0; c < 16; ++c) cp_async16(raw + c * kTcRawChunk + r * 16, src + c * 16);
-    } else {  // fp8 / int8: one byte per weight
-        const char* src = w + size_t(n) * p.K + size_t(kb) * 128;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) cp_async16(raw + c * kTcRawChunk + r * 16, src + c * 16);
+        for (int gi = 0; gi < ngr; ++gi) {
+            const uint32_t dsc = st + p.w_bytes + uint32_t(gi * 512);
+            if (silu) {
+                tc_bulk_g2s(dsc, s + (size_t(g0 + gi) * p.N + u * 64) * 4, 256, bar);
+                tc_bulk_g2s(dsc + 256, s + (size_t(g0 + gi) * p.N + (p.N >> 1) + u * 64) * 4, 256, bar);
+            } else {
+                tc_bulk_g2s(dsc, s + (size_t(g0 + gi) * p.N + u * 128) * 4, 512, bar);
+            }
+        }
     }
 }
 
-// Dequantizes row r's block from the ring slot into bf16 pairs (low half =
+// 16-byte chunk c of weight row r in a stage, as the tensor map's swizzle placed
+// it: int4 rows are 64 B (64-byte swizzle: chunk ^ bits 1-2 of the row), 8-bit
+// rows 128 B (128-byte swizzle: chunk ^ row % 8), bf16 two 128-byte halves.
+template <int FMT>
+__device__ __forceinline__ uint32_t tc_chunk(uint32_t st, int r, int c) {
+    if constexpr (FMT == BQ_W_INT4_TINYGEMM)
+        return st + uint32_t(r * 64 + 16 * c);  // 512-byte tiles copied as they are stored (no swizzle)
+    else if constexpr (FMT == BQ_W_INT4_PLAIN)
+        return st + uint32_t(r * 64 + 16 * (c ^ ((r >> 1) & 3)));
+    else if constexpr (FMT == BQ_W_BF16)
+        return st + uint32_t((c >> 3) * 128 * 128 + r * 128 + 16 * ((c & 7) ^ (r & 7)));
+    else
+        return st + uint32_t(r * 128 + 16 * (c ^ (r & 7)));
+}
+
+// Dequantizes row r's block from weight stage `st` into bf16 pairs (low half =
 // even k) and stores them to TMEM columns col .. col+63 of the warp's lane.
 template <int FMT>
-__device__ __forceinline__ void tc_dequant(const TcParams& p, int r, uint32_t raw, uint32_t sc, uint32_t taddr) {
+__device__ __forceinline__ void tc_dequant(const TcParams& p, int r, uint32_t st, uint32_t taddr) {
+    const uint32_t sc = st + p.w_bytes;
     if constexpr (FMT == BQ_W_INT4_TINYGEMM) {
         // word j of lane c, nibble pair i (bits 4i and 16 + 4i) holds the codes of
         // k = 32 j + 8 i + 2 c and k + 1 (even k in the low nibble of the pair)
         uint4 l[4];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) l[c] = lds128(raw + c * kTcRawChunk + r * 16);
+        for (int c = 0; c < 4; ++c) l[c] = lds128(tc_chunk<FMT>(st, r, c));
         const int g = p.group;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -315,7 +340,7 @@ __device__ __forceinline__ void tc_dequant(const TcParams& p, int r, uint32_t ra
         const uint32_t s2 = prmt(sz, sz, 0x1010u), m2 = prmt(sz, sz, 0x3232u);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-            const uint4 l = lds128(raw + c * kTcRawChunk + r * 16);
+            const uint4 l = lds128(tc_chunk<FMT>(st, r, c));
             uint32_t o[16];
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
@@ -337,7 +362,7 @@ __device__ __forceinline__ void tc_dequant(const TcParams& p, int r, uint32_t ra
             uint32_t o[16];
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
-                const uint4 l = lds128(raw + (4 * j + c) * kTcRawChunk + r * 16);
+                const uint4 l = lds128(tc_chunk<FMT>(st, r, 4 * j + c));
                 o[4 * c] = l.x;
                 o[4 * c + 1] = l.y;
                 o[4 * c + 2] = l.z;
@@ -352,7 +377,7 @@ __device__ __forceinline__ void tc_dequant(const TcParams& p, int r, uint32_t ra
             uint32_t o[16];
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-                const uint4 l = lds128(raw + (2 * j + h) * kTcRawChunk + r * 16);
+                const uint4 l = lds128(tc_chunk<FMT>(st, r, 2 * j + h));
 #pragma unroll
                 for (int t = 0; t < 4; ++t) {
                     const uint32_t wt = t == 0 ? l.x : t == 1 ? l.y : t == 2 ? l.z : l.w;
@@ -370,7 +395,6 @@ __device__ __forceinline__ void tc_dequant(const TcParams& p, int r, uint32_t ra
         }
     }
 }
-
 
 // Cluster barrier of every thread of every CTA of the cluster: writes to
 // shared memory before the arrive are visible to all after the wait.
@@ -416,11 +440,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(const __grid_con
 
     // barriers: full[4] (A stage dequantized), empty[4] (stage consumed by the MMAs),
     // xfull[4] (X stage landed), acc (accumulator complete), done (every MMA finished)
+    // wfull[8] / wempty[8] (weight stage landed / read by its dequantizer group)
     const uint32_t bars = sbase + p.sm_bar;
     const uint32_t bar_full = bars, bar_empty = bars + 32, bar_xfull = bars + 64, bar_acc = bars + 96,
-                   bar_done = bars + 104;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + p.sm_bar + 136);
-    volatile int* abort = reinterpret_cast<volatile int*>(smem + p.sm_bar + 140);
+                   bar_done = bars + 104, bar_wfull = bars + 128, bar_wempty = bars + 192;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + p.sm_bar + 112);
+    volatile int* abort = reinterpret_cast<volatile int*>(smem + p.sm_bar + 116);
     const long long lim = p.wait_cycles;
 
     if (threadIdx.x == 0) {
@@ -431,22 +456,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(const __grid_con
         }
         mbar_init(bar_acc, 1);
         mbar_init(bar_done, 1);
+        for (int w = 0; w < p.wst; ++w) {
+            mbar_init(bar_wfull + 8 * w, 1);
+            mbar_init(bar_wempty + 8 * w, 4);  // one arrival per warp of the consuming group
+        }
         *abort = 0;
         fence_barrier_init();
     }
-    // dequantizers: start the weight stream first (static data, before the PDL wait)
     const int grp = warp >> 2, r = ((warp & 3) << 5) | lane;
-    const int RD = p.raw_depth;
-    const uint32_t raw_g = sbase + p.sm_raw + grp * RD * p.raw_slot;
-    const uint32_t sc_g = sbase + p.sm_sc + grp * RD * p.sc_slot;
-    const int wrow = tc_row(p, u, r);
-    if (warp < 8) {
-        for (int jj = 0; jj < RD - 1; ++jj) {
-            const int b = grp + 2 * jj;
-            if (b < nb) tc_issue<FMT>(p, wrow, kb0 + b, r, raw_g + jj * p.raw_slot, sc_g + jj * p.sc_slot);
-            cp_async_commit();
-        }
-    }
+    const int WS = p.wst;
+    const uint32_t wst0 = sbase + p.sm_w;
     // activation rows M .. n_mma are outside the tensor map: the TMA fills them with zeros
     if (warp == kTcMmaWarp) tmem_alloc(smem_u32(tmem_slot), kTcTmemCols);
     pdl_launch_dependents();
@@ -458,30 +477,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(const __grid_con
     if (warp < 8) {
         // ---------------------------------------------------------- dequantizers
         const uint32_t lane_base = tmem + (uint32_t((warp & 3) * 32) << 16);
-        int j = 0;
-        for (int b = grp; b < nb; b += 2, ++j) {
-            {  // keep RD - 1 blocks of this group in flight
-                const int bn = b + 2 * (RD - 1);
-                if (bn < nb) {
-                    const int jn = (j + RD - 1) % RD;
-                    tc_issue<FMT>(p, wrow, kb0 + bn, r, raw_g + jn * p.raw_slot, sc_g + jn * p.sc_slot);
-                }
-                cp_async_commit();
-            }
-            cp_async_wait_depth(RD - 1);  // this thread's copies of block b have landed
-            const int a = b & 3;
-            if (b >= kTcStages) {  // the decision is warp-uniform: tcgen05.st is a warp-wide instruction
-                const bool ok = tc_wait(bar_empty + 8 * a, ((b >> 2) + 1) & 1, abort, lim);
-                if (!__all_sync(0xffffffffu, ok)) break;
-            }
+        for (int b = grp; b < nb; b += 2) {
+            const int a = b & 3, ws = b % WS;
+            // the weights of block b have landed (TMA), and TMEM stage a is free again
+            bool ok = tc_wait(bar_wfull + 8 * ws, (b / WS) & 1, abort, lim);
+            if (ok && b >= kTcStages) ok = tc_wait(bar_empty + 8 * a, ((b >> 2) + 1) & 1, abort, lim);
+            if (!__all_sync(0xffffffffu, ok)) break;  // warp-uniform: tcgen05.st is a warp-wide instruction
             tc_fence_after();
-            const int slot = j % RD;
-            tc_dequant<FMT>(p, r, raw_g + slot * p.raw_slot, sc_g + slot * p.sc_slot, lane_base + kTcACol0 + kTcACols * a);
+            tc_dequant<FMT>(p, r, wst0 + uint32_t(ws) * p.w_stage, lane_base + kTcACol0 + kTcACols * a);
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(bar_full + 8 * a);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_wempty + 8 * ws);  // this warp has read its rows of the stage
         }
-        cp_async_wait_depth(0);
     } else if (warp == kTcXWarp) {
         // ---------------------------------------------------------- activation loader (TMA)
         pdl_wait();  // x is written by the previous kernel
@@ -522,6 +531,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(const __grid_con
             if (ok) tc_commit(bar_acc);
             tc_commit(bar_done);  // every MMA issued above has finished once this completes
             tc_wait(bar_done, 0, nullptr, lim);  // also after an abort: TMEM is freed only when they are done
+        }
+        __syncwarp();
+    } else if (warp == kTcProdWarp) {
+        // ---------------------------------------------------------- weight producer (TMA)
+        if (lane == 0) {
+            int issued = 0;
+            for (int b = 0; b < nb; ++b, ++issued) {
+                const int ws = b % WS;
+                if (b >= WS && !tc_wait(bar_wempty + 8 * ws, ((b / WS) + 1) & 1, abort, lim)) break;
+                const uint32_t bar = bar_wfull + 8 * ws;
+                mbar_arrive_expect_tx(bar, p.tx_bytes);
+                tc_produce<FMT>(p, u, kb0 + b, wst0 + uint32_t(ws) * p.w_stage, bar);
+            }
+            // no copy may still be landing when the CTA leaves (an abort skips consumers)
+            for (int b = issued > WS ? issued - WS : 0; b < issued; ++b)
+                tc_wait(bar_wfull + 8 * (b % WS), (b / WS) & 1, nullptr, lim);
         }
         __syncwarp();
     } else {
@@ -686,6 +711,47 @@ int tc_encode_x(const void* x, int64_t ldx, int M, int K, int n_mma, CUtensorMap
     return BQ_OK;
 }
 
+// Tensor map of the weights, boxes of one k-block of a unit's rows (two 64-row
+// boxes per k-block with SiLU*up): int4 plain rows of K/2 bytes and tinygemm's
+// [N/8][K/128][8 rows][64 B] (64-byte swizzle), fp8 / int8 rows of K bytes and
+// bf16 rows of K elements in 64-element halves (128-byte swizzle).
+int tc_encode_weights(const bq_gemv_desc* d, CUtensorMap* map) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return set_error(BQ_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+    const cuuint32_t brows = d->epilogue == BQ_EPI_SILU_MUL ? 64u : 128u;
+    const cuuint32_t es[4] = {1, 1, 1, 1};
+    CUresult r;
+    void* w = const_cast<void*>(d->w);
+    if (d->wfmt == BQ_W_INT4_TINYGEMM) {
+        // [N/8][K/128][512 B]: a box is the unit's 8-row tiles of one k-block, 512 contiguous bytes each
+        const cuuint64_t dims[3] = {64, cuuint64_t(d->K / 128), cuuint64_t(d->N / 8)};
+        const cuuint64_t strides[2] = {512, cuuint64_t(d->K / 128) * 512};
+        const cuuint32_t box[3] = {64, 1, brows / 8};
+        r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, w, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else if (d->wfmt == BQ_W_INT4_PLAIN) {
+        const cuuint64_t dims[2] = {cuuint64_t(d->K / 2), cuuint64_t(d->N)};
+        const cuuint64_t strides[1] = {cuuint64_t(d->K / 2)};
+        const cuuint32_t box[2] = {64, brows};
+        r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else if (d->wfmt == BQ_W_BF16) {
+        const cuuint64_t dims[2] = {cuuint64_t(d->K), cuuint64_t(d->N)};
+        const cuuint64_t strides[1] = {cuuint64_t(d->K) * 2};
+        const cuuint32_t box[2] = {64, brows};
+        r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else {
+        const cuuint64_t dims[2] = {cuuint64_t(d->K), cuuint64_t(d->N)};
+        const cuuint64_t strides[1] = {cuuint64_t(d->K)};
+        const cuuint32_t box[2] = {128, brows};
+        r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
+    if (r != CUDA_SUCCESS) return set_error(BQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+    return BQ_OK;
+}
+
 // Plans depend on the shape, format, group, epilogue, norm and device only.
 std::mutex g_tc_mu;
 std::map<std::array<int, 9>, std::pair<bool, TcPlan>> g_tc_plans;
@@ -704,23 +770,23 @@ bool plan_tc_uncached(const bq_gemv_desc* d, TcPlan* pl) {
     p.KB = d->K / 128;
     p.units = d->N / 128;
     const bool int4 = d->wfmt == BQ_W_INT4_TINYGEMM || d->wfmt == BQ_W_INT4_PLAIN;
-    p.raw_slot = 128u * uint32_t(tc_row_bytes(d->wfmt));
-    p.sc_slot = int4 ? uint32_t(kTcScSlot) : 0u;
+    const int ngr = int4 && d->group < 128 ? 128 / d->group : 1;
+    p.w_bytes = 128u * uint32_t(tc_row_bytes(d->wfmt));
+    p.tx_bytes = p.w_bytes + (int4 ? uint32_t(ngr * 512) : 0u);
+    p.w_stage = (p.tx_bytes + 1023u) & ~1023u;  // swizzled boxes start on 1024-byte boundaries
     p.sm_x = 0;
     const uint32_t x_bytes = uint32_t(kTcStages) * uint32_t(p.n_mma) * 256u;
-    const uint32_t fixed = x_bytes + 256u + 1024u;  // + slack to align the layout to 1024 bytes
-    int rd = 0;
-    for (int c = 6; c >= 2; --c)
-        if (fixed + 2u * uint32_t(c) * (p.raw_slot + p.sc_slot) <= uint32_t(di->smem_optin)) {
-            rd = c;
+    p.sm_w = (x_bytes + 1023u) & ~1023u;
+    int ws = 0;
+    for (int c = std::min(kTcMaxWStages, p.KB); c >= 2; --c)
+        if (p.sm_w + uint32_t(c) * p.w_stage + 256u + 1024u <= uint32_t(di->smem_optin)) {
+            ws = c;
             break;
         }
-    if (!rd) return false;
-    p.raw_depth = rd;
-    p.sm_raw = x_bytes;
-    p.sm_sc = p.sm_raw + 2u * rd * p.raw_slot;
-    p.sm_bar = p.sm_sc + 2u * rd * p.sc_slot;
-    p.sm_total = p.sm_bar + 256u + 1024u;
+    if (!ws) return false;
+    p.wst = ws;
+    p.sm_bar = p.sm_w + uint32_t(ws) * p.w_stage;
+    p.sm_total = p.sm_bar + 256u + 1024u;  // + slack to align the layout to 1024 bytes
     p.red_pitch = uint32_t(p.n_mma) + 4u;
     if (ensure_smem_attr(fn, p.sm_total)) return false;
     // K slices per unit: fill the SMs in one wave with clusters of at most 8
@@ -839,18 +905,22 @@ int launch_tc(const bq_gemv_desc* d, const TcPlan& pl, void* workspace, cudaStre
     p.flags = d->flags;
     p.C = pl.C;
     p.n_mma = pl.n_mma;
-    p.raw_depth = pl.raw_depth;
+    p.wst = pl.wst;
     // kind::f16, fp32 accumulate, bf16 A and B, both K-major, N = n_mma, M = 128
     p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(pl.n_mma >> 3) << 17) | (uint32_t(128 >> 4) << 24);
     p.wait_cycles = kWaitCycles;
     p.sm_x = pl.sm_x;
-    p.sm_raw = pl.sm_raw;
-    p.sm_sc = pl.sm_sc;
+    p.sm_w = pl.sm_w;
     p.sm_bar = pl.sm_bar;
     p.sm_total = pl.sm_total;
     p.red_pitch = pl.red_pitch;
-    p.raw_slot = pl.raw_slot;
-    p.sc_slot = pl.sc_slot;
+    p.w_stage = pl.w_stage;
+    p.w_bytes = pl.w_bytes;
+    p.tx_bytes = pl.tx_bytes;
+    {
+        const int rc = tc_encode_weights(d, &p.wmap);
+        if (rc) return rc;
+    }
     int rc = ensure_smem_attr(fn, pl.sm_total);
     if (rc) return rc;
     cudaLaunchConfig_t cfg;
