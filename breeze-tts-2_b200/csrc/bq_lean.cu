@@ -117,6 +117,8 @@ int launch_lean(const bq_gemv_desc* d, const LeanPlan& pl, cudaStream_t stream) 
     p.inv_k = 1.0f / float(d->K);
     p.n_out = pl.tpu == 2 ? d->N / 2 : d->N;
     p.units = pl.units;
+    p.uq = pl.units / pl.grid;
+    p.ur = pl.units % pl.grid;
     p.nkw = pl.nkw;
     p.pitch = pl.pitch;
     p.upc = pl.upc;

@@ -67,6 +67,7 @@ struct LeanParams {
     float inv_k;     // 1 / K
     int32_t n_out;   // output columns: N, or N / 2 with SiLU*up
     int32_t units;   // 16-row units
+    int32_t uq, ur;  // units / grid, units % grid: CTAs below ur own uq + 1 units, the rest uq
     int32_t nkw;     // k-blocks of the widest warp: ceil(KB / 8)
     int32_t pitch;   // bytes per staged activation row (per warp)
     int32_t upc;     // units per CTA at most (fixes the shared-memory strides)
@@ -98,8 +99,9 @@ __global__ void __launch_bounds__(kLeanThreads, 2) gemv_lean_kernel(const __grid
     const int tq = lane & 3, tg = lane >> 2;
     constexpr int M = MR;
     const int KB = p.KB;
-    const int u0 = int(int64_t(blockIdx.x) * p.units / gridDim.x);
-    const int nu = int(int64_t(blockIdx.x + 1) * p.units / gridDim.x) - u0;  // 1 .. UPC
+    // the CTA's units, no division on the way to the weight copy
+    const int u0 = int(blockIdx.x) * p.uq + min(int(blockIdx.x), p.ur);
+    const int nu = p.uq + (int(blockIdx.x) < p.ur ? 1 : 0);  // 1 .. UPC
     const int kw0 = (warp * KB) >> 3, nkw = (((warp + 1) * KB) >> 3) - kw0;  // this warp's k-blocks
     const uint32_t sbase = smem_u32(smem);
     const uint8_t* wg = static_cast<const uint8_t*>(p.w);
