@@ -56,7 +56,8 @@ int launch_tc(const bq_gemv_desc* d, const TcPlan& pl, void* workspace, cudaStre
 // dependent-launch wait, no workspace).
 struct LeanPlan {
     int units, grid, upc, tpu, nkw, pitch, rbk;
-    uint32_t sm_w, sm_sc, sm_x, sm_xs, sm_part, sm_misc, sm_bar, sm_total;
+    int ks;  // K slices per unit (clusters of ks CTAs), 1 = no split
+    uint32_t sm_w, sm_sc, sm_x, sm_xs, sm_part, sm_misc, sm_red, sm_bar, sm_total;
 };
 bool plan_lean(const bq_gemv_desc* d, LeanPlan* pl);
 int launch_lean(const bq_gemv_desc* d, const LeanPlan& pl, cudaStream_t stream);

@@ -73,6 +73,7 @@ struct LeanParams {
     int32_t upc;     // units per CTA at most (fixes the shared-memory strides)
     int32_t rbk;     // weight bytes per row (K/2, K or 2K)
     uint32_t sm_w, sm_sc, sm_x, sm_xs, sm_part, sm_misc, sm_bar;
+    uint32_t sm_red;  // K split: [half][16 rows][8] partial sums + [8] sum(x^2) read by cluster rank 0
     long long wait_cycles;
 };
 
@@ -91,18 +92,37 @@ __device__ __forceinline__ int lean_row(const LeanParams& p, int u, int tile) {
 
 // MR: activation rows (1 or 2), a compile-time count so the staging and its
 // row reductions are straight-line code.
-template <int FMT, int TPU, int UPC, int MR>
+// KS: K slices per unit. KS > 1 (one unit per CTA, UPC 1) launches clusters of
+// KS CTAs, CTA rank r of a cluster owning k-blocks [r KB/KS, (r+1) KB/KS) of the
+// cluster's unit: each CTA copies only its slice of the unit's rows, and cluster
+// rank 0 adds the ranks' partial sums in rank order through distributed shared
+// memory before the epilogue -- for shapes with fewer 16-row units than half the
+// SMs (the depth decoder's down projection: 64 units over K = 8192).
+template <int FMT, int TPU, int UPC, int MR, int KS = 1>
 __global__ void __launch_bounds__(kLeanThreads, 2) gemv_lean_kernel(const __grid_constant__ LeanParams p) {
     using F = Fmt3<FMT>;
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tq = lane & 3, tg = lane >> 2;
     constexpr int M = MR;
+    static_assert(KS == 1 || UPC == 1, "a K-split CTA owns one unit");
     const int KB = p.KB;
-    // the CTA's units, no division on the way to the weight copy
-    const int u0 = int(blockIdx.x) * p.uq + min(int(blockIdx.x), p.ur);
-    const int nu = p.uq + (int(blockIdx.x) < p.ur ? 1 : 0);  // 1 .. UPC
-    const int kw0 = (warp * KB) >> 3, nkw = (((warp + 1) * KB) >> 3) - kw0;  // this warp's k-blocks
+    // the CTA's units and K slice, no division on the way to the weight copy
+    int u0, nu, kc0, KBc;
+    if constexpr (KS > 1) {
+        u0 = int(blockIdx.x) / KS;
+        nu = 1;
+        KBc = KB / KS;
+        kc0 = (int(blockIdx.x) % KS) * KBc;  // cluster rank x slice (clusters are KS consecutive CTAs)
+    } else {
+        u0 = int(blockIdx.x) * p.uq + min(int(blockIdx.x), p.ur);
+        nu = p.uq + (int(blockIdx.x) < p.ur ? 1 : 0);  // 1 .. UPC
+        kc0 = 0;
+        KBc = KB;
+    }
+    const int kw0 = kc0 + ((warp * KBc) >> 3), nkw = kc0 + (((warp + 1) * KBc) >> 3) - kw0;  // this warp's k-blocks
+    const int rbs = p.rbk / KS;  // bytes of the CTA's K slice of one row
+    constexpr int RBK = FMT == BQ_W_INT4_PLAIN || FMT == BQ_W_INT4_TINYGEMM ? 64 : (FMT == BQ_W_BF16 ? 256 : 128);
     const uint32_t sbase = smem_u32(smem);
     const uint8_t* wg = static_cast<const uint8_t*>(p.w);
     const uint8_t* szg = static_cast<const uint8_t*>(p.scale);
@@ -115,21 +135,32 @@ __global__ void __launch_bounds__(kLeanThreads, 2) gemv_lean_kernel(const __grid
         mbar_init(bar_w, 1);
         fence_barrier_init();
         const int half_rows = TPU == 2 ? (p.N >> 1) : p.N;
-        uint32_t bytes[TPU];
+        int nrw[TPU];
         uint32_t total = 0;
 #pragma unroll
         for (int tile = 0; tile < TPU; ++tile) {
-            const int r_end = min(16 * (u0 + nu), half_rows);
-            bytes[tile] = uint32_t(max(r_end - 16 * u0, 0)) * uint32_t(p.rbk);
-            total += bytes[tile];
+            nrw[tile] = max(min(16 * (u0 + nu), half_rows) - 16 * u0, 0);
+            total += uint32_t(nrw[tile]) * uint32_t(rbs);
         }
         mbar_arrive_expect_tx(bar_w, total);
 #pragma unroll
         for (int tile = 0; tile < TPU; ++tile) {
-            if (bytes[tile] == 0) continue;
+            if (nrw[tile] == 0) continue;
             const int64_t row0 = lean_row(p, u0, tile);
-            // tinygemm's 8-row tiles of all k-blocks are contiguous too: [N/8][KB][512]
-            lean_bulk_g2s(sbase + p.sm_w + uint32_t(tile * rows_cap * p.rbk), wg + row0 * p.rbk, bytes[tile], bar_w);
+            const uint32_t dst = sbase + p.sm_w + uint32_t(tile * rows_cap * rbs);
+            if constexpr (KS == 1) {
+                // one copy: the rows are contiguous in every layout (tinygemm: [N/8][KB][512])
+                lean_bulk_g2s(dst, wg + row0 * p.rbk, uint32_t(nrw[tile]) * uint32_t(p.rbk), bar_w);
+            } else if constexpr (FMT == BQ_W_INT4_TINYGEMM) {
+                // the slice of each 8-row tile: KBc contiguous 512-byte k-blocks
+                for (int t8 = 0; t8 < nrw[tile] / 8; ++t8)
+                    lean_bulk_g2s(dst + uint32_t(t8 * KBc * 512), wg + ((row0 / 8 + t8) * KB + kc0) * 512,
+                                  uint32_t(KBc * 512), bar_w);
+            } else {
+                for (int r = 0; r < nrw[tile]; ++r)
+                    lean_bulk_g2s(dst + uint32_t(r * rbs), wg + (row0 + r) * p.rbk + int64_t(kc0) * RBK,
+                                  uint32_t(rbs), bar_w);
+            }
         }
     }
     if constexpr (F::kInt4) {
@@ -412,16 +443,17 @@ __global__ void __launch_bounds__(kLeanThreads, 2) gemv_lean_kernel(const __grid
 #pragma unroll
             for (int tile = 0; tile < TPU; ++tile) {
                 // rows 16 ul + lane / 4 (r0) and + 8 (r1) of this half, the k-block's bytes
-                const uint8_t* half = smem + p.sm_w + size_t(tile) * rows_cap * p.rbk;
+                const uint8_t* half = smem + p.sm_w + size_t(tile) * rows_cap * rbs;
+                const int kbl = kb - kc0;  // k-block within the CTA's slice
                 const uint8_t* src;
                 int ostep;  // bytes between the two 8-row halves of the tile
                 if constexpr (FMT == BQ_W_INT4_TINYGEMM) {
-                    src = half + (size_t(2 * ul) * KB + kb) * 512 + lane * 16;  // [n8][KB][512]
-                    ostep = KB * 512;
+                    src = half + (size_t(2 * ul) * KBc + kbl) * 512 + lane * 16;  // [n8][KBc][512]
+                    ostep = KBc * 512;
                 } else {
                     constexpr int RB = (FMT == BQ_W_INT4_PLAIN) ? 64 : (FMT == BQ_W_BF16 ? 256 : 128);
-                    src = half + size_t(16 * ul + (lane >> 2)) * p.rbk + kb * RB + (lane & 3) * 16;
-                    ostep = 8 * p.rbk;
+                    src = half + size_t(16 * ul + (lane >> 2)) * rbs + kbl * RB + (lane & 3) * 16;
+                    ostep = 8 * rbs;
                 }
                 float c2[NCH][4];
 #pragma unroll
@@ -518,35 +550,88 @@ __global__ void __launch_bounds__(kLeanThreads, 2) gemv_lean_kernel(const __grid
     __syncthreads();
 
     // ---- 6. epilogue: output element (row m, column n) per task, warps summed in order
+    if constexpr (KS > 1) {
+        // The CTA's sums over its 8 warps (in order) go to its exchange buffer;
+        // cluster rank 0 adds the ranks' buffers in rank order (deterministic),
+        // sum(x^2) included, and finishes the unit's outputs.
+        float* red = reinterpret_cast<float*>(smem + p.sm_red);  // [TPU][16][8], then [8] sum(x^2)
+        const int t = threadIdx.x;
+        const int m = t % M, r = (t / M) & 15;
+        if (t < n_tasks) {
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        const int t = threadIdx.x + kLeanThreads * i;
-        if (t >= n_tasks) break;
-        const int m = t % M, r = (t / M) & 15, ul = t / (16 * M);
-        const int n = 16 * (u0 + ul) + r;
-        float inv = 1.f;
-        if (norm) {
+            for (int tile = 0; tile < TPU; ++tile) {
+                const float* pt = part + tile * 8 * 128 + r * 8 + m;
+                float a = 0.f;
+#pragma unroll
+                for (int w = 0; w < 8; ++w) a += pt[w * 128];
+                red[(tile * 16 + r) * 8 + m] = a;
+            }
+        }
+        if (t < M) {
             float a = 0.f;
 #pragma unroll
-            for (int w = 0; w < 8; ++w) a += s_ss[w * 8 + m];
-            inv = rsqrtf(a * p.inv_k + p.eps);
+            for (int w = 0; w < 8; ++w) a += s_ss[w * 8 + t];
+            red[TPU * 128 + t] = a;
         }
-        float v[TPU];
+        cluster_sync_all();
+        if (int(blockIdx.x) % KS == 0 && t < n_tasks) {
+            const uint32_t rb = smem_u32(red);
+            float v[TPU];
 #pragma unroll
-        for (int tile = 0; tile < TPU; ++tile) {
-            const float* pt = part + (ul * TPU + tile) * 8 * 128 + r * 8 + m;
-            float a = 0.f;
+            for (int tile = 0; tile < TPU; ++tile) v[tile] = red[(tile * 16 + r) * 8 + m];
+            float ss = red[TPU * 128 + m];
 #pragma unroll
-            for (int w = 0; w < 8; ++w) a += pt[w * 128];
-            v[tile] = a * inv * t_rs[i][tile] + t_rb[i][tile];
+            for (int q = 1; q < KS; ++q) {
+                const uint32_t rq = dsmem_addr(rb, uint32_t(q));
+#pragma unroll
+                for (int tile = 0; tile < TPU; ++tile) v[tile] += dsmem_ld_f32(rq + uint32_t(((tile * 16 + r) * 8 + m) * 4));
+                ss += dsmem_ld_f32(rq + uint32_t((TPU * 128 + m) * 4));
+            }
+            const float inv = norm ? rsqrtf(ss * p.inv_k + p.eps) : 1.f;
+#pragma unroll
+            for (int tile = 0; tile < TPU; ++tile) v[tile] = v[tile] * inv * t_rs[0][tile] + t_rb[0][tile];
+            const int n = 16 * u0 + r;
+            if (n < p.n_out) {
+                float o;
+                if (p.epi == BQ_EPI_SILU_MUL)
+                    o = silu(v[0]) * v[TPU - 1];
+                else
+                    o = p.epi == BQ_EPI_ADD_RESIDUAL ? v[0] + t_res[0] : v[0];
+                store_act(p.out, m * p.ldo + n, p.out_dtype, o);
+            }
         }
-        if (n >= p.n_out) continue;
-        float o;
-        if (p.epi == BQ_EPI_SILU_MUL)
-            o = silu(v[0]) * v[TPU - 1];
-        else
-            o = p.epi == BQ_EPI_ADD_RESIDUAL ? v[0] + t_res[i] : v[0];
-        store_act(p.out, m * p.ldo + n, p.out_dtype, o);
+        cluster_sync_all();  // the peers' buffers stay until rank 0 has read them
+    } else {
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int t = threadIdx.x + kLeanThreads * i;
+            if (t >= n_tasks) break;
+            const int m = t % M, r = (t / M) & 15, ul = t / (16 * M);
+            const int n = 16 * (u0 + ul) + r;
+            float inv = 1.f;
+            if (norm) {
+                float a = 0.f;
+#pragma unroll
+                for (int w = 0; w < 8; ++w) a += s_ss[w * 8 + m];
+                inv = rsqrtf(a * p.inv_k + p.eps);
+            }
+            float v[TPU];
+#pragma unroll
+            for (int tile = 0; tile < TPU; ++tile) {
+                const float* pt = part + (ul * TPU + tile) * 8 * 128 + r * 8 + m;
+                float a = 0.f;
+#pragma unroll
+                for (int w = 0; w < 8; ++w) a += pt[w * 128];
+                v[tile] = a * inv * t_rs[i][tile] + t_rb[i][tile];
+            }
+            if (n >= p.n_out) continue;
+            float o;
+            if (p.epi == BQ_EPI_SILU_MUL)
+                o = silu(v[0]) * v[TPU - 1];
+            else
+                o = p.epi == BQ_EPI_ADD_RESIDUAL ? v[0] + t_res[i] : v[0];
+            store_act(p.out, m * p.ldo + n, p.out_dtype, o);
+        }
     }
     if (threadIdx.x == 0 && !w_ok) mbar_wait(bar_w, 0);  // no bulk copy left in flight at exit
 }

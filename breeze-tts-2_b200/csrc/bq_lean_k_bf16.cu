@@ -2,5 +2,7 @@
 #include "bq_lean_kinst.h"
 
 namespace bq {
-const void* lean_kernel_bf16(int tpu, int upc, int rows) { return lean_select<BQ_W_BF16>(tpu, upc, rows); }
+const void* lean_kernel_bf16(int tpu, int upc, int rows, int ks) {
+    return lean_select<BQ_W_BF16>(tpu, upc, rows, ks);
+}
 }  // namespace bq

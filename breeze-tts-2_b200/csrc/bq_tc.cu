@@ -396,30 +396,6 @@ __device__ __forceinline__ void tc_dequant(const TcParams& p, int r, uint32_t st
     }
 }
 
-// Cluster barrier of every thread of every CTA of the cluster: writes to
-// shared memory before the arrive are visible to all after the wait.
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// Address of the same shared-memory location in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t dsmem_addr(uint32_t a, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
-    return r;
-}
-__device__ __forceinline__ float4 dsmem_ld4(uint32_t a) {
-    float4 v;
-    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a)
-                 : "memory");
-    return v;
-}
-__device__ __forceinline__ int dsmem_ld_s32(uint32_t a) {
-    int v;
-    asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
-    return v;
-}
-
 // Output of activation row m for weight row n (unit-relative row r), value v.
 __device__ __forceinline__ void tc_store(const TcParams& p, int m, int n, float v) {
     if (p.epi == BQ_EPI_ADD_RESIDUAL) v += load_act(p.residual, m * p.ldr + n, p.res_dtype);

@@ -3,8 +3,10 @@
 bq_gemv runs one or two activation rows on the resident-slice kernel (the
 CTA's whole weight slice copied to shared memory before the dependent-launch
 wait); BQ_FLAG_RING_KERNEL keeps such a call on the ring-streaming kernel,
-which also serves three to sixteen rows and the shapes the former declines
-(fewer 16-row units than half the SMs). Both must meet the suite's bar --
+which also serves three to sixteen rows and the shapes the former declines.
+Shapes with fewer 16-row units than half the SMs run the resident-slice kernel
+with K split across a cluster of two CTAs per unit (partial sums added in
+distributed shared memory). All must meet the suite's bar --
 max |err| / max |ref| <= 1e-2 against the oracle's fp32 dequant-then-linear --
 for every weight format, epilogue and the RMSNorm prologue, on shapes that
 give CTAs one to four units (ragged last unit included), and the
@@ -69,6 +71,46 @@ def test_resident_slice_rerun_is_bit_identical(fmt):
 
     a, _ = _run(fmt, 6144, 2048, 1, 0, True, 0, seed=3)
     b, _ = _run(fmt, 6144, 2048, 1, 0, True, 0, seed=3)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    assert L.device_status() == 0
+
+
+# (N, K) with fewer 16-row units than half the SMs: K split in two across a cluster of two
+# CTAs per unit -- the depth decoder's down projection (1024 x 8192), the shortest K the
+# split takes (eight k-blocks per CTA), a ragged last unit (1000 rows)
+SPLIT_SHAPES = [(1024, 8192), (1024, 2048), (1000, 4096)]
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+@pytest.mark.parametrize("m", [1, 2])
+@pytest.mark.parametrize("epi,norm", [(0, True), (0, False), (2, False), (2, True)])
+def test_k_split_matches_oracle(fmt, m, epi, norm):
+    from breeze_b200 import _lib as L
+
+    for n, k in SPLIT_SHAPES:
+        out, ref = _run(fmt, n, k, m, epi, norm, 0)
+        err = gemv.max_rel_err(out.cpu().float(), ref)
+        assert err < TOL, (fmt, m, epi, norm, n, k, err)
+    assert L.device_status() == 0
+
+
+@pytest.mark.parametrize("fmt", ["int4_tinygemm", "int4_plain", "fp8", "bf16"])
+def test_k_split_is_the_cluster_kernel_and_deterministic(fmt):
+    """The few-unit shape runs the K-split instantiation (kernel names from the profiler),
+    and a rerun gives bit-identical results (fixed rank order of the cluster sum)."""
+    from torch.profiler import ProfilerActivity, profile
+
+    from breeze_b200 import _lib as L
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        a, _ = _run(fmt, 1024, 8192, 1, 2, False, 0, seed=5)
+        torch.cuda.synchronize()
+    names = [e.name for e in prof.events() if "gemv" in e.name]
+    if not names:
+        pytest.skip("the profiler recorded no kernels on this box")
+    assert any("gemv_lean_kernel<" in nm and nm.split(">")[0].replace(" ", "").endswith(",2") for nm in names), names
+    b, _ = _run(fmt, 1024, 8192, 1, 2, False, 0, seed=5)
     torch.cuda.synchronize()
     assert torch.equal(a, b)
     assert L.device_status() == 0
