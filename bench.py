@@ -744,8 +744,9 @@ def main():
                          "RMSNorm unless EPI is 2) over rotated weight copies > 4x L2 and print its JSON")
     ap.add_argument("--depth-only", action="store_true",
                     help="run only the depth-decoder frame leg (one GPU; for profiling) and print its JSON")
-    ap.add_argument("--decode-only", default=None, metavar="FMT:ROWS",
-                    help="run only one decode-step configuration launch by launch (one GPU; for profiling)")
+    ap.add_argument("--decode-only", default=None, metavar="FMT:ROWS[:MODE]",
+                    help="run only one decode-step configuration (one GPU; for profiling): MODE per_op (default), "
+                         "chain or attn")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -761,9 +762,9 @@ def main():
     if args.decode_only:
         device = torch.device("cuda", local_rank)
         torch.cuda.set_device(device)
-        fmt, rows = args.decode_only.split(":")
+        fmt, rows, *mode = args.decode_only.split(":")
         print(json.dumps({"decode_step": decode_step_bench(device, Ranks(0, 1), formats=(fmt,), rows_list=(int(rows),),
-                                                           modes=("per_op",))}), flush=True)
+                                                           modes=tuple(mode) or ("per_op",))}), flush=True)
         return
     if args.depth_only:
         device = torch.device("cuda", local_rank)

@@ -102,58 +102,99 @@ __device__ __forceinline__ void load_row(const __nv_bfloat16* p, float (&v)[DPL]
     }
 }
 
-// One kv head of one batch row over the cache positions [s_lo, s_hi): the
-// query heads and the new k (normed, roped, rounded to the cache dtype) and v
-// into shared memory, the new k / v into the caches when `holds_pos` (register
-// copies stand in for position pos, so nothing reads it before it is written),
-// then each warp's online-softmax state over its positions in s_red. Ends
-// with a block barrier.
+// This lane's pieces of the step's inputs that do not depend on the cache
+// position: cos / sin, the warp's query heads, and (on the k / v warp) the new
+// k and v -- loaded right after the dependent-launch wait, together with the
+// position itself, so the chain pays one round trip for all of them.
+constexpr int kQPW = (kMaxG + 3) / 4;  // query heads per warp at most
 template <int DPL>
-__device__ __forceinline__ void attn_core(const AttnParams& p, int j, int b, int64_t pos, int s_lo, int s_hi,
-                                          bool holds_pos, float (*s_q)[32 * DPL], float* s_k, float* s_v,
-                                          float (*s_red)[kMaxG][32 * DPL + 2]) {
+struct AttnIn {
+    float c[DPL], s[DPL];
+    float q[kQPW][DPL];
+    float k[DPL];
+    __nv_bfloat16 v[DPL];
+};
+
+// The warp that owns the new k / v: one without a query head when G < 4, so
+// it runs beside the q heads.
+__device__ __forceinline__ int attn_kv_warp(int G) { return G < 4 ? G : 3; }
+
+template <int DPL>
+__device__ __forceinline__ void attn_load(const AttnParams& p, int j, int b, AttnIn<DPL>& in) {
     constexpr int D = 32 * DPL;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = p.G;
-    float c[DPL], s[DPL];
-    {
-        const __nv_bfloat16* cp = p.cos + int64_t(b) * p.ldcs + lane * DPL;
-        const __nv_bfloat16* sn = p.sin + int64_t(b) * p.ldcs + lane * DPL;
+    const __nv_bfloat16* cp = p.cos + int64_t(b) * p.ldcs + lane * DPL;
+    const __nv_bfloat16* sn = p.sin + int64_t(b) * p.ldcs + lane * DPL;
 #pragma unroll
-        for (int e = 0; e < DPL; ++e) {
-            c[e] = __bfloat162float(cp[e]);
-            s[e] = __bfloat162float(sn[e]);
-        }
+    for (int e = 0; e < DPL; ++e) {
+        in.c[e] = __bfloat162float(cp[e]);
+        in.s[e] = __bfloat162float(sn[e]);
     }
     const __nv_bfloat16* row = p.qkv + int64_t(b) * p.ldqkv;
-    // query heads of this kv head, scaled by D^-0.5 (kept in fp32, as the reference's q buffer)
-    for (int g = warp; g < G; g += 4) {
-        float v[DPL];
-        const __nv_bfloat16* q = row + (j * G + g) * D + lane * DPL;
 #pragma unroll
-        for (int e = 0; e < DPL; ++e) v[e] = __bfloat162float(q[e]);
-        norm_rope<DPL>(v, p.qn, p.eps, p.has_norm, c, s, lane);
+    for (int gi = 0; gi < kQPW; ++gi) {
+        const int g = warp + 4 * gi;
+        if (g < G) {
+            const __nv_bfloat16* q = row + (j * G + g) * D + lane * DPL;
 #pragma unroll
-        for (int e = 0; e < DPL; ++e) s_q[g][lane * DPL + e] = v[e] * p.scale;
+            for (int e = 0; e < DPL; ++e) in.q[gi][e] = __bfloat162float(q[e]);
+        }
     }
-    // the new k (normed, roped, rounded to the cache dtype) and v, on a warp
-    // that has no query head when G < 4, so it runs beside the q heads
-    if (warp == (G < 4 ? G : 3)) {
-        float v[DPL];
+    if (warp == attn_kv_warp(G)) {
         const __nv_bfloat16* k = row + (p.HQ + j) * D + lane * DPL;
-#pragma unroll
-        for (int e = 0; e < DPL; ++e) v[e] = __bfloat162float(k[e]);
-        norm_rope<DPL>(v, p.kn, p.eps, p.has_norm, c, s, lane);
         const __nv_bfloat16* vv = row + (p.HQ + p.HKV + j) * D + lane * DPL;
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) {
+            in.k[e] = __bfloat162float(k[e]);
+            in.v[e] = vv[e];
+        }
+    }
+}
+
+// One kv head of one batch row over the cache positions [s_lo, s_hi): the
+// query heads and the new k (normed, roped, rounded to the cache dtype) and v
+// (from `in`) into shared memory, the new k / v into the caches when
+// `holds_pos` (register copies stand in for position pos, so nothing reads it
+// before it is written), then each warp's online-softmax state over its
+// positions in s_red. Ends with a block barrier. (Requesting the warp's first
+// batch of cache rows before the q / k work as well measured slower on the
+// depth frame: 4649 -> 5212 us.)
+template <int DPL>
+__device__ __forceinline__ void attn_core(const AttnParams& p, int j, int b, int64_t pos, int s_lo, int s_hi,
+                                          bool holds_pos, const AttnIn<DPL>& in, float (*s_q)[32 * DPL], float* s_k,
+                                          float* s_v, float (*s_red)[kMaxG][32 * DPL + 2]) {
+    constexpr int D = 32 * DPL;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = p.G;
+    // query heads of this kv head, scaled by D^-0.5 (kept in fp32, as the reference's q buffer)
+#pragma unroll
+    for (int gi = 0; gi < kQPW; ++gi) {
+        const int g = warp + 4 * gi;
+        if (g < G) {
+            float v[DPL];
+#pragma unroll
+            for (int e = 0; e < DPL; ++e) v[e] = in.q[gi][e];
+            norm_rope<DPL>(v, p.qn, p.eps, p.has_norm, in.c, in.s, lane);
+#pragma unroll
+            for (int e = 0; e < DPL; ++e) s_q[g][lane * DPL + e] = v[e] * p.scale;
+        }
+    }
+    // the new k (normed, roped, rounded to the cache dtype) and v
+    if (warp == attn_kv_warp(G)) {
+        float v[DPL];
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) v[e] = in.k[e];
+        norm_rope<DPL>(v, p.kn, p.eps, p.has_norm, in.c, in.s, lane);
         const int64_t at = ((int64_t(b) * p.HKV + j) * p.S + pos) * D + lane * DPL;
 #pragma unroll
         for (int e = 0; e < DPL; ++e) {
             const __nv_bfloat16 kb = __float2bfloat16_rn(v[e]);
             s_k[lane * DPL + e] = __bfloat162float(kb);
-            s_v[lane * DPL + e] = __bfloat162float(vv[e]);
+            s_v[lane * DPL + e] = __bfloat162float(in.v[e]);
             if (holds_pos) {
                 p.kc[at + e] = kb;
-                p.vc[at + e] = vv[e];
+                p.vc[at + e] = in.v[e];
             }
         }
     }
@@ -283,6 +324,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_step_kernel(const Attn
     }
     pdl_wait();  // qkv comes from the preceding projection
 
+    AttnIn<DPL> in;
+    attn_load<DPL>(p, j, b, in);  // in flight together with the position
     const int64_t pos = *p.pos;
     if (pos < 0 || pos >= p.S) {  // a position outside the cache: flag it, touch nothing
         if (threadIdx.x == 0 && sp == 0 && j == 0 && b == 0) atomicOr(&g_device_error, BQ_DEVERR_POSITION_BIT);
@@ -293,7 +336,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_step_kernel(const Attn
     const int s_lo = sp * per, s_hi = min(s_lo + per, kv_len);
     const bool holds_pos = pos >= s_lo && pos < s_hi;
 
-    attn_core<DPL>(p, j, b, pos, s_lo, s_hi, holds_pos, s_q, s_k, s_v, s_red);
+    attn_core<DPL>(p, j, b, pos, s_lo, s_hi, holds_pos, in, s_q, s_k, s_v, s_red);
     // the next launch starts once this step's cache reads are done (decode step with
     // attention, int4 M=1: 1017 -> 980 us; the fused attention + O kernel keeps its
     // trigger before the wait: the depth frame measured slower the other way)
@@ -416,6 +459,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_o_kernel(const AttnOPa
     pdl_launch_dependents();
     pdl_wait();  // qkv and the residual come from preceding kernels
 
+    AttnIn<DPL> in;
+    attn_load<DPL>(a, j, b, in);  // in flight together with the position
     const int64_t pos = *a.pos;
     if (pos < 0 || pos >= a.S) {  // a position outside the cache: flag it, touch nothing
         cp_async_wait_all();
@@ -430,7 +475,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_o_kernel(const AttnOPa
     const float res_first =
         r_first < R ? __bfloat162float(p.res[int64_t(b) * p.ldr + int64_t(c) * R + r_first]) : 0.f;
     {
-        attn_core<DPL>(a, j, b, pos, 0, kv_len, c == 0, s_q, s_k, s_v, s_red);
+        attn_core<DPL>(a, j, b, pos, 0, kv_len, c == 0, in, s_q, s_k, s_v, s_red);
         for (int t = threadIdx.x; t < GD; t += kAttnThreads) {
             const int g = t / D, d = t - g * D;
             float mm = -1e30f;
