@@ -438,8 +438,15 @@ __global__ void __launch_bounds__(kLeanThreads, 2) gemv_lean_kernel(const __grid
         const int rows_cap = 16 * p.upc;
 #pragma unroll
         for (int us = 0; us < UPC; ++us) {
-            if (us >= nu) break;
-            const int ul = us;
+            // One tile per unit: straight-line over UPC units (UPC is the plan's exact
+            // maximum), so the compiler can overlap one unit's loads with another's
+            // MMAs; a CTA with fewer units repeats its last one, and that result is
+            // never written. SiLU*up (two independent tiles per unit already) keeps
+            // the exit: straight-line it spills.
+            if constexpr (TPU == 2) {
+                if (us >= nu) break;
+            }
+            const int ul = us < nu ? us : nu - 1;
 #pragma unroll
             for (int tile = 0; tile < TPU; ++tile) {
                 // rows 16 ul + lane / 4 (r0) and + 8 (r1) of this half, the k-block's bytes

@@ -11,10 +11,12 @@ const void* lean_select_m(int tpu, int upc) {
     if (tpu == 2) {
         if (upc <= 1) return reinterpret_cast<const void*>(&gemv_lean_kernel<FMT, 2, 1, MR>);
         if (upc <= 2) return reinterpret_cast<const void*>(&gemv_lean_kernel<FMT, 2, 2, MR>);
+        if (upc <= 3) return reinterpret_cast<const void*>(&gemv_lean_kernel<FMT, 2, 3, MR>);
         return reinterpret_cast<const void*>(&gemv_lean_kernel<FMT, 2, 4, MR>);
     }
     if (upc <= 1) return reinterpret_cast<const void*>(&gemv_lean_kernel<FMT, 1, 1, MR>);
     if (upc <= 2) return reinterpret_cast<const void*>(&gemv_lean_kernel<FMT, 1, 2, MR>);
+    if (upc <= 3) return reinterpret_cast<const void*>(&gemv_lean_kernel<FMT, 1, 3, MR>);
     return reinterpret_cast<const void*>(&gemv_lean_kernel<FMT, 1, 4, MR>);
 }
 
