@@ -96,7 +96,7 @@ def measured_peak():
 # DRAM bytes (read + write) of one GEMV launch on this workload (the resident-slice
 # kernel, gemv_lean_kernel), from an ncu capture of this workload
 # (dram__bytes_read.sum + dram__bytes_write.sum); re-captured whenever the kernel changes.
-NCU_TRAFFIC_BYTES = 6_749_184
+NCU_TRAFFIC_BYTES = 6_742_528
 
 
 class ClockSampler:
