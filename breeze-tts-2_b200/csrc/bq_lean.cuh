@@ -1,5 +1,6 @@
-// Resident-slice GEMV for 1..8 activation rows (the decode step and BASELINE
-// config 1): out = epilogue(norm(x) @ W^T), one launch, no cross-CTA traffic.
+// Resident-slice GEMV for one or two activation rows (the decode step and
+// BASELINE config 1): out = epilogue(norm(x) @ W^T), one launch, no global
+// scratch.
 //
 // Why a second small-M kernel: a decode GEMV is a chain of dependent launches,
 // and its time per call is the length of the serial path after the
@@ -9,8 +10,10 @@
 //
 //  * One CTA per SM (148), 8 warps, at most ~110 KB of shared memory where the
 //    shape allows, so the next launch's CTA parks beside the running one. A CTA
-//    owns whole 16-row units (SiLU*up: 16 gate + 16 up rows): no split-K, no
-//    partial sums in global memory, no counters.
+//    owns whole 16-row units (SiLU*up: 16 gate + 16 up rows): no partial sums
+//    in global memory, no counters. Shapes with fewer units than half the SMs
+//    split K in two across a cluster of two CTAs per unit instead, the partial
+//    sums meeting in distributed shared memory (KS below).
 //  * Before the wait: the CTA's entire weight slice goes to shared memory as
 //    one bulk copy (TMA engine) per half -- a CTA's rows are contiguous in
 //    every layout -- completing on an mbarrier; the int4 scale/zero rows of
@@ -26,7 +29,8 @@
 //    loop: a warp only reads its own K range.
 //  * Main loop, k-block-major: the activation fragments of a k-block are loaded
 //    once and used for every unit of the CTA (independent accumulators, so the
-//    MMA latency of one unit hides behind the others).
+//    MMA latency of one unit hides behind the others; one-tile shapes run the
+//    unit loop straight-line over the plan's exact unit count).
 //  * int4: codes become bf16 128 + q with one LOP3 per pair (exact); the group's
 //    scale and zero are applied in fp32 per group: s (C - (128 + o) X) + z X
 //    with X the staged activations' group sum (o = 8 tinygemm, 0 plain).

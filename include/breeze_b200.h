@@ -82,8 +82,8 @@ extern "C" {
                                        Int8Linear does for bf16 activations              */
 #define BQ_FLAG_NO_TC 4u            /* keep 17..128-row calls on the mma.sync kernel (row
                                        blocks of 16) instead of the tcgen05 kernel        */
-#define BQ_FLAG_RING_KERNEL 8u      /* keep 1..8-row calls on the ring-streaming kernel
-                                       instead of the resident-slice kernel (for
+#define BQ_FLAG_RING_KERNEL 8u      /* keep one- and two-row calls on the ring-streaming
+                                       kernel instead of the resident-slice kernel (for
                                        comparisons; results agree within rounding)       */
 
 typedef struct bq_gemv_desc {
