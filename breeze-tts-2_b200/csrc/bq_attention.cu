@@ -533,7 +533,9 @@ __global__ void __launch_bounds__(kAttnThreads) attention_o_kernel(const AttnOPa
             v += r == r_first ? res_first : __bfloat162float(p.res[int64_t(b) * p.ldr + n]);
             p.out[int64_t(b) * p.ldo + n] = __float2bfloat16_rn(v);
         }
-        cluster.sync();  // no CTA leaves while another may still read its partials
+        // no CTA leaves while another may still read its partials (every read above
+        // was consumed by its store, so the barrier needs no memory ordering)
+        cluster_sync_relaxed();
         return;
     }
     __threadfence();

@@ -177,6 +177,13 @@ __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// Cluster barrier that orders no memory: every thread of every CTA of the
+// cluster has arrived. For keeping a CTA's shared memory alive until its peers
+// have read it, when those reads were consumed before the arrive.
+__device__ __forceinline__ void cluster_sync_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+}
 // Address of the same shared-memory location in CTA `rank` of the cluster.
 __device__ __forceinline__ uint32_t dsmem_addr(uint32_t a, uint32_t rank) {
     uint32_t r;

@@ -611,7 +611,9 @@ __global__ void __launch_bounds__(kLeanThreads, 2) gemv_lean_kernel(const __grid
                 store_act(p.out, m * p.ldo + n, p.out_dtype, o);
             }
         }
-        cluster_sync_all();  // the peers' buffers stay until rank 0 has read them
+        // the peers' buffers stay until rank 0 has read them (its reads were consumed
+        // by the stores above, so this barrier orders no memory)
+        cluster_sync_relaxed();
     } else {
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
