@@ -607,7 +607,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(const __grid_con
             }
         }
     }
-    cluster_sync_all();  // no CTA leaves while another may still read its shared memory
+    // no CTA leaves while another may still read its shared memory (every read above
+    // was consumed by a store or by `bad`, so this barrier orders no memory)
+    cluster_sync_relaxed();
     if (warp == kTcMmaWarp) tmem_dealloc(tmem, kTcTmemCols);
 }
 
