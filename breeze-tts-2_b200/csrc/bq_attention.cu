@@ -295,12 +295,19 @@ __device__ __forceinline__ void attn_core(const AttnParams& p, int j, int b, int
     __syncthreads();
 }
 
-template <int DPL>
+// CLUSTER (1 < splits <= 8): the splits of one (row, kv head) form a
+// thread-block cluster; each keeps its (acc, m, l) per head in shared memory and
+// every CTA combines a slice of the output dimensions over all splits through
+// distributed shared memory, in split order (the same arithmetic and order as
+// the global combine, so the results agree bit for bit): no global partials,
+// fences or arrival counters.
+template <int DPL, bool CLUSTER>
 __global__ void __launch_bounds__(kAttnThreads) attention_step_kernel(const AttnParams p) {
     constexpr int D = 32 * DPL;
     __shared__ float s_q[kMaxG][D];
     __shared__ float s_k[D], s_v[D];
     __shared__ float s_red[4][kMaxG][D + 2];
+    __shared__ float s_split[CLUSTER ? kMaxG : 1][D + 2];  // cluster mode: this split's (acc, m, l) per head
     __shared__ unsigned int s_last;
     const int sp = blockIdx.x, j = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -358,6 +365,12 @@ __global__ void __launch_bounds__(kAttnThreads) attention_step_kernel(const Attn
         }
         if (p.splits == 1) {
             p.out[int64_t(b) * p.ldo + (j * G + g) * D + d] = __float2bfloat16_rn(aa / ll);
+        } else if constexpr (CLUSTER) {
+            s_split[g][d] = aa;
+            if (d == 0) {
+                s_split[g][D] = mm;
+                s_split[g][D + 1] = ll;
+            }
         } else {
             float* part = p.partials + (((int64_t(b) * p.HKV + j) * p.splits + sp) * G + g) * (D + 2);
             __stcg(part + d, aa);
@@ -368,6 +381,42 @@ __global__ void __launch_bounds__(kAttnThreads) attention_step_kernel(const Attn
         }
     }
     if (p.splits == 1) return;
+    if constexpr (CLUSTER) {
+        cluster_sync_all();  // every split's (acc, m, l) is in its shared memory
+        // split sp (= cluster rank) finishes output elements [sp GD / splits, (sp + 1) GD / splits)
+        const int GD = G * D, lo = sp * GD / p.splits, hi = (sp + 1) * GD / p.splits;
+        for (int t = lo + threadIdx.x; t < hi; t += kAttnThreads) {
+            const int g = t / D, d = t - g * D;
+            const uint32_t a0 = smem_u32(&s_split[g][0]);
+            float mq[8], lq[8], aq[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                if (q < p.splits) {
+                    const uint32_t aq_ = dsmem_addr(a0, uint32_t(q));
+                    mq[q] = dsmem_ld_f32(aq_ + uint32_t(D * 4));
+                    lq[q] = dsmem_ld_f32(aq_ + uint32_t((D + 1) * 4));
+                    aq[q] = dsmem_ld_f32(aq_ + uint32_t(d * 4));
+                }
+            }
+            float mm = -1e30f;
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+                if (q < p.splits) mm = fmaxf(mm, mq[q]);
+            float ll = 0.f, aa = 0.f;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                if (q < p.splits) {
+                    const float f = __expf(mq[q] - mm);
+                    ll += lq[q] * f;
+                    aa += aq[q] * f;
+                }
+            }
+            p.out[int64_t(b) * p.ldo + (j * G + g) * D + d] = __float2bfloat16_rn(aa / ll);
+        }
+        // the peers' buffers stay until read (the reads were consumed by the stores above)
+        cluster_sync_relaxed();
+        return;
+    }
     // ---- the last split to finish merges all splits (fixed order)
     __threadfence();
     __syncthreads();
@@ -677,20 +726,33 @@ int32_t bq_attention_step(const bq_attn_desc* d, void* workspace, size_t workspa
         p.counters = static_cast<unsigned int*>(workspace);
         p.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + counters);
     }
-    const void* fn = d->D == 128 ? reinterpret_cast<const void*>(&attention_step_kernel<4>)
-                                 : reinterpret_cast<const void*>(&attention_step_kernel<2>);
+    // the splits of a (row, kv head) as one cluster when they fit the portable size
+    const bool cluster = p.splits > 1 && p.splits <= 8;
+    const void* fn = d->D == 128 ? (cluster ? reinterpret_cast<const void*>(&attention_step_kernel<4, true>)
+                                            : reinterpret_cast<const void*>(&attention_step_kernel<4, false>))
+                                 : (cluster ? reinterpret_cast<const void*>(&attention_step_kernel<2, true>)
+                                            : reinterpret_cast<const void*>(&attention_step_kernel<2, false>));
     cudaLaunchConfig_t cfg;
     std::memset(&cfg, 0, sizeof(cfg));
     cfg.gridDim = dim3(p.splits, d->HKV, d->B);
     cfg.blockDim = dim3(kAttnThreads);
     cfg.stream = static_cast<cudaStream_t>(stream);
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
+    int na = 0;
     if (d->flags & BQ_FLAG_PDL) {
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
     }
+    if (cluster) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = unsigned(p.splits);
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    cfg.attrs = na ? attr : nullptr;
+    cfg.numAttrs = na;
     void* args[] = {&p};
     cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
     if (e != cudaSuccess) return set_error(BQ_ERR_CUDA, "attention launch failed: %s", cudaGetErrorString(e));
